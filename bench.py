@@ -1,0 +1,419 @@
+"""Benchmark of the reduce / broadcast hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--suite]
+
+Metric: reduce/broadcast GB/s (algorithmic HBM bytes per second, whole job)
+and its fraction of the B200 HBM roofline, against the reference's CPU path.
+
+Workload (one "step"): BASELINE config 2, the broadcasted Add and Mul of float32
+a[256,1,4096] ~ U(-1,1) with b[1,512,4096] ~ U(-1,1) into [256,512,4096] (2 GiB each),
+evaluated through the C ABI (mtxc_broadcast_binary) with the metadata the reference's
+operator+ / operator* build.  Algorithmic bytes per op: out 2^31 + a 2^22 + b 2^23 =
+2,160,066,560.  Inputs are synthetic (seeded), as BASELINE names no dataset.
+
+Multi-GPU (torchrun, one rank per GPU): weak scaling.  The global a is [256*N, 1, 4096],
+sharded along its leading axis; each rank evaluates its shard against a replicated b.  The
+op needs no collective.  Time is measured with CUDA events on the launching stream and the
+maximum over ranks is reported.
+
+`--impl reference` times the reference's own CPU loop for the same ops (the broadcast
+lambdas of Matrix.mm:7475-7567, compiled from the reference tree into
+oracle/_ref/libmtx_ref.so), one slice of output rows per host thread, on a bounded sample.
+
+`--suite` additionally prints one line per other BASELINE config (C1, C3, C4, C5a, C5b);
+those lines are diagnostics, not the headline.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "reduce/broadcast GB/s and % of HBM peak at 1/2/4/8 B200 vs host-CPU ref"
+UNIT = "GB/s"
+A_SHAPE, B_SHAPE, OUT_SHAPE = [256, 1, 4096], [1, 512, 4096], [256, 512, 4096]
+OP_BYTES = (256 * 512 * 4096 + 256 * 4096 + 512 * 4096) * 4  # 2,160,066,560
+OPS = ("add", "mul")
+WORKLOAD = "C2: broadcast Add+Mul f32 a[256,1,4096] (op) b[1,512,4096] -> [256,512,4096]"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    p = REPO / "profiles" / "broadcast_rows_c2.json"
+    try:
+        return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------------------------------
+# clocks
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuids):
+        self.uuids = {u.lower() for u in uuids}
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sm, smax, reasons, n = [], [], set(), 0
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            uuid = parts[0].lower()
+            if self.uuids and not any(uuid.endswith(u) or u.endswith(uuid) or u in uuid for u in self.uuids):
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            n += 1
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": n}
+
+
+# ------------------------------------------------------------------------------------------
+# inputs
+# ------------------------------------------------------------------------------------------
+def c2_inputs_numpy(rank: int = 0):
+    """Seeded synthetic inputs: a shard `rank` of the global a, and the replicated b."""
+    a = np.random.default_rng([1, rank]).uniform(-1, 1, 256 * 4096).astype(np.float32).reshape(A_SHAPE)
+    b = np.random.default_rng([1, 1 << 20]).uniform(-1, 1, 512 * 4096).astype(np.float32).reshape(B_SHAPE)
+    return a, b
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline: the reference's own loop (or the oracle restatement), threads over row slices
+# ------------------------------------------------------------------------------------------
+def cpu_evaluator():
+    from oracle import oracle
+
+    ref = oracle.reference()
+    if ref is not None:
+        return ref, "reference"
+    p = oracle.port()
+    p.threads = 1
+    return p, "port"
+
+
+def cpu_c2_step(ev, meta_rows, a, b, out, rows: int, threads: int):
+    """Evaluates `rows` leading rows of both ops, one contiguous slice of rows per thread."""
+    from oracle.oracle import BINARY_OPS, DTYPES, _arr
+
+    per = [rows * t // threads for t in range(threads + 1)]
+    f = ev._f["broadcast"]
+    extra = [1] if ev.threaded else []
+
+    def work(lo, hi, op):
+        if hi <= lo:
+            return
+        m = meta_rows(hi - lo)
+        total = (hi - lo) * 512 * 4096
+        rc = f(BINARY_OPS[op], DTYPES[np.dtype(np.float32)], out.ctypes.data + lo * 512 * 4096 * 4,
+               a.ctypes.data + lo * 4096 * 4, b.ctypes.data, m["cdims"], _arr(m["sr"]), _arr(m["sa"]), _arr(m["sb"]),
+               total, *extra)
+        assert rc == 0
+
+    for op in OPS:
+        ths = [threading.Thread(target=work, args=(per[t], per[t + 1], op)) for t in range(threads)]
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+
+
+def cpu_c2_sampler(threads: int, target_s: float):
+    """Returns (run_sample(), sample_rows, bytes_per_sample, kind)."""
+    ev, kind = cpu_evaluator()
+    a, b = c2_inputs_numpy(0)
+    cache = {}
+
+    def meta_rows(r):
+        if r not in cache:
+            cache[r] = ev.binary_meta([r, 1, 4096], [4096, 4096, 1], B_SHAPE, [2097152, 4096, 1])
+        return cache[r]
+
+    threads = max(1, min(threads, 256))
+    rows = threads
+    out = np.empty((256, 512, 4096), dtype=np.float32)
+    t0 = time.perf_counter()
+    cpu_c2_step(ev, meta_rows, a, b, out, rows, threads)
+    dt = time.perf_counter() - t0
+    # scale the sample to about target_s of wall time, in whole rows per thread
+    rows = int(min(256, max(rows, rows * target_s / max(dt, 1e-6))))
+    rows = max(threads, rows // threads * threads)
+    bytes_per = 2 * (rows * 512 * 4096 + rows * 4096 + 512 * 4096) * 4
+
+    def run():
+        cpu_c2_step(ev, meta_rows, a, b, out, rows, threads)
+
+    return run, rows, bytes_per, kind
+
+
+def cpu_baseline_line(threads: int, target_s: float = 10.0):
+    run, rows, bytes_per, kind = cpu_c2_sampler(threads, target_s)
+    t0 = time.perf_counter()
+    run()
+    dt = time.perf_counter() - t0
+    return {"value": round(bytes_per / dt / 1e9, 4), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"C2 Add+Mul on the first {rows} of 256 rows of a ({rows}x512x4096 outputs per op), "
+                      f"{'the reference CPU loop (Matrix.mm:7475-7567) compiled from its tree' if kind == 'reference' else 'oracle restatement'}, "
+                      f"{threads} thread(s) over row slices, {dt:.2f} s"}
+
+
+# ------------------------------------------------------------------------------------------
+# reference arm
+# ------------------------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    run, rows, bytes_per, kind = cpu_c2_sampler(threads, target_s=2.0)
+    for _ in range(args.warmup):
+        run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = bytes_per * args.steps / total / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded U(-1,1))",
+        "config": {"workload": WORKLOAD, "ops": list(OPS), "sample_rows": rows, "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{rows} of 256 rows of a per step ({rows}x512x4096 outputs per op), one row slice per thread"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from matrix_b200 import _abi, backend
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    backend.init(local)
+    stream = torch.cuda.current_stream(dev)
+    L = _abi.lib()
+
+    a_np, b_np = c2_inputs_numpy(rank)
+    a = torch.from_numpy(a_np).to(dev)
+    b = torch.from_numpy(b_np).to(dev)
+    outs = {op: torch.empty(OUT_SHAPE, dtype=torch.float32, device=dev) for op in OPS}
+    meta = backend.binary_meta(A_SHAPE, list(a.stride()), B_SHAPE, list(b.stride()))
+
+    def step(ev_pairs=None):
+        for op in OPS:
+            if ev_pairs is not None:
+                ev_pairs[op][0].record(stream)
+            backend.binary_launch(op, a.data_ptr(), b.data_ptr(), 0, outs[op].data_ptr(), meta)
+            if ev_pairs is not None:
+                ev_pairs[op][1].record(stream)
+
+    # correctness spot check (not timed): single IEEE op per element, so numpy matches exactly
+    step()
+    torch.cuda.synchronize()
+    for op, fn in (("add", np.add), ("mul", np.multiply)):
+        got = outs[op][::97].cpu().numpy()
+        want = fn(a_np[::97], b_np)
+        if got.tobytes() != want.tobytes():
+            raise SystemExit(f"bench: {op} output differs from the reference semantics")
+
+    sampler = None
+    if rank == 0:
+        uuids = []
+        for i in range(torch.cuda.device_count()):
+            try:
+                uuids.append(str(torch.cuda.get_device_properties(i).uuid))
+            except Exception:
+                pass
+        sampler = ClockSampler(uuids[:world] if world > 1 else uuids[local:local + 1])
+        sampler.start()
+        time.sleep(0.3)
+
+    for _ in range(args.warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    per_launch = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pairs = [{op: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for op in OPS}
+             for _ in range(args.steps)]
+    start.record(stream)
+    for k in range(args.steps):
+        step(pairs[k])
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    for pr in pairs:
+        for op in OPS:
+            per_launch.append(pr[op][0].elapsed_time(pr[op][1]))
+    clocks = sampler.stop() if sampler else None
+
+    # e2e through the C ABI with host buffers: upload a and b from pinned memory, run both
+    # ops, read both results back into pinned memory, every step
+    e2e_steps = max(3, min(args.steps, 5))
+    h_a = torch.from_numpy(a_np).pin_memory()
+    h_b = torch.from_numpy(b_np).pin_memory()
+    h_out = torch.empty(OUT_SHAPE, dtype=torch.float32).pin_memory()
+    nbytes_out = outs["add"].numel() * 4
+
+    def e2e_step():
+        _abi.check(L.mtxc_upload(a.data_ptr(), h_a.data_ptr(), a.numel() * 4))
+        _abi.check(L.mtxc_upload(b.data_ptr(), h_b.data_ptr(), b.numel() * 4))
+        for op in OPS:
+            backend.binary_launch(op, a.data_ptr(), b.data_ptr(), 0, outs[op].data_ptr(), meta)
+            _abi.check(L.mtxc_download(h_out.data_ptr(), outs[op].data_ptr(), nbytes_out))
+        _abi.check(L.mtxc_sync())
+
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        avg_launch_s = statistics.mean(per_launch) / 1e3
+        achieved = OP_BYTES / avg_launch_s / 1e9
+        traffic = profile_traffic()
+        total_bytes = OP_BYTES * len(OPS) * args.steps * world
+        value = total_bytes / (elapsed_ms / 1e3) / 1e9
+        e2e_value = OP_BYTES * len(OPS) * e2e_steps * world / (e2e_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U(-1,1))",
+            "config": {"workload": WORKLOAD, "ops": list(OPS), "bytes_per_op": OP_BYTES,
+                       "l2": "outputs (2 GiB per op) exceed L2; the broadcast operands a, b (12 MiB) stay L2-resident by design",
+                       "parallelism": f"weak: a sharded on its leading axis over {world} GPU(s), b replicated, no collective"},
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "broadcast_rows_kernel", "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6.65 TB/s"},
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT,
+                    "h2d_bytes_per_step": (a.numel() + b.numel()) * 4, "d2h_bytes_per_step": nbytes_out * len(OPS),
+                    "steps": e2e_steps, "path": "mtxc_upload + mtxc_broadcast_binary + mtxc_download (pinned host)"},
+            "gpu_launches": len(OPS) * args.steps,
+        }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline_line(os.cpu_count() or 1, target_s=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+        if args.suite:
+            from matrix_b200 import suite
+
+            for extra in suite.run_all(dev, stream):
+                print(json.dumps(extra), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--suite", action="store_true", help="also time the other BASELINE configs")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,232 @@
+/*
+ * mtxc.h -- C ABI of the B200 (sm_100a) backend for the reduce / broadcast hot path of
+ * AlanAditya/matrix.
+ *
+ * The reference evaluates its axis reductions (Sum, Max, Min, ArgMax, ArgMin) and its
+ * broadcasted binary ops (Add, Sub, Mul, Divide, Max, Min) either with CPU loops or by
+ * encoding Metal compute kernels through one global GPUManager.  This library replaces the
+ * Metal branch: every entry point below is what the reference's Phase-3 backend methods
+ * would call in place of their `ExecutionDevice::METAL` branch.  Shapes and strides are the
+ * reference's collapsed metadata (uint32 `size_m`, at most MTXC_MAX_DIMS axes), element
+ * offsets are in elements, and a view offset is folded into the pointer, as the reference's
+ * setBufferOrBytes does with its buffer offset.
+ *
+ * Conventions
+ *   - Every function returns an int status (MTXC_OK == 0) unless stated otherwise; on
+ *     failure mtxc_last_error() returns a message for the calling thread.
+ *   - Kernels are enqueued on the calling thread's stream (mtxc_set_stream, else a stream
+ *     the runtime creates in mtxc_init) and run asynchronously; mtxc_sync() waits.  Device
+ *     faults surface at the next synchronising call.  This mirrors the reference's
+ *     thread-local command buffer / encoder and its commit + waitUntilCompleted.
+ *   - Inputs and outputs are caller-owned device buffers.  The hot-path calls never
+ *     allocate or free: reductions that split an axis across CTAs use the calling thread's
+ *     workspace, allocated in mtxc_init or supplied with mtxc_set_workspace.
+ */
+#ifndef MTXC_H
+#define MTXC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MTXC_ABI_VERSION 1
+#define MTXC_MAX_DIMS 8 /* MAX_TENSOR_DIMS, Mods/Utils.h:127 */
+
+/* Status codes.  The reference throws std::runtime_error for a missing kernel / dtype
+ * (Mods/GPUManager.h:62-71) and std::invalid_argument for shape errors (Matrix.mm:220);
+ * a C++ caller rethrows these codes as the same exception types. */
+enum {
+    MTXC_OK = 0,
+    MTXC_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad op code, cdims > MTXC_MAX_DIMS, ... */
+    MTXC_ERR_UNSUPPORTED_DTYPE = 2,
+    MTXC_ERR_SHAPE = 3,           /* incompatible broadcast shapes */
+    MTXC_ERR_CUDA = 4,            /* a CUDA runtime call or kernel launch failed */
+    MTXC_ERR_TIMEOUT = 5,         /* a bounded device-side wait gave up */
+    MTXC_ERR_NOT_INITIALIZED = 6, /* mtxc_init was not called on this thread */
+    MTXC_ERR_WORKSPACE = 7        /* the thread's workspace cannot hold the split partials */
+};
+
+/* dtype codes: identical to the reference's `enum class dtype` (matrix.h:35-51). */
+enum {
+    MTXC_FLOAT = 0,
+    MTXC_FLOAT16 = 1,
+    MTXC_UINT8 = 2,
+    MTXC_INT32 = 3,
+    MTXC_INT16 = 4,
+    MTXC_UINT32 = 5,
+    MTXC_UINT16 = 6,
+    MTXC_BOOL = 7,
+    MTXC_INT8 = 8,
+    MTXC_COMPLEX64 = 9,
+    MTXC_BFLOAT16 = 10,
+    MTXC_INT64 = 11,
+    MTXC_UINT64 = 12
+};
+
+/* Reduction ops: SumPrimitive, MaxReductionPrimitive, MinReductionPrimitive, ArgMaxPrimitive,
+ * ArgMinPrimitive (primitives.cpp:2825-2971, 1967-2252, 7584-7799). */
+enum { MTXC_REDUCE_SUM = 0, MTXC_REDUCE_MAX = 1, MTXC_REDUCE_MIN = 2, MTXC_REDUCE_ARGMAX = 3, MTXC_REDUCE_ARGMIN = 4 };
+
+/* Broadcast binary ops: Addition/Subtraction/Multiplication/DivisionPrimitive and
+ * Max/MinPrimitive (primitives.cpp:397-1046, 2515-2823). */
+enum { MTXC_BINARY_ADD = 0, MTXC_BINARY_SUB = 1, MTXC_BINARY_MUL = 2, MTXC_BINARY_DIV = 3, MTXC_BINARY_MAX = 4, MTXC_BINARY_MIN = 5 };
+
+/* Unary ops: ExpPrimitive (primitives.cpp:5332-5463). */
+enum { MTXC_UNARY_EXP = 0 };
+
+/* ------------------------------------------------------------------------------------------
+ * Runtime.  Replaces GPUManager's device / queue / per-thread command buffer layer
+ * (Mods/GPUManager.h:47-600) and the no-copy buffer wrap buildMetalBuffer (matrix.h:677-680).
+ * ---------------------------------------------------------------------------------------- */
+
+/* Returns MTXC_ABI_VERSION. */
+int mtxc_abi_version(void);
+
+/* Binds the calling thread to CUDA device `device`, creates its stream and allocates its
+ * workspace (MTXC_WORKSPACE_MB in the environment, default 64 MiB).  Replaces the
+ * GPUManager constructor (Mods/GPUManager.h:53-54) and its lazy init* calls. */
+int mtxc_init(int device);
+
+/* Releases the calling thread's stream (if the runtime created it) and workspace (if the
+ * runtime allocated it). */
+int mtxc_shutdown(void);
+
+/* Message describing the calling thread's last failure ("" when none).  The pointer stays
+ * valid until the thread's next mtxc_* call. */
+const char* mtxc_last_error(void);
+
+int mtxc_device_count(int* count);
+
+/* Makes `stream` (a cudaStream_t) the calling thread's stream; NULL restores the stream the
+ * runtime created.  The caller keeps ownership. */
+int mtxc_set_stream(void* stream);
+void* mtxc_get_stream(void);
+
+/* Waits for all work on the calling thread's stream (the reference's commitCommandBuffer,
+ * which commits and waits: Mods/GPUManager.h:558-562).  Reports asynchronous faults. */
+int mtxc_sync(void);
+
+/* Uses caller-owned device memory as the calling thread's workspace (replacing and freeing
+ * one the runtime allocated).  bytes must be a multiple of 256 and ptr 256-byte aligned. */
+int mtxc_set_workspace(void* ptr, size_t bytes);
+/* Current workspace size in bytes of the calling thread. */
+int mtxc_workspace_size(size_t* bytes);
+/* Bytes of workspace mtxc_reduce would use for these arguments (0 when it needs none). */
+int mtxc_reduce_workspace_bytes(int op, int dtype, uint32_t reduce_stride, uint32_t reduce_len, uint32_t cdims,
+                                const uint32_t* shape, const uint32_t* dst_strides, const uint32_t* src_strides,
+                                size_t* bytes);
+
+/* Device memory (on the calling thread's device) and page-locked host memory. */
+int mtxc_alloc(size_t bytes, void** dptr);
+int mtxc_free(void* dptr);
+int mtxc_host_alloc(size_t bytes, void** hptr);
+int mtxc_host_free(void* hptr);
+/* Asynchronous copies on the calling thread's stream. */
+int mtxc_upload(void* dst_device, const void* src_host, size_t bytes);
+int mtxc_download(void* dst_host, const void* src_device, size_t bytes);
+int mtxc_copy_device(void* dst_device, const void* src_device, size_t bytes);
+int mtxc_memset(void* dptr, int value, size_t bytes);
+
+/* ------------------------------------------------------------------------------------------
+ * Shape folding (host, no device work).  Same results as the reference's helpers, bit for
+ * bit, including uint32 arithmetic.  Outputs are arrays of MTXC_MAX_DIMS entries; the
+ * return value is the collapsed rank (`out_dims`).
+ * ---------------------------------------------------------------------------------------- */
+
+/* collapse_dims, 1 / 2 / 3 operands (Mods/Utils.mm:114-136, 138-166, 169-202). */
+uint32_t mtxc_collapse_dims1(const uint32_t* shape, const uint32_t* s0, uint32_t dims, uint64_t size_cap,
+                             uint32_t* out_shape, uint32_t* out_s0);
+uint32_t mtxc_collapse_dims2(const uint32_t* shape, const uint32_t* s0, const uint32_t* s1, uint32_t dims,
+                             uint64_t size_cap, uint32_t* out_shape, uint32_t* out_s0, uint32_t* out_s1);
+uint32_t mtxc_collapse_dims3(const uint32_t* shape, const uint32_t* s0, const uint32_t* s1, const uint32_t* s2,
+                             uint32_t dims, uint64_t size_cap, uint32_t* out_shape, uint32_t* out_s0,
+                             uint32_t* out_s1, uint32_t* out_s2);
+/* collapse_dims_reduce, 1 / 2 / 3 operands (Mods/Utils.mm:270-319, 321-376, 378-435). */
+uint32_t mtxc_collapse_dims_reduce1(const uint32_t* shape, const uint32_t* s_out, uint32_t dims, int axis,
+                                    int keep_dims, uint64_t size_cap, uint32_t* out_shape, uint32_t* out_s_out);
+uint32_t mtxc_collapse_dims_reduce2(const uint32_t* shape, const uint32_t* s_out, const uint32_t* s_in,
+                                    uint32_t dims, int axis, int keep_dims, int outer_collapsed,
+                                    uint64_t size_cap, uint32_t* out_shape, uint32_t* out_s_out,
+                                    uint32_t* out_s_in);
+uint32_t mtxc_collapse_dims_reduce3(const uint32_t* shape, const uint32_t* s_out, const uint32_t* s_b,
+                                    const uint32_t* s_c, uint32_t dims, int axis, int keep_dims,
+                                    uint64_t size_cap, uint32_t* out_shape, uint32_t* out_s_out,
+                                    uint32_t* out_s_b, uint32_t* out_s_c);
+
+/* broadcast_shapes (Matrix.mm:161-232): right-aligned broadcast of (shape1, strides1, dim1)
+ * against (shape2, strides2, dim2).  Fills the output shape and row-major strides and each
+ * operand's broadcast shape and strides (0 on broadcast axes), max(dim1, dim2) entries
+ * each.  Returns MTXC_ERR_SHAPE where the reference throws std::invalid_argument. */
+int mtxc_broadcast_shapes(const uint32_t* shape1, const uint32_t* strides1, int dim1, const uint32_t* shape2,
+                          const uint32_t* strides2, int dim2, uint32_t* out_shape, uint32_t* out_strides,
+                          uint32_t* a_shape, uint32_t* a_strides, uint32_t* b_shape, uint32_t* b_strides);
+
+/* promote_types (Matrix.mm:107-109, table matrix.h:166-180).  Returns the dtype code, or -1
+ * for an out-of-range code. */
+int mtxc_promote_types(int a, int b);
+
+/* ------------------------------------------------------------------------------------------
+ * Hot path.
+ * ---------------------------------------------------------------------------------------- */
+
+/* Axis reduction.  Replaces the METAL branch of matrix::sum / max / min / argmax / argmin
+ * (Matrix.mm:15134-15186, 14841-14893, 14985-15037, 16211-16276, 16366-16431) and carries
+ * exactly what those branches bind: the reduced axis' input stride and length, and the
+ * primitive's collapsed metadata (collapse_dims_reduce with the output strides first).
+ *
+ * Output element gid (0 <= gid < prod(shape[0..cdims))) is written at dst[gid]; its input
+ * run starts at src + sum_i (rem / dst_strides[i]) * src_strides[i] (rem %= dst_strides[i])
+ * and holds reduce_len elements reduce_stride apart.  cdims == 0 means a single output.
+ *
+ * Results equal the reference CPU eval (Matrix.mm:15187-15207, 14894-14914, 15038-15058,
+ * 16279-16302, 16434-16457): integer sums wrap like the reference's T accumulator; Max / Min
+ * return the first element (lowest index) among the equal extremes, starting from
+ * dtype_lowest / dtype_max, and never select NaN; ArgMax / ArgMin write int32 indices, the
+ * first one on ties, 0 when no element beats the initial value.  Float sums are summed in a
+ * different order (tree instead of sequential), so they agree within rounding.
+ * dtypes: float, int32, uint32, int64, uint64, int16, uint16, int8, uint8. */
+int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
+                uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides, const uint32_t* src_strides);
+
+/* Broadcasted binary op.  Replaces add/subtract/multiply/divide_gpu_brodcasted
+ * (Matrix.mm:7709-8239) and the METAL branch of matrix::max / min(other, result, dev)
+ * (Matrix.mm:13396-13450, 14701-14755), binding the primitive's collapsed_dims_3:
+ * shape, the result strides, and the per-operand strides (0 on broadcast axes).
+ *
+ * Result element gid (0 <= gid < prod(shape)) is written at r[gid] and equals
+ * a[sum idx_i * a_strides[i]] op b[sum idx_i * b_strides[i]] with idx_i decoded from gid by
+ * the result strides (Matrix.mm:7475-7498).  cdims == 0 is the scalar case.  Float results
+ * are bit-exact with the reference CPU (one IEEE-rounded op per element, no contraction);
+ * Max / Min keep `a` unless `b` is strictly greater / smaller (std::max / std::min).
+ * Integer results wrap; integer division by zero is undefined, as in the reference.
+ * Both operands have dtype `dtype` (the reference promotes with astype first). */
+int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, const void* b, uint32_t cdims,
+                          const uint32_t* shape, const uint32_t* r_strides, const uint32_t* a_strides,
+                          const uint32_t* b_strides);
+
+/* Elementwise unary op over collapse_dims(shape, out strides, in strides) metadata
+ * (Matrix.mm:6934-7065).  EXP on float: CUDA expf, within 2 ulp of the CPU's std::exp. */
+int mtxc_unary(int op, int dtype, void* dst, const void* src, uint32_t cdims, const uint32_t* shape,
+               const uint32_t* dst_strides, const uint32_t* src_strides);
+
+/* ------------------------------------------------------------------------------------------
+ * Compiled trace: record the kernels one execute pass enqueues and replay them.  The B200
+ * form of the reference's compile-once / execute-many model (Matrix.mm:8452-8475).
+ * ---------------------------------------------------------------------------------------- */
+
+/* Starts capturing the calling thread's stream into a CUDA graph. */
+int mtxc_graph_begin(void);
+/* Ends the capture and instantiates it; *graph receives an opaque handle. */
+int mtxc_graph_end(void** graph);
+/* Replays a captured graph on the calling thread's stream. */
+int mtxc_graph_launch(void* graph);
+int mtxc_graph_destroy(void* graph);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MTXC_H */

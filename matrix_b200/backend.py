@@ -1,0 +1,206 @@
+"""Python driver of the C ABI on device tensors.
+
+The functions here mirror the reference's frontends for the hot path: they compute the same
+metadata the reference's graph-building methods cache on their primitive, using the library's
+own shape folding (mtxc_collapse_dims*, mtxc_broadcast_shapes), and then call the backend entry
+point with it.  ``reduce("sum", x, -1)`` is the reference's ``x.sum(-1)`` followed by
+``eval()`` on the GPU (Matrix.mm:15071-15186); ``binary("add", a, b)`` is ``a + b``
+(Matrix.mm:8312-8331, 7709-7868).  PyTorch only provides device memory and streams.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _abi
+from ._abi import check, lib, u32_array
+
+UINT32_MAX = 0xFFFFFFFF
+INT32_MAX = 0x7FFFFFFF
+
+TORCH_DTYPES = {
+    torch.float32: 0, torch.uint8: 2, torch.int32: 3, torch.int16: 4, torch.uint32: 5,
+    torch.uint16: 6, torch.int8: 8, torch.int64: 11, torch.uint64: 12,
+}
+
+
+def dtype_code(t: torch.dtype) -> int:
+    try:
+        return TORCH_DTYPES[t]
+    except KeyError:
+        raise _abi.MtxcError(_abi.ERR_UNSUPPORTED_DTYPE, f"no kernel for {t}") from None
+
+
+def init(device: int = 0, stream: torch.cuda.Stream | None = None) -> None:
+    """Binds the calling thread to `device` and makes `stream` (default: torch's current
+    stream on that device) the stream the backend launches on."""
+    check(lib().mtxc_init(int(device)))
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    check(lib().mtxc_set_stream(stream.cuda_stream))
+
+
+def set_stream(stream: torch.cuda.Stream) -> None:
+    check(lib().mtxc_set_stream(stream.cuda_stream))
+
+
+def sync() -> None:
+    check(lib().mtxc_sync())
+
+
+def row_major(shape):
+    strides, acc = [0] * len(shape), 1
+    for i in range(len(shape) - 1, -1, -1):
+        strides[i] = acc & 0xFFFFFFFF
+        acc *= int(shape[i])
+    return strides
+
+
+# ------------------------------------------------------------------------------------------
+# Frontend metadata
+# ------------------------------------------------------------------------------------------
+@dataclass
+class ReduceMeta:
+    out_shape: list
+    cdims: int
+    shape: list
+    s_out: list
+    s_in: list
+    rstride: int
+    rlen: int
+    arrays: tuple = field(default=(), repr=False)
+
+
+def reduce_meta(shape, strides, axis: int, keepdims: bool = False) -> ReduceMeta:
+    """Output shape and collapse_dims_reduce(shape, out.strides, in.strides, dims, axis, false,
+    !keepdims, UINT32_MAX), as matrix::sum / max / min / argmax / argmin build them
+    (Matrix.mm:15071-15097, 14784-14810, 14927-14954, 16150-16180, 16305-16335)."""
+    dims = len(shape)
+    if dims == 0:
+        raise ValueError("reduction of a 0-d tensor")
+    if axis < 0:
+        axis += dims
+    if not 0 <= axis < dims:
+        raise ValueError(f"axis {axis} out of range for rank {dims}")
+    if keepdims:
+        out_shape = list(shape)
+        out_shape[axis] = 1
+    else:
+        out_shape = list(shape[:axis]) + list(shape[axis + 1:])
+    out_strides = row_major(out_shape) + [0] * (dims - len(out_shape))
+    o = [u32_array([]) for _ in range(3)]
+    k = lib().mtxc_collapse_dims_reduce2(u32_array(shape), u32_array(out_strides), u32_array(strides), dims, axis, 0,
+                                         int(not keepdims), UINT32_MAX, *o)
+    arr = tuple(o)
+    return ReduceMeta(out_shape, k, list(o[0][:k]), list(o[1][:k]), list(o[2][:k]), int(strides[axis]),
+                      int(shape[axis]), arr)
+
+
+@dataclass
+class BinaryMeta:
+    out_shape: list
+    cdims: int
+    shape: list
+    sr: list
+    sa: list
+    sb: list
+    arrays: tuple = field(default=(), repr=False)
+
+
+def binary_meta(shape_a, strides_a, shape_b, strides_b) -> BinaryMeta:
+    """broadcast_shapes, then collapse_dims(desc_a.shape, desc_a.strides, desc_b.strides,
+    result.strides, dims, INT32_MAX), as operator+ - * / and matrix::max / min(a, b) do
+    (Matrix.mm:8312-8382, 13363-13376, 14668-14682)."""
+    od = max(len(shape_a), len(shape_b))
+    outs = [u32_array([]) for _ in range(6)]
+    rc = lib().mtxc_broadcast_shapes(u32_array(shape_a), u32_array(strides_a), len(shape_a), u32_array(shape_b),
+                                     u32_array(strides_b), len(shape_b), *outs)
+    if rc == _abi.ERR_SHAPE:
+        raise ValueError("Incompatible shapes for broadcasting")
+    check(rc)
+    out_shape, out_strides, a_shape, a_strides, _b_shape, b_strides = outs
+    o = [u32_array([]) for _ in range(4)]
+    k = lib().mtxc_collapse_dims3(a_shape, a_strides, b_strides, out_strides, od, INT32_MAX, *o)
+    return BinaryMeta(list(out_shape[:od]), k, list(o[0][:k]), list(o[3][:k]), list(o[1][:k]), list(o[2][:k]),
+                      (o[0], o[3], o[1], o[2]))
+
+
+@dataclass
+class UnaryMeta:
+    out_shape: list
+    cdims: int
+    shape: list
+    s_out: list
+    s_in: list
+    arrays: tuple = field(default=(), repr=False)
+
+
+def unary_meta(shape, strides) -> UnaryMeta:
+    """collapse_dims(shape, out.strides, in.strides, dims, INT32_MAX) (Matrix.mm:6934-6947)."""
+    o = [u32_array([]) for _ in range(3)]
+    k = lib().mtxc_collapse_dims2(u32_array(shape), u32_array(row_major(shape)), u32_array(strides), len(shape),
+                                  INT32_MAX, *o)
+    return UnaryMeta(list(shape), k, list(o[0][:k]), list(o[1][:k]), list(o[2][:k]), tuple(o))
+
+
+# ------------------------------------------------------------------------------------------
+# Device ops
+# ------------------------------------------------------------------------------------------
+def _check_strides(x: torch.Tensor):
+    st = x.stride()
+    if any(s < 0 for s in st):
+        raise ValueError("negative strides are not representable in the reference's size_m metadata")
+    return list(st)
+
+
+def reduce_launch(op: str, x_ptr: int, dtype: int, out_ptr: int, meta: ReduceMeta) -> None:
+    shape, s_out, s_in = meta.arrays
+    check(lib().mtxc_reduce(_abi.REDUCE_OPS[op], dtype, out_ptr, x_ptr, meta.rstride & 0xFFFFFFFF, meta.rlen,
+                            meta.cdims, shape, s_out, s_in))
+
+
+def reduce(op: str, x: torch.Tensor, axis: int, keepdims: bool = False, out: torch.Tensor | None = None,
+           meta: ReduceMeta | None = None) -> torch.Tensor:
+    """x.<op>(axis, keepdims) evaluated on the GPU through mtxc_reduce."""
+    code = dtype_code(x.dtype)
+    if meta is None:
+        meta = reduce_meta(list(x.shape), _check_strides(x), axis, keepdims)
+    odt = torch.int32 if op in ("argmax", "argmin") else x.dtype
+    if out is None:
+        out = torch.empty(meta.out_shape, dtype=odt, device=x.device)
+    reduce_launch(op, x.data_ptr(), code, out.data_ptr(), meta)
+    return out
+
+
+def binary_launch(op: str, a_ptr: int, b_ptr: int, dtype: int, out_ptr: int, meta: BinaryMeta) -> None:
+    shape, sr, sa, sb = meta.arrays
+    check(lib().mtxc_broadcast_binary(_abi.BINARY_OPS[op], dtype, out_ptr, a_ptr, b_ptr, meta.cdims, shape, sr, sa,
+                                      sb))
+
+
+def binary(op: str, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+           meta: BinaryMeta | None = None) -> torch.Tensor:
+    """a <op> b with broadcasting, evaluated through mtxc_broadcast_binary.  Both operands must
+    already share a dtype (the reference inserts astype before the op)."""
+    if a.dtype != b.dtype:
+        raise _abi.MtxcError(_abi.ERR_UNSUPPORTED_DTYPE, "operands must share a dtype (astype first)")
+    code = dtype_code(a.dtype)
+    if meta is None:
+        meta = binary_meta(list(a.shape), _check_strides(a), list(b.shape), _check_strides(b))
+    if out is None:
+        out = torch.empty(meta.out_shape, dtype=a.dtype, device=a.device)
+    binary_launch(op, a.data_ptr(), b.data_ptr(), code, out.data_ptr(), meta)
+    return out
+
+
+def exp(x: torch.Tensor, out: torch.Tensor | None = None, meta: UnaryMeta | None = None) -> torch.Tensor:
+    """matrix::exp(x) evaluated through mtxc_unary."""
+    code = dtype_code(x.dtype)
+    if meta is None:
+        meta = unary_meta(list(x.shape), _check_strides(x))
+    if out is None:
+        out = torch.empty(meta.out_shape, dtype=x.dtype, device=x.device)
+    shape, so, si = meta.arrays
+    check(lib().mtxc_unary(_abi.UNARY_OPS["exp"], code, out.data_ptr(), x.data_ptr(), meta.cdims, shape, so, si))
+    return out

@@ -1,0 +1,269 @@
+// Broadcasted binary ops (Add, Sub, Mul, Divide, Max, Min) for sm_100a.
+//
+// Replaces ComputeShaders/Brodcasted{Add,Sub,Mul,Divide,Max,Min}.metal behind
+// add/subtract/multiply/divide_gpu_brodcasted (Matrix.mm:7709-8239) and the METAL branch of
+// matrix::max / min(other, result, dev) (Matrix.mm:13378-13476, 14683-14783).
+//
+// Semantics follow the reference CPU loops (Matrix.mm:7475-7498 and siblings): result element
+// gid, decoded axis by axis with the result strides, reads a and b through their own strides
+// (0 on broadcast axes).  Float ops are one IEEE round-to-nearest operation each
+// (__fadd_rn & co. keep the compiler from contracting anything), so results are bit-exact
+// with the CPU; Max / Min keep `a` unless `b` is strictly greater / smaller (std::max /
+// std::min); integer arithmetic wraps.
+//
+// Two kernels:
+//   rows     the result is contiguous (row-major strides), and along the innermost axis each
+//            operand is either contiguous or broadcast (stride 1 or 0) with 16-byte aligned
+//            rows.  Rows of the innermost axis are spread over threads: a row is decoded once
+//            (a few fast divisions) and then streamed with 128-bit loads of the contiguous
+//            operands (through L2, where broadcast operands stay resident) and 128-bit
+//            evict-first stores of the result.
+//   generic  anything else: a grid-stride loop over elements with the reference's per-element
+//            stride decode.
+#include <algorithm>
+
+#include "mtxc_internal.cuh"
+
+namespace mtxc {
+namespace {
+
+constexpr int kBlock = 256;
+
+template <int OP, typename T>
+__device__ __forceinline__ T apply(T x, T y) {
+    if constexpr (std::is_same_v<T, float>) {
+        if constexpr (OP == MTXC_BINARY_ADD) return __fadd_rn(x, y);
+        else if constexpr (OP == MTXC_BINARY_SUB) return __fsub_rn(x, y);
+        else if constexpr (OP == MTXC_BINARY_MUL) return __fmul_rn(x, y);
+        else if constexpr (OP == MTXC_BINARY_DIV) return __fdiv_rn(x, y);
+        else if constexpr (OP == MTXC_BINARY_MAX) return (x < y) ? y : x;
+        else return (y < x) ? y : x;
+    } else {
+        // integers: C++ promotion then truncation back to T, with the + - * done in unsigned
+        // arithmetic so that overflow wraps as it does on the reference's CPU
+        using W = std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>;
+        if constexpr (OP == MTXC_BINARY_ADD) return (T)(W)((W)x + (W)y);
+        else if constexpr (OP == MTXC_BINARY_SUB) return (T)(W)((W)x - (W)y);
+        else if constexpr (OP == MTXC_BINARY_MUL) return (T)(W)((W)x * (W)y);
+        else if constexpr (OP == MTXC_BINARY_DIV) {
+            using P = decltype(x / y);  // the promoted type the reference divides in
+            return (T)((P)x / (P)y);
+        } else if constexpr (OP == MTXC_BINARY_MAX) return (x < y) ? y : x;
+        else return (y < x) ? y : x;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// rows: contiguous result, innermost operand strides in {0, 1}
+// ------------------------------------------------------------------------------------------
+struct RowArgs {
+    void* r;
+    const void* a;
+    const void* b;
+    uint32_t rows;       // number of innermost rows
+    uint32_t vec_per_row;
+    uint32_t tpr;        // threads per row (power of two, <= kBlock)
+    uint32_t a_inner;    // innermost stride of a (0 or 1)
+    uint32_t b_inner;
+    Dims d;              // outer axes: shape (fast divisors), a strides in s0, b strides in s1
+};
+
+template <int OP, typename T>
+__global__ void __launch_bounds__(kBlock) broadcast_rows_kernel(const RowArgs args) {
+    constexpr int V = Vec16<T>::N;
+    const uint32_t rows_per_block = kBlock / args.tpr;
+    const uint32_t sub = threadIdx.x / args.tpr;
+    const uint32_t lane = threadIdx.x % args.tpr;
+    const T* __restrict__ pa = static_cast<const T*>(args.a);
+    const T* __restrict__ pb = static_cast<const T*>(args.b);
+    T* __restrict__ pr = static_cast<T*>(args.r);
+    const uint64_t row_len = (uint64_t)args.vec_per_row * V;
+
+    for (uint64_t row = (uint64_t)blockIdx.x * rows_per_block + sub; row < args.rows;
+         row += (uint64_t)gridDim.x * rows_per_block) {
+        uint64_t oa = 0, ob = 0;
+        uint32_t rem = (uint32_t)row;
+#pragma unroll 1
+        for (int i = (int)args.d.n - 1; i >= 0; --i) {
+            uint32_t q, idx;
+            args.d.fdiv[i].divmod(rem, q, idx);
+            oa += (uint64_t)idx * args.d.s0[i];
+            ob += (uint64_t)idx * args.d.s1[i];
+            rem = q;
+        }
+        const T* ra = pa + oa;
+        const T* rb = pb + ob;
+        T* rr = pr + row * row_len;
+        Vec16<T> sa, sb;
+        if (!args.a_inner) {
+            const T v = ra[0];
+#pragma unroll
+            for (int j = 0; j < V; ++j) sa.v[j] = v;
+        }
+        if (!args.b_inner) {
+            const T v = rb[0];
+#pragma unroll
+            for (int j = 0; j < V; ++j) sb.v[j] = v;
+        }
+#pragma unroll 4
+        for (uint32_t c = lane; c < args.vec_per_row; c += args.tpr) {
+            const Vec16<T> xa = args.a_inner ? load_cached(ra + (uint64_t)c * V) : sa;
+            const Vec16<T> xb = args.b_inner ? load_cached(rb + (uint64_t)c * V) : sb;
+            Vec16<T> out;
+#pragma unroll
+            for (int j = 0; j < V; ++j) out.v[j] = apply<OP, T>(xa.v[j], xb.v[j]);
+            store_stream(rr + (uint64_t)c * V, out);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// generic: the reference's per-element decode (Matrix.mm:7486-7494)
+// ------------------------------------------------------------------------------------------
+struct GenericArgs {
+    void* r;
+    const void* a;
+    const void* b;
+    uint64_t total;
+    uint32_t cdims;
+    uint32_t sr[MTXC_MAX_DIMS];
+    uint32_t sa[MTXC_MAX_DIMS];
+    uint32_t sb[MTXC_MAX_DIMS];
+    FastDiv fr[MTXC_MAX_DIMS];  // divisors = result strides (used when total < 2^32)
+};
+
+template <int OP, typename T, bool k32>
+__global__ void __launch_bounds__(kBlock) broadcast_generic_kernel(const GenericArgs g) {
+    const T* __restrict__ pa = static_cast<const T*>(g.a);
+    const T* __restrict__ pb = static_cast<const T*>(g.b);
+    T* __restrict__ pr = static_cast<T*>(g.r);
+    for (uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < g.total;
+         gid += (uint64_t)gridDim.x * blockDim.x) {
+        uint64_t ia = 0, ib = 0;
+        if constexpr (k32) {
+            uint32_t rem = (uint32_t)gid;
+            for (uint32_t i = 0; i < g.cdims; ++i) {
+                uint32_t q, r;
+                g.fr[i].divmod(rem, q, r);
+                ia += (uint64_t)q * g.sa[i];
+                ib += (uint64_t)q * g.sb[i];
+                rem = r;
+            }
+        } else {
+            uint64_t rem = gid;
+            for (uint32_t i = 0; i < g.cdims; ++i) {
+                const uint64_t q = rem / g.sr[i];
+                ia += q * g.sa[i];
+                ib += q * g.sb[i];
+                rem %= g.sr[i];
+            }
+        }
+        pr[gid] = apply<OP, T>(pa[ia], pb[ib]);
+    }
+}
+
+template <int OP, typename T>
+__global__ void broadcast_scalar_kernel(void* r, const void* a, const void* b) {
+    static_cast<T*>(r)[0] = apply<OP, T>(static_cast<const T*>(a)[0], static_cast<const T*>(b)[0]);
+}
+
+template <int OP, typename T>
+int launch_broadcast(void* r, const void* a, const void* b, uint32_t cdims, const uint32_t* shape,
+                     const uint32_t* sr, const uint32_t* sa, const uint32_t* sb, int sm_count, cudaStream_t stream) {
+    constexpr uint32_t V = Vec16<T>::N;
+    if (cdims == 0) {
+        broadcast_scalar_kernel<OP, T><<<1, 1, 0, stream>>>(r, a, b);
+        return check_launch("broadcast_scalar_kernel");
+    }
+    const uint64_t total = product(shape, cdims);
+    if (total == 0) return MTXC_OK;
+    const uint32_t k = cdims - 1;
+    bool rows_ok = is_row_major(shape, sr, cdims) && sr[k] == 1 && (sa[k] <= 1) && (sb[k] <= 1) &&
+                   shape[k] % V == 0 && aligned16(r) && aligned16(a) && aligned16(b) && total / shape[k] < (1ull << 32);
+    for (uint32_t i = 0; i < k && rows_ok; ++i)
+        rows_ok = shape[i] == 1 || (sa[i] % V == 0 && sb[i] % V == 0);
+    if (rows_ok) {
+        RowArgs args{};
+        args.r = r;
+        args.a = a;
+        args.b = b;
+        args.rows = (uint32_t)(total / shape[k]);
+        args.vec_per_row = shape[k] / V;
+        uint32_t tpr = 1;
+        while (tpr < args.vec_per_row && tpr < (uint32_t)kBlock) tpr <<= 1;
+        args.tpr = tpr;
+        args.a_inner = sa[k];
+        args.b_inner = sb[k];
+        args.d.n = k;
+        for (uint32_t i = 0; i < k; ++i) {
+            args.d.shape[i] = shape[i];
+            args.d.s0[i] = sa[i];
+            args.d.s1[i] = sb[i];
+            args.d.fdiv[i] = FastDiv(shape[i]);
+        }
+        const uint32_t rows_per_block = kBlock / tpr;
+        uint64_t blocks = (args.rows + rows_per_block - 1) / rows_per_block;
+        blocks = std::min<uint64_t>(blocks, (uint64_t)sm_count * 8);
+        broadcast_rows_kernel<OP, T><<<(unsigned)blocks, kBlock, 0, stream>>>(args);
+        return check_launch("broadcast_rows_kernel");
+    }
+    GenericArgs g{};
+    g.r = r;
+    g.a = a;
+    g.b = b;
+    g.total = total;
+    g.cdims = cdims;
+    for (uint32_t i = 0; i < cdims; ++i) {
+        if (sr[i] == 0) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: zero result stride");
+        g.sr[i] = sr[i];
+        g.sa[i] = sa[i];
+        g.sb[i] = sb[i];
+        g.fr[i] = FastDiv(sr[i]);
+    }
+    const uint64_t blocks = std::min<uint64_t>((total + kBlock - 1) / kBlock, (uint64_t)sm_count * 16);
+    if (total < (1ull << 32)) broadcast_generic_kernel<OP, T, true><<<(unsigned)blocks, kBlock, 0, stream>>>(g);
+    else broadcast_generic_kernel<OP, T, false><<<(unsigned)blocks, kBlock, 0, stream>>>(g);
+    return check_launch("broadcast_generic_kernel");
+}
+
+template <typename T>
+int launch_broadcast_op(int op, void* r, const void* a, const void* b, uint32_t cdims, const uint32_t* shape,
+                        const uint32_t* sr, const uint32_t* sa, const uint32_t* sb, int sms, cudaStream_t st) {
+    switch (op) {
+        case MTXC_BINARY_ADD: return launch_broadcast<MTXC_BINARY_ADD, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
+        case MTXC_BINARY_SUB: return launch_broadcast<MTXC_BINARY_SUB, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
+        case MTXC_BINARY_MUL: return launch_broadcast<MTXC_BINARY_MUL, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
+        case MTXC_BINARY_DIV: return launch_broadcast<MTXC_BINARY_DIV, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
+        case MTXC_BINARY_MAX: return launch_broadcast<MTXC_BINARY_MAX, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
+        case MTXC_BINARY_MIN: return launch_broadcast<MTXC_BINARY_MIN, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
+        default: return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: unknown op");
+    }
+}
+
+}  // namespace
+}  // namespace mtxc
+
+using namespace mtxc;
+
+extern "C" int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, const void* b, uint32_t cdims,
+                                     const uint32_t* shape, const uint32_t* r_strides, const uint32_t* a_strides,
+                                     const uint32_t* b_strides) {
+    if (int rc = require_init()) return rc;
+    if (op < MTXC_BINARY_ADD || op > MTXC_BINARY_MIN)
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: unknown op");
+    if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: cdims > MTXC_MAX_DIMS");
+    if (cdims && (!shape || !r_strides || !a_strides || !b_strides))
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: null metadata pointer");
+    if (cdims && product(shape, cdims) == 0) return MTXC_OK;
+    if (!r || !a || !b) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: null buffer");
+    ThreadCtx& c = ctx();
+    int rc = MTXC_OK;
+    const bool known = dispatch_dtype(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        rc = launch_broadcast_op<T>(op, r, a, b, cdims, shape, r_strides, a_strides, b_strides, c.sm_count, c.stream());
+    });
+    if (!known)
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE,
+                    std::string("mtxc_broadcast_binary: no kernel for dtype ") + dtype_name(dtype));
+    return rc;
+}

@@ -1,0 +1,180 @@
+// Internal definitions shared by the mtxc translation units: the per-thread runtime context,
+// error reporting, dtype dispatch, 32-bit fast division and the 128-bit memory helpers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <type_traits>
+
+#include "mtxc.h"
+
+namespace mtxc {
+
+// ------------------------------------------------------------------------------------------
+// Runtime context: one per host thread, the analogue of the reference's thread-local command
+// buffer and encoder (Mods/GPUManager.h:57-58).
+// ------------------------------------------------------------------------------------------
+struct ThreadCtx {
+    int device = -1;
+    cudaStream_t own_stream = nullptr;   // created by mtxc_init
+    cudaStream_t user_stream = nullptr;  // set by mtxc_set_stream
+    void* workspace = nullptr;
+    size_t workspace_bytes = 0;
+    bool own_workspace = false;
+    int sm_count = 148;
+    std::string last_error;
+    cudaStream_t stream() const { return user_stream ? user_stream : own_stream; }
+};
+
+ThreadCtx& ctx();
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t err, const char* what);
+// Checks that mtxc_init ran on this thread; returns MTXC_OK or an error status.
+int require_init();
+// Checks the launch that just happened; returns MTXC_OK or MTXC_ERR_CUDA.
+int check_launch(const char* what);
+
+// ------------------------------------------------------------------------------------------
+// dtype dispatch.  The functor receives a null pointer of the element type.
+// ------------------------------------------------------------------------------------------
+template <typename Fn>
+bool dispatch_dtype(int dtype, Fn&& fn) {
+    switch (dtype) {
+        case MTXC_FLOAT: fn((float*)nullptr); return true;
+        case MTXC_INT32: fn((int32_t*)nullptr); return true;
+        case MTXC_UINT32: fn((uint32_t*)nullptr); return true;
+        case MTXC_INT64: fn((int64_t*)nullptr); return true;
+        case MTXC_UINT64: fn((uint64_t*)nullptr); return true;
+        case MTXC_INT16: fn((int16_t*)nullptr); return true;
+        case MTXC_UINT16: fn((uint16_t*)nullptr); return true;
+        case MTXC_INT8: fn((int8_t*)nullptr); return true;
+        case MTXC_UINT8: fn((uint8_t*)nullptr); return true;
+        default: return false;
+    }
+}
+const char* dtype_name(int dtype);
+
+// Smallest / largest finite value: dtype_lowest / dtype_max (matrix.h:271-282).
+template <typename T>
+__host__ __device__ constexpr T lowest_value() {
+    if constexpr (std::is_same_v<T, float>) return -3.402823466e+38f;
+    else if constexpr (std::is_signed_v<T>) return T(T(1) << (sizeof(T) * 8 - 1));
+    else return T(0);
+}
+template <typename T>
+__host__ __device__ constexpr T highest_value() {
+    if constexpr (std::is_same_v<T, float>) return 3.402823466e+38f;
+    else if constexpr (std::is_signed_v<T>) return T(~(T(1) << (sizeof(T) * 8 - 1)));
+    else return T(~T(0));
+}
+
+// ------------------------------------------------------------------------------------------
+// Metadata passed by value to kernels.
+// ------------------------------------------------------------------------------------------
+// Division by a runtime-invariant 32-bit divisor via a multiply-high (Granlund & Montgomery,
+// "Division by invariant integers using multiplication", PLDI 1994, round-up variant):
+// q = (umulhi(n, m) + n) >> s with s = ceil(log2 d), m = floor(2^32 (2^s - d) / d) + 1.
+// Exact for every 32-bit n and 1 <= d < 2^31.
+struct FastDiv {
+    uint32_t d = 1, m = 0, s = 0;
+    FastDiv() = default;
+    explicit FastDiv(uint32_t div) : d(div) {
+        s = 0;
+        while ((1ull << s) < div) ++s;
+        m = (uint32_t)(((1ull << 32) * ((1ull << s) - div)) / div + 1);
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        return (uint32_t)(((uint64_t)__umulhi(n, m) + n) >> s);
+    }
+    __device__ __forceinline__ void divmod(uint32_t n, uint32_t& q, uint32_t& r) const {
+        q = div(n);
+        r = n - q * d;
+    }
+};
+
+// Per-axis metadata (reference collapsed dims), at most MTXC_MAX_DIMS axes.
+struct Dims {
+    uint32_t n = 0;
+    uint32_t shape[MTXC_MAX_DIMS];
+    uint32_t s0[MTXC_MAX_DIMS];
+    uint32_t s1[MTXC_MAX_DIMS];
+    uint32_t s2[MTXC_MAX_DIMS];
+    FastDiv fdiv[MTXC_MAX_DIMS];  // per-axis divisor (shape or stride, as the kernel needs)
+};
+
+inline uint64_t product(const uint32_t* shape, uint32_t n) {
+    uint64_t p = 1;
+    for (uint32_t i = 0; i < n; ++i) p *= shape[i];
+    return p;
+}
+
+// True when strides are the row-major strides of shape (axes of extent 1 are ignored).
+inline bool is_row_major(const uint32_t* shape, const uint32_t* strides, uint32_t n) {
+    uint64_t acc = 1;
+    for (int i = (int)n - 1; i >= 0; --i) {
+        if (shape[i] != 1 && strides[i] != acc) return false;
+        acc *= shape[i];
+    }
+    return true;
+}
+
+// ------------------------------------------------------------------------------------------
+// 128-bit memory helpers.
+// ------------------------------------------------------------------------------------------
+template <typename T>
+struct alignas(16) Vec16 {
+    static constexpr int N = 16 / sizeof(T);
+    T v[N];
+};
+
+// Streaming read that bypasses L1 (data read once).
+template <typename T>
+__device__ __forceinline__ Vec16<T> load_stream(const T* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    Vec16<T> out;
+    memcpy(&out, &r, 16);
+    return out;
+}
+// Read through the read-only path (data reused across threads: broadcast operands).
+template <typename T>
+__device__ __forceinline__ Vec16<T> load_cached(const T* p) {
+    uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    Vec16<T> out;
+    memcpy(&out, &r, 16);
+    return out;
+}
+// Streaming scalar read of any 1/2/4/8-byte element type.
+template <typename T>
+__device__ __forceinline__ T load_scalar_stream(const T* p) {
+    T out;
+    if constexpr (sizeof(T) == 8) {
+        unsigned long long r = __ldcs(reinterpret_cast<const unsigned long long*>(p));
+        memcpy(&out, &r, 8);
+    } else if constexpr (sizeof(T) == 4) {
+        unsigned int r = __ldcs(reinterpret_cast<const unsigned int*>(p));
+        memcpy(&out, &r, 4);
+    } else if constexpr (sizeof(T) == 2) {
+        unsigned short r = __ldcs(reinterpret_cast<const unsigned short*>(p));
+        memcpy(&out, &r, 2);
+    } else {
+        unsigned char r = __ldcs(reinterpret_cast<const unsigned char*>(p));
+        memcpy(&out, &r, 1);
+    }
+    return out;
+}
+// Streaming (evict-first) store: the output is written once and not re-read by this op.
+template <typename T>
+__device__ __forceinline__ void store_stream(T* p, const Vec16<T>& v) {
+    uint4 r;
+    memcpy(&r, &v, 16);
+    __stcs(reinterpret_cast<uint4*>(p), r);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace mtxc

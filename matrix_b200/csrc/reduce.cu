@@ -1,0 +1,688 @@
+// Axis reductions (Sum, Max, Min, ArgMax, ArgMin) for sm_100a.
+//
+// Replaces the reference's Metal reduction kernels (ComputeShaders/Sum.metal, Max.metal,
+// Min.metal, ArgMax.metal, ArgMin.metal) behind the METAL branch of matrix::sum / max / min /
+// argmax / argmin (Matrix.mm:14812-16458).  The results follow the reference CPU eval:
+//   Sum     T accumulator from 0; integer sums wrap (accumulated in the unsigned type of the
+//           accumulator width, which is the same value modulo 2^bits); float sums agree
+//           within rounding (tree order instead of sequential order).
+//   Max/Min start from dtype_lowest / dtype_max; an element replaces the running value only
+//           when strictly greater / smaller, so NaN never wins and among equal extremes the
+//           first one is kept (this matters for floats: -0.0 vs +0.0).
+//   ArgMax/ArgMin (value, index) with the same strict rule; the lowest index wins ties; 0 when
+//           no element beats the initial value.  Output int32.
+// Float Max / Min therefore carry the element index too: a (value, index) pair reduction is
+// the one order-free formulation of "first among equals", which is what lets the kernels
+// read elements in any order (vector lanes, interleaved rows, split axes).
+//
+// Three kernels, chosen on the host from the collapsed metadata:
+//   rows    reduce_stride == 1: each output reduces a contiguous run.  A warp (G = 32) or a
+//           256-thread CTA (G = 256) owns a (row, split) unit and streams it with 128-bit
+//           loads (scalar head / tail around the 16-byte aligned body).
+//   cols    reduce_stride != 1 and the innermost output axis is contiguous in the input: a
+//           warp spans 32 x (16 / sizeof(T)) consecutive outputs with one 128-bit load per
+//           lane per reduced row, the CTA's 8 warps interleave the reduced rows, and CTAs
+//           split the reduced axis when there are too few outputs to fill 148 SMs.
+//   generic anything else (non-row-major output strides, short rows, odd layouts): one
+//           thread per output walking its run, exactly like the reference CPU loop.
+// When the axis is split across CTAs, per-split partials go to the thread's workspace and a
+// second kernel merges them in split order.
+#include <algorithm>
+#include <map>
+#include <mutex>
+
+#include "mtxc_internal.cuh"
+
+namespace mtxc {
+namespace {
+
+constexpr int kBlock = 256;
+constexpr int kUnroll = 4;
+
+// ------------------------------------------------------------------------------------------
+// Reducer definitions
+// ------------------------------------------------------------------------------------------
+template <typename T>
+struct Pair {
+    T v;
+    int32_t i;
+};
+
+template <typename T>
+using SumAcc = std::conditional_t<std::is_same_v<T, float>, float,
+                                  std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>>;
+
+template <typename T>
+__device__ __forceinline__ T shfl_xor(T v, int mask) {
+    if constexpr (sizeof(T) == 8) {
+        unsigned long long x;
+        memcpy(&x, &v, 8);
+        x = __shfl_xor_sync(0xffffffffu, x, mask);
+        T r;
+        memcpy(&r, &x, 8);
+        return r;
+    } else if constexpr (sizeof(T) == 4) {
+        unsigned x;
+        memcpy(&x, &v, 4);
+        x = __shfl_xor_sync(0xffffffffu, x, mask);
+        T r;
+        memcpy(&r, &x, 4);
+        return r;
+    } else {
+        // 8- and 16-bit values travel sign- or zero-extended in a 32-bit register
+        int x = (int)v;
+        x = __shfl_xor_sync(0xffffffffu, x, mask);
+        return (T)x;
+    }
+}
+
+template <int OP, typename T>
+struct Reducer;
+
+template <typename T>
+struct Reducer<MTXC_REDUCE_SUM, T> {
+    using State = SumAcc<T>;
+    __device__ static State init() { return State(0); }
+    __device__ static void fold(State& s, T v, uint32_t) {
+        if constexpr (std::is_same_v<T, float>) s = __fadd_rn(s, v);
+        else s = (State)(s + (State)v);
+    }
+    __device__ static void merge(State& s, const State& o) {
+        if constexpr (std::is_same_v<T, float>) s = __fadd_rn(s, o);
+        else s = (State)(s + o);
+    }
+    __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
+    __device__ static void store(void* dst, uint64_t gid, const State& s) { static_cast<T*>(dst)[gid] = (T)s; }
+};
+
+// Extremum with index (floats for Max / Min; every type for ArgMax / ArgMin).
+template <typename T, bool kMax>
+struct PairExtremum {
+    using State = Pair<T>;
+    __device__ static State init() { return State{kMax ? lowest_value<T>() : highest_value<T>(), 0}; }
+    __device__ static bool beats(T a, T b) { return kMax ? (a > b) : (a < b); }
+    __device__ static void fold(State& s, T v, uint32_t i) {
+        if (beats(v, s.v)) {
+            s.v = v;
+            s.i = (int32_t)i;
+        }
+    }
+    __device__ static void merge(State& s, const State& o) {
+        if (beats(o.v, s.v) || (o.v == s.v && o.i < s.i)) s = o;
+    }
+    __device__ static State shfl(const State& s, int m) { return State{shfl_xor(s.v, m), shfl_xor(s.i, m)}; }
+};
+
+// Integer Max / Min: equal values are indistinguishable, so no index is needed.
+template <typename T, bool kMax>
+struct ValueExtremum {
+    using State = T;
+    __device__ static State init() { return kMax ? lowest_value<T>() : highest_value<T>(); }
+    __device__ static void fold(State& s, T v, uint32_t) {
+        if (kMax ? (s < v) : (v < s)) s = v;
+    }
+    __device__ static void merge(State& s, const State& o) { fold(s, o, 0); }
+    __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
+    __device__ static void store(void* dst, uint64_t gid, const State& s) { static_cast<T*>(dst)[gid] = s; }
+};
+
+template <typename T>
+struct Reducer<MTXC_REDUCE_MAX, T>
+    : std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, true>, ValueExtremum<T, true>> {
+    using Base = std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, true>, ValueExtremum<T, true>>;
+    __device__ static void store(void* dst, uint64_t gid, const typename Base::State& s) {
+        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(dst)[gid] = s.v;
+        else static_cast<T*>(dst)[gid] = s;
+    }
+};
+template <typename T>
+struct Reducer<MTXC_REDUCE_MIN, T>
+    : std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, false>, ValueExtremum<T, false>> {
+    using Base = std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, false>, ValueExtremum<T, false>>;
+    __device__ static void store(void* dst, uint64_t gid, const typename Base::State& s) {
+        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(dst)[gid] = s.v;
+        else static_cast<T*>(dst)[gid] = s;
+    }
+};
+template <typename T>
+struct Reducer<MTXC_REDUCE_ARGMAX, T> : PairExtremum<T, true> {
+    __device__ static void store(void* dst, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(dst)[gid] = s.i; }
+};
+template <typename T>
+struct Reducer<MTXC_REDUCE_ARGMIN, T> : PairExtremum<T, false> {
+    __device__ static void store(void* dst, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(dst)[gid] = s.i; }
+};
+
+template <typename R>
+__device__ __forceinline__ void warp_reduce(typename R::State& s) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        typename R::State o = R::shfl(s, m);
+        R::merge(s, o);
+    }
+}
+
+// Offset of the run of output `row` (row-major over `shape`) in the input.
+__device__ __forceinline__ uint64_t run_offset(uint32_t row, const Dims& d) {
+    uint64_t off = 0;
+#pragma unroll 1
+    for (int i = (int)d.n - 1; i >= 0; --i) {
+        uint32_t q, r;
+        d.fdiv[i].divmod(row, q, r);
+        off += (uint64_t)r * d.s1[i];
+        row = q;
+    }
+    return off;
+}
+
+// ------------------------------------------------------------------------------------------
+// rows: contiguous reduced axis
+// ------------------------------------------------------------------------------------------
+struct RowArgs {
+    void* dst;
+    const void* src;
+    void* partials;     // S * M states when split > 1
+    uint32_t len;       // elements per run
+    uint32_t seg;       // elements per split (multiple of 16 / sizeof(T) unless split == 1)
+    uint32_t split;     // S
+    uint32_t rows;      // M
+    Dims d;             // shape (with fast divisors) and input strides in s1
+};
+
+template <int OP, typename T, int G>
+__global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
+    using R = Reducer<OP, T>;
+    using S = typename R::State;
+    constexpr int V = Vec16<T>::N;
+    constexpr int kUnitsPerBlock = kBlock / G;
+    __shared__ S warp_partial[kBlock / 32];
+
+    const int slot = threadIdx.x / G;
+    const int lane = threadIdx.x % G;
+    const uint64_t units = (uint64_t)a.rows * a.split;
+    const T* __restrict__ src = static_cast<const T*>(a.src);
+
+    // With G == kBlock every thread of the CTA runs the same trip count (slot == 0), so the
+    // __syncthreads() of the block reduction below is reached uniformly.
+    for (uint64_t u = (uint64_t)blockIdx.x * kUnitsPerBlock + slot; u < units;
+         u += (uint64_t)gridDim.x * kUnitsPerBlock) {
+        const uint32_t row = (uint32_t)(u / a.split);
+        const uint32_t part = (uint32_t)(u - (uint64_t)row * a.split);
+        const uint32_t begin = part * a.seg;
+        const uint32_t end = min(a.len, begin + a.seg);
+        const T* p = src + run_offset(row, a.d);
+
+        S st[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) st[j] = R::init();
+
+        // scalar head up to the first 16-byte boundary
+        uint32_t head = (uint32_t)(((16u - (reinterpret_cast<uintptr_t>(p + begin) & 15u)) & 15u) / sizeof(T));
+        head = min(head, end - begin);
+        if ((uint32_t)lane < head) R::fold(st[0], p[begin + lane], begin + lane);
+        const uint32_t vbeg = begin + head;
+        const uint32_t nvec = (end - vbeg) / V;
+        const T* pv = p + vbeg;
+        uint32_t c = lane;
+        for (; c + (kUnroll - 1) * G < nvec; c += kUnroll * G) {
+            Vec16<T> x[kUnroll];
+#pragma unroll
+            for (int k = 0; k < kUnroll; ++k) x[k] = load_stream(pv + (size_t)(c + k * G) * V);
+#pragma unroll
+            for (int k = 0; k < kUnroll; ++k)
+#pragma unroll
+                for (int j = 0; j < V; ++j) R::fold(st[j], x[k].v[j], vbeg + (c + k * G) * V + j);
+        }
+        for (; c < nvec; c += G) {
+            Vec16<T> x = load_stream(pv + (size_t)c * V);
+#pragma unroll
+            for (int j = 0; j < V; ++j) R::fold(st[j], x.v[j], vbeg + c * V + j);
+        }
+        for (uint32_t i = vbeg + nvec * V + lane; i < end; i += G) R::fold(st[0], p[i], i);
+
+#pragma unroll
+        for (int j = 1; j < V; ++j) R::merge(st[0], st[j]);
+        warp_reduce<R>(st[0]);
+        if constexpr (G == kBlock) {
+            if ((threadIdx.x & 31) == 0) warp_partial[threadIdx.x / 32] = st[0];
+            __syncthreads();
+            if (threadIdx.x < 32) {
+                // init() is an identity for every reducer: a (value, index) state still equal
+                // to its initial value was never updated, so its index is 0, as init's is.
+                S s = threadIdx.x < kBlock / 32 ? warp_partial[threadIdx.x] : R::init();
+                warp_reduce<R>(s);
+                st[0] = s;
+            }
+            __syncthreads();
+        }
+        if (lane == 0) {
+            if (a.split == 1) R::store(a.dst, row, st[0]);
+            else static_cast<S*>(a.partials)[(uint64_t)part * a.rows + row] = st[0];
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// cols: strided reduced axis, contiguous innermost output axis
+// ------------------------------------------------------------------------------------------
+struct ColArgs {
+    void* dst;
+    const void* src;
+    void* partials;
+    uint32_t len;         // reduced axis length
+    uint32_t rstride;     // reduced axis stride (elements)
+    uint32_t seg;         // reduced rows per split
+    uint32_t split;
+    uint32_t inner;       // extent of the innermost output axis
+    uint32_t outer;       // product of the other output axes
+    uint32_t col_tiles;   // CTAs across `inner`
+    uint32_t tx;          // threads across columns (power of two, <= 32)
+    uint64_t outputs;     // M = outer * inner
+    Dims d;               // outer axes: shape (fast divisors) and input strides in s1
+};
+
+template <int OP, typename T, int V>
+__global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
+    using R = Reducer<OP, T>;
+    using S = typename R::State;
+    __shared__ S partial[kBlock * V];
+
+    const uint32_t tx = threadIdx.x % a.tx;
+    const uint32_t ty = threadIdx.x / a.tx;
+    const uint32_t ty_count = kBlock / a.tx;
+    uint32_t b = blockIdx.x;
+    const uint32_t tile = b % a.col_tiles;
+    b /= a.col_tiles;
+    const uint32_t o = b % a.outer;
+    const uint32_t part = b / a.outer;
+    const uint32_t col = (tile * a.tx + tx) * V;
+    const bool active = col < a.inner;
+
+    S st[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) st[j] = R::init();
+
+    if (active) {
+        const T* __restrict__ p = static_cast<const T*>(a.src) + run_offset(o, a.d) + col;
+        const uint32_t begin = part * a.seg;
+        const uint32_t end = min(a.len, begin + a.seg);
+        uint32_t r = begin + ty;
+        const uint32_t step = ty_count;
+        if constexpr (V > 1) {
+            for (; r + (kUnroll - 1) * step < end; r += kUnroll * step) {
+                Vec16<T> x[kUnroll];
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) x[k] = load_stream(p + (size_t)(r + k * step) * a.rstride);
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k)
+#pragma unroll
+                    for (int j = 0; j < V; ++j) R::fold(st[j], x[k].v[j], r + k * step);
+            }
+            for (; r < end; r += step) {
+                Vec16<T> x = load_stream(p + (size_t)r * a.rstride);
+#pragma unroll
+                for (int j = 0; j < V; ++j) R::fold(st[j], x.v[j], r);
+            }
+        } else {
+            for (; r + (kUnroll - 1) * step < end; r += kUnroll * step) {
+                T x[kUnroll];
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) x[k] = load_scalar_stream(p + (size_t)(r + k * step) * a.rstride);
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) R::fold(st[0], x[k], r + k * step);
+            }
+            for (; r < end; r += step) R::fold(st[0], load_scalar_stream(p + (size_t)r * a.rstride), r);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) partial[threadIdx.x * V + j] = st[j];
+    __syncthreads();
+    if (ty == 0 && active) {
+        for (uint32_t t = 1; t < ty_count; ++t) {
+#pragma unroll
+            for (int j = 0; j < V; ++j) R::merge(st[j], partial[(t * a.tx + tx) * V + j]);
+        }
+        const uint64_t gid = (uint64_t)o * a.inner + col;
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            if (a.split == 1) R::store(a.dst, gid + j, st[j]);
+            else static_cast<S*>(a.partials)[(uint64_t)part * a.outputs + gid + j] = st[j];
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// finalize: merge split partials in split order
+// ------------------------------------------------------------------------------------------
+template <int OP, typename T>
+__global__ void __launch_bounds__(kBlock) reduce_finalize_kernel(void* dst, const void* partials, uint64_t outputs,
+                                                                 uint32_t split) {
+    using R = Reducer<OP, T>;
+    using S = typename R::State;
+    const S* ps = static_cast<const S*>(partials);
+    for (uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < outputs;
+         gid += (uint64_t)gridDim.x * blockDim.x) {
+        S s = ps[gid];
+        for (uint32_t k = 1; k < split; ++k) R::merge(s, ps[(uint64_t)k * outputs + gid]);
+        R::store(dst, gid, s);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// generic: one thread per output, the reference CPU loop (Matrix.mm:15193-15205)
+// ------------------------------------------------------------------------------------------
+struct GenericArgs {
+    void* dst;
+    const void* src;
+    uint64_t outputs;
+    uint32_t len;
+    uint32_t rstride;
+    uint32_t cdims;
+    uint32_t s_out[MTXC_MAX_DIMS];
+    uint32_t s_in[MTXC_MAX_DIMS];
+};
+
+template <int OP, typename T>
+__global__ void __launch_bounds__(kBlock) reduce_generic_kernel(const GenericArgs a) {
+    using R = Reducer<OP, T>;
+    const T* __restrict__ src = static_cast<const T*>(a.src);
+    for (uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < a.outputs;
+         gid += (uint64_t)gridDim.x * blockDim.x) {
+        uint64_t off = 0, rem = gid;
+        for (uint32_t i = 0; i < a.cdims; ++i) {
+            off += (rem / a.s_out[i]) * a.s_in[i];
+            rem %= a.s_out[i];
+        }
+        typename R::State s = R::init();
+        const T* p = src + off;
+        for (uint32_t i = 0; i < a.len; ++i) R::fold(s, p[(uint64_t)i * a.rstride], i);
+        R::store(a.dst, gid, s);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// host planning
+// ------------------------------------------------------------------------------------------
+int blocks_per_sm(const void* kernel) {
+    static std::mutex mu;
+    static std::map<const void*, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(kernel);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kBlock, 0) != cudaSuccess || n < 1) n = 1;
+    cache[kernel] = n;
+    return n;
+}
+
+// Picks the split count in [1, max_split] whose CTA count fills whole waves best, preferring
+// at least one full wave and then fewer splits.
+uint32_t choose_split(uint64_t base_units, uint64_t units_per_wave, uint32_t max_split) {
+    if (base_units >= units_per_wave || max_split <= 1) return 1;
+    uint32_t best = 1;
+    double best_score = -1.0;
+    for (uint32_t s = 1; s <= max_split; ++s) {
+        const uint64_t units = base_units * s;
+        const uint64_t waves = (units + units_per_wave - 1) / units_per_wave;
+        double eff = (double)units / (double)(waves * units_per_wave);
+        if (units < units_per_wave) eff *= 0.5;  // under one wave: idle SMs
+        if (eff > best_score + 1e-9) {
+            best_score = eff;
+            best = s;
+        }
+        if (units >= 4 * units_per_wave) break;
+    }
+    return best;
+}
+
+enum class Plan { kRows, kCols, kGeneric };
+
+struct ReducePlan {
+    Plan kind = Plan::kGeneric;
+    int group = 32;       // rows: threads per unit
+    int vec = 1;          // cols: elements per thread
+    uint32_t split = 1;
+    uint32_t seg = 0;
+    uint32_t tx = 32;
+    uint64_t outputs = 0;
+    size_t partial_bytes = 0;
+};
+
+struct Meta {
+    uint32_t cdims;
+    uint32_t shape[MTXC_MAX_DIMS];
+    uint32_t s_out[MTXC_MAX_DIMS];
+    uint32_t s_in[MTXC_MAX_DIMS];
+};
+
+template <int OP, typename T>
+ReducePlan plan_reduce(const Meta& m, const void* src, uint32_t rstride, uint32_t len, size_t workspace_bytes,
+                       int sm_count) {
+    using S = typename Reducer<OP, T>::State;
+    constexpr uint32_t V = Vec16<T>::N;
+    ReducePlan p;
+    p.outputs = product(m.shape, m.cdims);
+    if (p.outputs == 0 || len == 0 || p.outputs >= (1ull << 32) || !is_row_major(m.shape, m.s_out, m.cdims))
+        return p;
+    const uint32_t k = m.cdims - 1;
+    const uint64_t max_partials = workspace_bytes / sizeof(S);
+    if (rstride == 1 && len >= 32) {
+        p.kind = Plan::kRows;
+        const uint64_t warp_slots = (uint64_t)sm_count * 64;
+        if (len <= 32 * V * 8 || p.outputs >= warp_slots) {
+            p.group = 32;
+            const uint32_t max_split = std::max<uint32_t>(1, len / (32 * V * kUnroll));
+            p.split = choose_split(p.outputs, warp_slots, max_split);
+        } else {
+            p.group = kBlock;
+            const void* fn = (const void*)reduce_rows_kernel<OP, T, kBlock>;
+            const uint64_t block_slots = (uint64_t)sm_count * blocks_per_sm(fn);
+            const uint32_t max_split = std::max<uint32_t>(1, len / (kBlock * V * kUnroll));
+            p.split = choose_split(p.outputs, block_slots, max_split);
+        }
+        while (p.split > 1 && p.outputs * p.split > max_partials) p.split /= 2;
+        p.seg = p.split == 1 ? len : (uint32_t)(((uint64_t)len + p.split - 1) / p.split + V - 1) / V * V;
+        if (p.split > 1) p.split = (len + p.seg - 1) / p.seg;
+        p.partial_bytes = p.split > 1 ? p.outputs * p.split * sizeof(S) : 0;
+        return p;
+    }
+    if (rstride != 1 && m.s_in[k] == 1 && m.shape[k] >= 2) {
+        p.kind = Plan::kCols;
+        const uint32_t inner = m.shape[k];
+        bool vec_ok = aligned16(src) && inner % V == 0 && rstride % V == 0;
+        for (uint32_t i = 0; i < k; ++i) vec_ok = vec_ok && (m.shape[i] == 1 || m.s_in[i] % V == 0);
+        p.vec = vec_ok ? (int)V : 1;
+        const uint32_t threads_across = (inner + p.vec - 1) / p.vec;
+        uint32_t tx = 1;
+        while (tx < threads_across && tx < 32) tx <<= 1;
+        p.tx = tx;
+        const uint64_t col_tiles = (threads_across + tx - 1) / tx;
+        const uint64_t base = col_tiles * (p.outputs / inner);
+        // the split is planned with the vector kernel's occupancy whatever the alignment, so
+        // the workspace a call needs does not depend on its pointers
+        const void* fn = (const void*)reduce_cols_kernel<OP, T, V>;
+        const uint64_t block_slots = (uint64_t)sm_count * blocks_per_sm(fn);
+        const uint32_t ty_count = kBlock / tx;
+        const uint32_t max_split = std::max<uint32_t>(1, len / (ty_count * 8));
+        p.split = choose_split(base, block_slots, max_split);
+        while (p.split > 1 && p.outputs * p.split > max_partials) p.split /= 2;
+        p.seg = (len + p.split - 1) / p.split;
+        p.split = (len + p.seg - 1) / p.seg;
+        p.partial_bytes = p.split > 1 ? p.outputs * p.split * sizeof(S) : 0;
+        return p;
+    }
+    return p;
+}
+
+template <int OP, typename T>
+int launch_reduce(const Meta& m, void* dst, const void* src, uint32_t rstride, uint32_t len, void* workspace,
+                  size_t workspace_bytes, int sm_count, cudaStream_t stream) {
+    const ReducePlan p = plan_reduce<OP, T>(m, src, rstride, len, workspace_bytes, sm_count);
+    if (p.outputs == 0) return MTXC_OK;
+    if (p.partial_bytes > workspace_bytes)
+        return fail(MTXC_ERR_WORKSPACE, "mtxc_reduce: workspace too small for the split partials");
+    constexpr int V = Vec16<T>::N;
+    const uint32_t k = m.cdims - 1;
+    if (p.kind == Plan::kRows) {
+        RowArgs a{};
+        a.dst = dst;
+        a.src = src;
+        a.partials = workspace;
+        a.len = len;
+        a.seg = p.seg;
+        a.split = p.split;
+        a.rows = (uint32_t)p.outputs;
+        a.d.n = m.cdims;
+        for (uint32_t i = 0; i < m.cdims; ++i) {
+            a.d.shape[i] = m.shape[i];
+            a.d.s1[i] = m.s_in[i];
+            a.d.fdiv[i] = FastDiv(m.shape[i]);
+        }
+        const uint64_t units = p.outputs * p.split;
+        const uint64_t upb = kBlock / p.group;
+        uint64_t blocks = (units + upb - 1) / upb;
+        blocks = std::min<uint64_t>(blocks, (uint64_t)sm_count * 64);
+        if (p.group == 32) reduce_rows_kernel<OP, T, 32><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        else reduce_rows_kernel<OP, T, kBlock><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        if (int rc = check_launch("reduce_rows_kernel")) return rc;
+    } else if (p.kind == Plan::kCols) {
+        ColArgs a{};
+        a.dst = dst;
+        a.src = src;
+        a.partials = workspace;
+        a.len = len;
+        a.rstride = rstride;
+        a.seg = p.seg;
+        a.split = p.split;
+        a.inner = m.shape[k];
+        a.outer = (uint32_t)(p.outputs / m.shape[k]);
+        a.tx = p.tx;
+        a.col_tiles = (((a.inner + p.vec - 1) / p.vec) + p.tx - 1) / p.tx;
+        a.outputs = p.outputs;
+        a.d.n = k;
+        for (uint32_t i = 0; i < k; ++i) {
+            a.d.shape[i] = m.shape[i];
+            a.d.s1[i] = m.s_in[i];
+            a.d.fdiv[i] = FastDiv(m.shape[i]);
+        }
+        const uint64_t blocks = (uint64_t)a.col_tiles * a.outer * p.split;
+        if (blocks >= (1ull << 31)) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: too many column tiles");
+        if (p.vec > 1) reduce_cols_kernel<OP, T, V><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        else reduce_cols_kernel<OP, T, 1><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        if (int rc = check_launch("reduce_cols_kernel")) return rc;
+    } else {
+        GenericArgs a{};
+        a.dst = dst;
+        a.src = src;
+        a.outputs = p.outputs;
+        a.len = len;
+        a.rstride = rstride;
+        a.cdims = m.cdims;
+        for (uint32_t i = 0; i < m.cdims; ++i) {
+            a.s_out[i] = m.s_out[i];
+            a.s_in[i] = m.s_in[i];
+        }
+        const uint64_t blocks = std::min<uint64_t>((p.outputs + kBlock - 1) / kBlock, (uint64_t)sm_count * 32);
+        reduce_generic_kernel<OP, T><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        return check_launch("reduce_generic_kernel");
+    }
+    if (p.split > 1) {
+        const uint64_t blocks = std::min<uint64_t>((p.outputs + kBlock - 1) / kBlock, (uint64_t)sm_count * 32);
+        reduce_finalize_kernel<OP, T><<<(unsigned)blocks, kBlock, 0, stream>>>(dst, workspace, p.outputs, p.split);
+        if (int rc = check_launch("reduce_finalize_kernel")) return rc;
+    }
+    return MTXC_OK;
+}
+
+template <typename T>
+int launch_reduce_op(int op, const Meta& m, void* dst, const void* src, uint32_t rstride, uint32_t len, void* ws,
+                     size_t wsb, int sms, cudaStream_t st) {
+    switch (op) {
+        case MTXC_REDUCE_SUM: return launch_reduce<MTXC_REDUCE_SUM, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case MTXC_REDUCE_MAX: return launch_reduce<MTXC_REDUCE_MAX, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case MTXC_REDUCE_MIN: return launch_reduce<MTXC_REDUCE_MIN, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case MTXC_REDUCE_ARGMAX: return launch_reduce<MTXC_REDUCE_ARGMAX, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case MTXC_REDUCE_ARGMIN: return launch_reduce<MTXC_REDUCE_ARGMIN, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        default: return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: unknown op");
+    }
+}
+
+template <typename T>
+size_t partial_bytes_op(int op, const Meta& m, const void* src, uint32_t rstride, uint32_t len, int sms) {
+    const size_t unlimited = ~size_t(0) / 2;
+    switch (op) {
+        case MTXC_REDUCE_SUM: return plan_reduce<MTXC_REDUCE_SUM, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+        case MTXC_REDUCE_MAX: return plan_reduce<MTXC_REDUCE_MAX, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+        case MTXC_REDUCE_MIN: return plan_reduce<MTXC_REDUCE_MIN, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+        case MTXC_REDUCE_ARGMAX: return plan_reduce<MTXC_REDUCE_ARGMAX, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+        default: return plan_reduce<MTXC_REDUCE_ARGMIN, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+    }
+}
+
+int make_meta(uint32_t cdims, const uint32_t* shape, const uint32_t* s_out, const uint32_t* s_in, Meta& m) {
+    if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: cdims > MTXC_MAX_DIMS");
+    if (cdims == 0) {
+        // the reference's single-output case (Matrix.mm:15121-15126)
+        m.cdims = 1;
+        m.shape[0] = 1;
+        m.s_out[0] = 1;
+        m.s_in[0] = 1;
+        return MTXC_OK;
+    }
+    if (!shape || !s_out || !s_in) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: null metadata pointer");
+    m.cdims = cdims;
+    for (uint32_t i = 0; i < cdims; ++i) {
+        if (s_out[i] == 0 && shape[i] > 1)
+            return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: zero output stride");
+        m.shape[i] = shape[i];
+        m.s_out[i] = s_out[i] ? s_out[i] : 1;
+        m.s_in[i] = s_in[i];
+    }
+    return MTXC_OK;
+}
+
+}  // namespace
+}  // namespace mtxc
+
+using namespace mtxc;
+
+extern "C" int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
+                           uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides,
+                           const uint32_t* src_strides) {
+    if (int rc = require_init()) return rc;
+    if (op < MTXC_REDUCE_SUM || op > MTXC_REDUCE_ARGMIN) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: unknown op");
+    Meta m;
+    if (int rc = make_meta(cdims, shape, dst_strides, src_strides, m)) return rc;
+    if (product(m.shape, m.cdims) == 0) return MTXC_OK;
+    if (!dst || (!src && reduce_len)) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: null buffer");
+    ThreadCtx& c = ctx();
+    int rc = MTXC_OK;
+    const bool known = dispatch_dtype(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        rc = launch_reduce_op<T>(op, m, dst, src, reduce_stride, reduce_len, c.workspace, c.workspace_bytes, c.sm_count,
+                                 c.stream());
+    });
+    if (!known)
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_reduce: no kernel for dtype ") + dtype_name(dtype));
+    return rc;
+}
+
+extern "C" int mtxc_reduce_workspace_bytes(int op, int dtype, uint32_t reduce_stride, uint32_t reduce_len,
+                                           uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides,
+                                           const uint32_t* src_strides, size_t* bytes) {
+    if (!bytes) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_workspace_bytes: null pointer");
+    if (op < MTXC_REDUCE_SUM || op > MTXC_REDUCE_ARGMIN)
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_workspace_bytes: unknown op");
+    Meta m;
+    if (int rc = make_meta(cdims, shape, dst_strides, src_strides, m)) return rc;
+    const int sms = ctx().device >= 0 ? ctx().sm_count : 148;
+    size_t b = 0;
+    const bool known = dispatch_dtype(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        // alignment only affects the column kernel's vector width, not the partial count
+        b = partial_bytes_op<T>(op, m, nullptr, reduce_stride, reduce_len, sms);
+    });
+    if (!known) return fail(MTXC_ERR_UNSUPPORTED_DTYPE, "mtxc_reduce_workspace_bytes: unsupported dtype");
+    *bytes = b;
+    return MTXC_OK;
+}

@@ -1,0 +1,145 @@
+// Elementwise unary ops for sm_100a: exp (ExpPrimitive, primitives.cpp:5332-5463).
+//
+// Replaces ComputeShaders/exp.metal behind matrix::exp(output, dev) (Matrix.mm:6949-7011).
+// The metadata is the primitive's collapse_dims(shape, output strides, input strides); the
+// element position is decoded from the collapsed shape, innermost axis fastest, as the CPU
+// branch does (Matrix.mm:7014-7063).  exp is CUDA's expf (full-range, <= 2 ulp), so results
+// agree with the CPU's std::exp within a few ulp rather than bit for bit.
+#include <algorithm>
+
+#include "mtxc_internal.cuh"
+
+namespace mtxc {
+namespace {
+
+constexpr int kBlock = 256;
+
+struct UnaryRows {
+    float* dst;
+    const float* src;
+    uint32_t rows;
+    uint32_t vec_per_row;
+    uint32_t tpr;
+    Dims d;  // outer axes: shape (fast divisors), dst strides in s0, src strides in s1
+};
+
+__global__ void __launch_bounds__(kBlock) exp_rows_kernel(const UnaryRows a) {
+    const uint32_t rows_per_block = kBlock / a.tpr;
+    const uint32_t sub = threadIdx.x / a.tpr;
+    const uint32_t lane = threadIdx.x % a.tpr;
+    for (uint64_t row = (uint64_t)blockIdx.x * rows_per_block + sub; row < a.rows;
+         row += (uint64_t)gridDim.x * rows_per_block) {
+        uint64_t od = 0, os = 0;
+        uint32_t rem = (uint32_t)row;
+#pragma unroll 1
+        for (int i = (int)a.d.n - 1; i >= 0; --i) {
+            uint32_t q, idx;
+            a.d.fdiv[i].divmod(rem, q, idx);
+            od += (uint64_t)idx * a.d.s0[i];
+            os += (uint64_t)idx * a.d.s1[i];
+            rem = q;
+        }
+        const float* ps = a.src + os;
+        float* pd = a.dst + od;
+#pragma unroll 4
+        for (uint32_t c = lane; c < a.vec_per_row; c += a.tpr) {
+            Vec16<float> x = load_stream(ps + (uint64_t)c * 4);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) x.v[j] = expf(x.v[j]);
+            store_stream(pd + (uint64_t)c * 4, x);
+        }
+    }
+}
+
+struct UnaryGeneric {
+    float* dst;
+    const float* src;
+    uint64_t total;
+    uint32_t cdims;
+    uint32_t shape[MTXC_MAX_DIMS];
+    uint32_t sd[MTXC_MAX_DIMS];
+    uint32_t ss[MTXC_MAX_DIMS];
+};
+
+__global__ void __launch_bounds__(kBlock) exp_generic_kernel(const UnaryGeneric g) {
+    for (uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < g.total;
+         gid += (uint64_t)gridDim.x * blockDim.x) {
+        uint64_t od = 0, os = 0, rem = gid;
+        for (int i = (int)g.cdims - 1; i >= 0; --i) {
+            const uint64_t idx = rem % g.shape[i];
+            od += idx * g.sd[i];
+            os += idx * g.ss[i];
+            rem /= g.shape[i];
+        }
+        g.dst[od] = expf(g.src[os]);
+    }
+}
+
+int launch_exp(float* dst, const float* src, uint32_t cdims, const uint32_t* shape, const uint32_t* sd,
+               const uint32_t* ss, int sm_count, cudaStream_t stream) {
+    uint32_t one = 1;
+    if (cdims == 0) {
+        cdims = 1;
+        shape = sd = ss = &one;
+    }
+    const uint64_t total = product(shape, cdims);
+    if (total == 0) return MTXC_OK;
+    const uint32_t k = cdims - 1;
+    bool rows_ok = sd[k] == 1 && ss[k] == 1 && shape[k] % 4 == 0 && aligned16(dst) && aligned16(src) &&
+                   total / shape[k] < (1ull << 32);
+    for (uint32_t i = 0; i < k && rows_ok; ++i) rows_ok = shape[i] == 1 || (sd[i] % 4 == 0 && ss[i] % 4 == 0);
+    if (rows_ok) {
+        UnaryRows a{};
+        a.dst = dst;
+        a.src = src;
+        a.rows = (uint32_t)(total / shape[k]);
+        a.vec_per_row = shape[k] / 4;
+        uint32_t tpr = 1;
+        while (tpr < a.vec_per_row && tpr < (uint32_t)kBlock) tpr <<= 1;
+        a.tpr = tpr;
+        a.d.n = k;
+        for (uint32_t i = 0; i < k; ++i) {
+            a.d.shape[i] = shape[i];
+            a.d.s0[i] = sd[i];
+            a.d.s1[i] = ss[i];
+            a.d.fdiv[i] = FastDiv(shape[i]);
+        }
+        const uint32_t rpb = kBlock / tpr;
+        const uint64_t blocks = std::min<uint64_t>((a.rows + rpb - 1) / rpb, (uint64_t)sm_count * 8);
+        exp_rows_kernel<<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        return check_launch("exp_rows_kernel");
+    }
+    UnaryGeneric g{};
+    g.dst = dst;
+    g.src = src;
+    g.total = total;
+    g.cdims = cdims;
+    for (uint32_t i = 0; i < cdims; ++i) {
+        g.shape[i] = shape[i];
+        g.sd[i] = sd[i];
+        g.ss[i] = ss[i];
+    }
+    const uint64_t blocks = std::min<uint64_t>((total + kBlock - 1) / kBlock, (uint64_t)sm_count * 16);
+    exp_generic_kernel<<<(unsigned)blocks, kBlock, 0, stream>>>(g);
+    return check_launch("exp_generic_kernel");
+}
+
+}  // namespace
+}  // namespace mtxc
+
+using namespace mtxc;
+
+extern "C" int mtxc_unary(int op, int dtype, void* dst, const void* src, uint32_t cdims, const uint32_t* shape,
+                          const uint32_t* dst_strides, const uint32_t* src_strides) {
+    if (int rc = require_init()) return rc;
+    if (op != MTXC_UNARY_EXP) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: unknown op");
+    if (dtype != MTXC_FLOAT)
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_unary: exp has no kernel for dtype ") + dtype_name(dtype));
+    if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: cdims > MTXC_MAX_DIMS");
+    if (cdims && (!shape || !dst_strides || !src_strides))
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: null metadata pointer");
+    if (!dst || !src) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: null buffer");
+    ThreadCtx& c = ctx();
+    return launch_exp(static_cast<float*>(dst), static_cast<const float*>(src), cdims, shape, dst_strides, src_strides,
+                      c.sm_count, c.stream());
+}

@@ -1,0 +1,243 @@
+"""Python access to the CPU oracle (test infrastructure only).
+
+Two interchangeable evaluators with the same interface:
+
+* ``port()``      oracle/liboracle.so, the restatement in oracle/oracle.cpp;
+* ``reference()`` oracle/_ref/libmtx_ref.so, the reference's own CPU loops and shape helpers
+                  compiled by oracle/build_ref.py (None when it was not built).
+
+The frontends here mirror the reference's graph-building methods (output shape, contiguous
+output strides, collapse metadata) so a test states an op the way the reference's user would:
+``ev.reduce("sum", x, axis=-1)`` is ``x.sum(-1)`` evaluated with ``eval_cpu()``.
+Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline leg import this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+PORT_LIB = HERE / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libmtx_ref.so"
+
+MAX_DIMS = 8
+UINT32_MAX = 0xFFFFFFFF
+INT32_MAX = 0x7FFFFFFF
+
+# dtype codes, matrix.h:35-51
+DTYPES = {
+    np.dtype(np.float32): 0, np.dtype(np.uint8): 2, np.dtype(np.int32): 3, np.dtype(np.int16): 4,
+    np.dtype(np.uint32): 5, np.dtype(np.uint16): 6, np.dtype(np.int8): 8, np.dtype(np.int64): 11,
+    np.dtype(np.uint64): 12, np.dtype(np.float16): 1,
+}
+REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
+BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5}
+
+U32P = C.POINTER(C.c_uint32)
+
+
+def _arr(vals, n=MAX_DIMS):
+    a = (C.c_uint32 * n)()
+    for i, v in enumerate(vals):
+        a[i] = int(v) & 0xFFFFFFFF
+    return a
+
+
+def row_major(shape):
+    strides, acc = [0] * len(shape), 1
+    for i in range(len(shape) - 1, -1, -1):
+        strides[i] = acc & 0xFFFFFFFF  # size_m arithmetic
+        acc *= int(shape[i])
+    return strides
+
+
+def elem_strides(x: np.ndarray):
+    return [s // x.itemsize for s in x.strides]
+
+
+class CpuEval:
+    """ctypes wrapper over one of the two oracle libraries."""
+
+    def __init__(self, path: Path, prefix: str, threaded: bool):
+        self.path = path
+        self.prefix = prefix
+        self.threaded = threaded
+        self.lib = C.CDLL(str(path))
+        self.threads = int(os.environ.get("ORACLE_THREADS", "1"))
+        L = self.lib
+        u32, u64, i32 = C.c_uint32, C.c_uint64, C.c_int
+        vp = C.c_void_p
+        self._f = {}
+
+        def fn(name, res, args):
+            f = getattr(L, prefix + name)
+            f.restype, f.argtypes = res, args
+            self._f[name] = f
+
+        fn("collapse1", u32, [U32P, U32P, u32, u64, U32P, U32P])
+        fn("collapse2", u32, [U32P, U32P, U32P, u32, u64, U32P, U32P, U32P])
+        fn("collapse3", u32, [U32P, U32P, U32P, U32P, u32, u64, U32P, U32P, U32P, U32P])
+        fn("collapse_reduce1", u32, [U32P, U32P, u32, i32, i32, u64, U32P, U32P])
+        fn("collapse_reduce2", u32, [U32P, U32P, U32P, u32, i32, i32, i32, u64, U32P, U32P, U32P])
+        fn("collapse_reduce3", u32, [U32P, U32P, U32P, U32P, u32, i32, i32, u64, U32P, U32P, U32P, U32P])
+        fn("broadcast_shapes", i32, [U32P, U32P, i32, U32P, U32P, i32, U32P, U32P, U32P, U32P, U32P, U32P])
+        fn("promote", i32, [i32, i32])
+        extra = [i32] if threaded else []
+        fn("reduce", i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P, u64] + extra)
+        fn("broadcast", i32, [i32, i32, vp, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
+        fn("exp", i32, [i32, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
+
+    # -- shape folding ---------------------------------------------------------------------
+    def collapse(self, shape, *strides, cap=INT32_MAX):
+        n = len(strides)
+        o = [_arr([]) for _ in range(n + 1)]
+        args = [_arr(shape)] + [_arr(s) for s in strides] + [len(shape), cap] + o
+        k = self._f[f"collapse{n}"](*args)
+        return k, [list(a[:k]) for a in o]
+
+    def collapse_reduce(self, shape, *strides, axis, keep=False, outer=None, cap=UINT32_MAX):
+        n = len(strides)
+        o = [_arr([]) for _ in range(n + 1)]
+        args = [_arr(shape)] + [_arr(s) for s in strides] + [len(shape), axis, int(keep)]
+        if n == 2:
+            args.append(int(bool(outer)))
+        args += [cap] + o
+        k = self._f[f"collapse_reduce{n}"](*args)
+        return k, [list(a[:k]) for a in o]
+
+    def broadcast_shapes(self, shape1, strides1, shape2, strides2):
+        od = max(len(shape1), len(shape2))
+        outs = [_arr([]) for _ in range(6)]
+        rc = self._f["broadcast_shapes"](_arr(shape1), _arr(strides1), len(shape1), _arr(shape2), _arr(strides2),
+                                         len(shape2), *outs)
+        if rc != 0:
+            raise ValueError("Incompatible shapes for broadcasting")
+        return [list(a[:od]) for a in outs]  # out_shape, out_strides, a_shape, a_strides, b_shape, b_strides
+
+    def promote(self, a, b):
+        return self._f["promote"](a, b)
+
+    # -- frontends (the reference's graph-building metadata) -------------------------------
+    def reduce_meta(self, shape, strides, axis, keepdims=False):
+        """matrix::sum/max/... (Matrix.mm:15071-15097): output shape, row-major output strides,
+        collapse_dims_reduce(shape, out.strides, in.strides, dims, axis, false, !keepdims, UINT32_MAX)."""
+        dims = len(shape)
+        if axis < 0:
+            axis += dims
+        if keepdims:
+            out_shape = list(shape)
+            out_shape[axis] = 1
+        else:
+            out_shape = list(shape[:axis]) + list(shape[axis + 1:])
+        out_strides = row_major(out_shape)
+        so = out_strides + [0] * (dims - len(out_strides))
+        k, (cshape, s_out, s_in) = self.collapse_reduce(shape, so, strides, axis=axis, keep=False,
+                                                        outer=not keepdims, cap=UINT32_MAX)
+        return dict(out_shape=out_shape, cdims=k, shape=cshape, s_out=s_out, s_in=s_in,
+                    rstride=int(strides[axis]), rlen=int(shape[axis]))
+
+    def binary_meta(self, shape_a, strides_a, shape_b, strides_b):
+        """operator+ & co. (Matrix.mm:8312-8331): broadcast_shapes, then collapse_dims over
+        (desc_a.shape, desc_a.strides, desc_b.strides, result.strides) with cap INT32_MAX."""
+        out_shape, out_strides, a_shape, a_strides, b_shape, b_strides = self.broadcast_shapes(
+            shape_a, strides_a, shape_b, strides_b)
+        k, (cshape, sa, sb, sr) = self.collapse(a_shape, a_strides, b_strides, out_strides, cap=INT32_MAX)
+        return dict(out_shape=out_shape, cdims=k, shape=cshape, sa=sa, sb=sb, sr=sr)
+
+    def unary_meta(self, shape, strides):
+        """matrix::exp (Matrix.mm:6934-6947): collapse_dims(shape, out.strides, in.strides)."""
+        k, (cshape, so, si) = self.collapse(shape, row_major(shape), strides, cap=INT32_MAX)
+        return dict(out_shape=list(shape), cdims=k, shape=cshape, s_out=so, s_in=si)
+
+    # -- evaluation --------------------------------------------------------------------------
+    def _thr(self):
+        return [self.threads] if self.threaded else []
+
+    def reduce_raw(self, op, x_base: np.ndarray, offset: int, meta, out_dtype=None):
+        total = int(np.prod(meta["out_shape"], dtype=np.int64)) if meta["out_shape"] else 1
+        opc = REDUCE_OPS[op]
+        odt = np.int32 if opc >= 3 else x_base.dtype
+        out = np.empty(max(total, 1), dtype=odt)
+        ptr = x_base.ctypes.data + offset * x_base.itemsize
+        rc = self._f["reduce"](opc, DTYPES[x_base.dtype], out.ctypes.data, ptr, meta["rstride"] & 0xFFFFFFFF,
+                               meta["rlen"], meta["cdims"], _arr(meta["shape"]), _arr(meta["s_out"]),
+                               _arr(meta["s_in"]), total, *self._thr())
+        if rc != 0:
+            raise RuntimeError(f"{self.prefix}reduce failed")
+        return out[:total].reshape(meta["out_shape"])
+
+    def reduce(self, op, x: np.ndarray, axis: int, keepdims=False):
+        """x.op(axis, keepdims).eval_cpu() for a (possibly strided) numpy view x."""
+        base, offset = _base_and_offset(x)
+        meta = self.reduce_meta(list(x.shape), elem_strides(x), axis, keepdims)
+        return self.reduce_raw(op, base, offset, meta)
+
+    def binary_raw(self, op, a_base, a_off, b_base, b_off, meta):
+        total = int(np.prod(meta["out_shape"], dtype=np.int64)) if meta["out_shape"] else 1
+        out = np.empty(max(total, 1), dtype=a_base.dtype)
+        rc = self._f["broadcast"](BINARY_OPS[op], DTYPES[a_base.dtype], out.ctypes.data,
+                                  a_base.ctypes.data + a_off * a_base.itemsize,
+                                  b_base.ctypes.data + b_off * b_base.itemsize, meta["cdims"], _arr(meta["sr"]),
+                                  _arr(meta["sa"]), _arr(meta["sb"]), total, *self._thr())
+        if rc != 0:
+            raise RuntimeError(f"{self.prefix}broadcast failed")
+        return out[:total].reshape(meta["out_shape"])
+
+    def binary(self, op, a: np.ndarray, b: np.ndarray):
+        """(a op b).eval_cpu() with both operands already of the same dtype."""
+        assert a.dtype == b.dtype
+        ab, ao = _base_and_offset(a)
+        bb, bo = _base_and_offset(b)
+        meta = self.binary_meta(list(a.shape), elem_strides(a), list(b.shape), elem_strides(b))
+        return self.binary_raw(op, ab, ao, bb, bo, meta)
+
+    def exp(self, x: np.ndarray):
+        base, offset = _base_and_offset(x)
+        meta = self.unary_meta(list(x.shape), elem_strides(x))
+        total = int(np.prod(x.shape, dtype=np.int64)) if x.shape else 1
+        out = np.empty(max(total, 1), dtype=np.float32)
+        rc = self._f["exp"](0, out.ctypes.data, base.ctypes.data + offset * base.itemsize, meta["cdims"],
+                            _arr(meta["shape"]), _arr(meta["s_out"]), _arr(meta["s_in"]), total, *self._thr())
+        if rc != 0:
+            raise RuntimeError(f"{self.prefix}exp failed")
+        return out[:total].reshape(x.shape)
+
+
+def _base_and_offset(x: np.ndarray):
+    """The flat base buffer of a view and the view's element offset into it."""
+    base = x
+    while isinstance(base.base, np.ndarray):
+        base = base.base
+    if not (base.flags.c_contiguous or base.flags.f_contiguous):
+        base = np.ascontiguousarray(base)
+    flat = base.reshape(-1, order="A") if base.ndim != 1 else base
+    off_bytes = x.__array_interface__["data"][0] - flat.__array_interface__["data"][0]
+    assert off_bytes % x.itemsize == 0
+    if flat.dtype != x.dtype:
+        flat = flat.view(x.dtype)
+    return flat, off_bytes // x.itemsize
+
+
+_PORT = None
+_REF = None
+
+
+def port() -> CpuEval:
+    global _PORT
+    if _PORT is None:
+        if not PORT_LIB.exists():
+            raise FileNotFoundError(f"{PORT_LIB} is missing: run `python oracle/build.py`")
+        _PORT = CpuEval(PORT_LIB, "orc_", threaded=True)
+    return _PORT
+
+
+def reference() -> CpuEval | None:
+    global _REF
+    if _REF is None:
+        if not REF_LIB.exists():
+            return None
+        _REF = CpuEval(REF_LIB, "ref_", threaded=False)
+    return _REF
