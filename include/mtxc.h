@@ -100,9 +100,11 @@ const char* mtxc_last_error(void);
 
 int mtxc_device_count(int* count);
 
-/* Makes `stream` (a cudaStream_t) the calling thread's stream; NULL restores the stream the
- * runtime created.  The caller keeps ownership. */
+/* Makes `stream` (a cudaStream_t) the calling thread's stream.  NULL is CUDA's legacy default
+ * stream, as everywhere in CUDA.  The caller keeps ownership. */
 int mtxc_set_stream(void* stream);
+/* Goes back to the stream the runtime created in mtxc_init. */
+int mtxc_use_own_stream(void);
 void* mtxc_get_stream(void);
 
 /* Waits for all work on the calling thread's stream (the reference's commitCommandBuffer,

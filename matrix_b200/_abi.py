@@ -51,6 +51,7 @@ def lib() -> C.CDLL:
             "mtxc_last_error": (C.c_char_p, []),
             "mtxc_device_count": (i32, [C.POINTER(i32)]),
             "mtxc_set_stream": (i32, [vp]),
+            "mtxc_use_own_stream": (i32, []),
             "mtxc_get_stream": (vp, []),
             "mtxc_sync": (i32, []),
             "mtxc_set_workspace": (i32, [vp, sz]),

@@ -19,13 +19,14 @@ namespace mtxc {
 struct ThreadCtx {
     int device = -1;
     cudaStream_t own_stream = nullptr;   // created by mtxc_init
-    cudaStream_t user_stream = nullptr;  // set by mtxc_set_stream
+    cudaStream_t user_stream = nullptr;  // set by mtxc_set_stream (may be the default stream, 0)
+    bool has_user_stream = false;
     void* workspace = nullptr;
     size_t workspace_bytes = 0;
     bool own_workspace = false;
     int sm_count = 148;
     std::string last_error;
-    cudaStream_t stream() const { return user_stream ? user_stream : own_stream; }
+    cudaStream_t stream() const { return has_user_stream ? user_stream : own_stream; }
 };
 
 ThreadCtx& ctx();

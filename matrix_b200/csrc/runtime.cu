@@ -113,6 +113,14 @@ const char* mtxc_last_error(void) { return ctx().last_error.c_str(); }
 int mtxc_set_stream(void* stream) {
     if (int rc = require_init()) return rc;
     ctx().user_stream = static_cast<cudaStream_t>(stream);
+    ctx().has_user_stream = true;
+    return MTXC_OK;
+}
+
+int mtxc_use_own_stream(void) {
+    if (int rc = require_init()) return rc;
+    ctx().user_stream = nullptr;
+    ctx().has_user_stream = false;
     return MTXC_OK;
 }
 

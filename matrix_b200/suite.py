@@ -1,0 +1,142 @@
+"""Device-time measurements of the other BASELINE configs (bench.py --suite).
+
+Each config is run through the same C-ABI calls a user makes (matrix_b200.backend), with
+seeded synthetic inputs generated on the device, 3 warm-up repetitions and the median of 10
+timed repetitions (CUDA events on the launching stream).  Inputs larger than L2 are streamed
+as they are; C1's 16 MiB input fits in L2, so L2 is flushed (a 512 MiB write) before each
+repetition and only the reduction is timed.
+"""
+from __future__ import annotations
+
+import json
+import statistics
+from pathlib import Path
+
+import torch
+
+from . import backend
+
+REPO = Path(__file__).resolve().parent.parent
+GiB = 1 << 30
+
+
+def _peak() -> float:
+    try:
+        return float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
+    except Exception:
+        return 6650.0
+
+
+def _time(fn, stream, reps=10, warmup=3, flush=None):
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times)
+
+
+def _line(name, workload, nbytes, ms, peak, **extra):
+    gbs = nbytes / (ms / 1e3) / 1e9
+    d = {"suite": name, "workload": workload, "algorithmic_bytes": nbytes, "ms": round(ms, 4),
+         "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4)}
+    d.update(extra)
+    return d
+
+
+def run_all(dev, stream):
+    peak = _peak()
+    g = torch.Generator(device=dev)
+    out = []
+
+    # C1: Sum over the last axis of f32 [1024, 4096] ~ N(0,1)
+    g.manual_seed(0)
+    x = torch.randn(1024, 4096, generator=g, device=dev)
+    y = torch.empty(1024, device=dev)
+    m = backend.reduce_meta([1024, 4096], [4096, 1], -1)
+    scratch = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    ms = _time(lambda: backend.reduce("sum", x, -1, out=y, meta=m), stream, flush=lambda: scratch.fill_(1))
+    out.append(_line("C1", "Sum(axis=-1) f32 [1024,4096] (L2 flushed before each rep)", 1024 * 4096 * 4 + 4096, ms,
+                     peak))
+    del x, y, scratch
+
+    # C3: Max and ArgMax along axis 1 of f32 [64, 8192, 1024], values k/256
+    g.manual_seed(2)
+    x = torch.floor(torch.rand(64, 8192, 1024, generator=g, device=dev) * 256) / 256
+    m = backend.reduce_meta([64, 8192, 1024], list(x.stride()), 1)
+    vmax = torch.empty(64, 1024, device=dev)
+    imax = torch.empty(64, 1024, dtype=torch.int32, device=dev)
+    nbytes = 64 * 8192 * 1024 * 4 + 64 * 1024 * 4
+    ms = _time(lambda: backend.reduce("max", x, 1, out=vmax, meta=m), stream)
+    out.append(_line("C3-max", "Max(axis=1) f32 [64,8192,1024]", nbytes, ms, peak))
+    ms = _time(lambda: backend.reduce("argmax", x, 1, out=imax, meta=m), stream)
+    out.append(_line("C3-argmax", "ArgMax(axis=1) f32 [64,8192,1024]", nbytes, ms, peak))
+    del x
+
+    # C4: Sum over axes (0, 2) of [32, 4096, 2048], f32 N(0,1) and i32 U{-1000..1000}
+    g.manual_seed(3)
+    for name, x in (("C4-f32", torch.randn(32, 4096, 2048, generator=g, device=dev)),
+                    ("C4-i32", torch.randint(-1000, 1001, (32, 4096, 2048), generator=g, device=dev,
+                                             dtype=torch.int32))):
+        m2 = backend.reduce_meta([32, 4096, 2048], list(x.stride()), 2)
+        mid = torch.empty(32, 4096, dtype=x.dtype, device=dev)
+        m0 = backend.reduce_meta([32, 4096], [4096, 1], 0)
+        fin = torch.empty(4096, dtype=x.dtype, device=dev)
+
+        def c4():
+            backend.reduce("sum", x, 2, out=mid, meta=m2)
+            backend.reduce("sum", mid, 0, out=fin, meta=m0)
+
+        ms = _time(c4, stream)
+        out.append(_line(name, "x.sum(2).sum(0) [32,4096,2048]", 32 * 4096 * 2048 * 4 + 4096 * 4, ms, peak,
+                         moved_bytes=32 * 4096 * 2048 * 4 + 2 * 32 * 4096 * 4 + 4096 * 4))
+        del x, mid
+
+    # C5a: softmax trace on f32 [8192, 32768] ~ N(0, 4): max, sub, exp, sum, div (5 kernels)
+    g.manual_seed(4)
+    x = torch.randn(8192, 32768, generator=g, device=dev) * 2
+    mx = torch.empty(8192, 1, device=dev)
+    t = torch.empty_like(x)
+    s = torch.empty(8192, 1, device=dev)
+    mm = backend.reduce_meta([8192, 32768], [32768, 1], -1, True)
+    msub = backend.binary_meta([8192, 32768], [32768, 1], [8192, 1], [1, 1])
+    mexp = backend.unary_meta([8192, 32768], [32768, 1])
+    mdiv = msub
+
+    def trace():
+        backend.reduce("max", x, -1, True, out=mx, meta=mm)
+        backend.binary("sub", x, mx, out=t, meta=msub)
+        backend.exp(t, out=t, meta=mexp)
+        backend.reduce("sum", t, -1, True, out=s, meta=mm)
+        backend.binary("div", t, s, out=t, meta=mdiv)
+
+    ms = _time(trace, stream)
+    n = 8192 * 32768 * 4
+    out.append(_line("C5a-trace", "softmax trace max,sub,exp,sum,div f32 [8192,32768] (5 kernels)", 2 * n, ms, peak,
+                     moved_bytes=8 * n))
+    del x, t
+
+    # C5b: full Sum of 2^32 f32 ~ N(0,1) as [8, 2^29] (16 GiB): sum(1) then sum(0)
+    g.manual_seed(5)
+    x = torch.randn(8, 1 << 29, generator=g, device=dev)
+    r1 = torch.empty(8, device=dev)
+    r0 = torch.empty((), device=dev)
+    m1 = backend.reduce_meta([8, 1 << 29], [1 << 29, 1], 1)
+    m0 = backend.reduce_meta([8], [1], 0)
+
+    def c5b():
+        backend.reduce("sum", x, 1, out=r1, meta=m1)
+        backend.reduce("sum", r1, 0, out=r0, meta=m0)
+
+    ms = _time(c5b, stream, reps=5)
+    out.append(_line("C5b", "full Sum f32 2^32 as [8,2^29] (1 GPU)", 16 * GiB, ms, peak))
+    del x
+    torch.cuda.empty_cache()
+    return out

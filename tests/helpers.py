@@ -3,9 +3,15 @@ the comparison rules.
 
 Comparison rules (stated once, used everywhere):
   * integer results, ArgMax / ArgMin indices, Max / Min values and every single elementwise
-    float op (add, sub, mul, div, max, min) must match the oracle bit for bit;
+    float op (add, sub, mul, div, max, min) must match the oracle bit for bit, with one
+    exception: all NaNs compare equal.  The sign and payload of a NaN that arithmetic creates
+    (inf - inf, 0 * inf, ...) or propagates are architecture-defined -- x86 makes 0xffc00000,
+    the reference's ARM host 0x7fc00000, NVIDIA GPUs 0x7fffffff -- so they carry no meaning;
   * float sums, whose summation order differs from the reference's sequential loop, must satisfy
-    |gpu - cpu| <= 1e-5 * sum(|x|) over the reduced run (plus 1e-30 absolute slack);
+    |gpu - cpu| <= tol with tol = 1e-5 * sum(|x|) over the reduced run (plus 1e-30).  Where the
+    reference's own sequential fp32 sum is off the exact (fp64) sum by more than tol -- long runs
+    of same-sign values -- the GPU result is accepted when it is within tol of the exact sum and
+    no further from the CPU result than the CPU result is from the exact sum (plus tol);
   * exp is CUDA's expf against the CPU's expf: at most 2 ulp apart.
 """
 from __future__ import annotations
@@ -19,7 +25,7 @@ INT_DTYPES = [np.int32, np.uint32, np.int64, np.uint64, np.int16, np.uint16, np.
 ALL_DTYPES = [np.float32] + INT_DTYPES
 
 
-def make_values(rng: np.random.Generator, n: int, dtype, kind: str = "normal") -> np.ndarray:
+def make_values(rng: np.random.Generator, n: int, dtype, kind: str = "normal", extremes: bool = True) -> np.ndarray:
     dtype = np.dtype(dtype)
     if dtype == np.float32:
         if kind == "normal":
@@ -36,8 +42,9 @@ def make_values(rng: np.random.Generator, n: int, dtype, kind: str = "normal") -
             v[pick == 2] = -np.inf
             v[pick == 3] = 0.0
             v[pick == 4] = -0.0
-            v[pick == 5] = np.finfo(np.float32).max
-            v[pick == 6] = -np.finfo(np.float32).max
+            if extremes:  # +-FLT_MAX: fp32 partial sums overflow in an order-dependent way
+                v[pick == 5] = np.finfo(np.float32).max
+                v[pick == 6] = -np.finfo(np.float32).max
             return v
         raise ValueError(kind)
     info = np.iinfo(dtype)
@@ -66,9 +73,16 @@ def device_view(dbase, shape, strides, offset: int = 0):
     return torch.as_strided(dbase, tuple(shape), tuple(strides), offset)
 
 
+def canonical_nans(a: np.ndarray) -> np.ndarray:
+    a = np.array(a, order="C", copy=True)
+    if a.dtype.kind == "f":
+        a[np.isnan(a)] = np.nan
+    return a
+
+
 def bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
-    a = np.ascontiguousarray(a)
-    b = np.ascontiguousarray(b)
+    a = canonical_nans(a)
+    b = canonical_nans(b)
     return a.shape == b.shape and a.dtype == b.dtype and a.tobytes() == b.tobytes()
 
 
@@ -76,6 +90,7 @@ def assert_bits_equal(gpu: np.ndarray, cpu: np.ndarray, what: str = "") -> None:
     assert gpu.shape == cpu.shape, f"{what}: shape {gpu.shape} != {cpu.shape}"
     assert gpu.dtype == cpu.dtype, f"{what}: dtype {gpu.dtype} != {cpu.dtype}"
     if not bits_equal(gpu, cpu):
+        gpu, cpu = canonical_nans(gpu), canonical_nans(cpu)
         g = gpu.reshape(-1).view(np.uint8).reshape(gpu.size, -1) if gpu.size else gpu
         c = cpu.reshape(-1).view(np.uint8).reshape(cpu.size, -1) if cpu.size else cpu
         bad = np.nonzero(np.any(g != c, axis=1))[0]
@@ -84,14 +99,19 @@ def assert_bits_equal(gpu: np.ndarray, cpu: np.ndarray, what: str = "") -> None:
                              f"gpu={gpu.reshape(-1)[i]!r} cpu={cpu.reshape(-1)[i]!r}")
 
 
-def assert_sum_close(gpu: np.ndarray, cpu: np.ndarray, abs_sum: np.ndarray, what: str = "") -> None:
+def assert_sum_close(gpu: np.ndarray, cpu: np.ndarray, abs_sum: np.ndarray, what: str = "",
+                     exact: np.ndarray | None = None) -> None:
     assert gpu.shape == cpu.shape, f"{what}: shape {gpu.shape} != {cpu.shape}"
     g = gpu.astype(np.float64)
     c = cpu.astype(np.float64)
-    tol = SUM_RTOL * abs_sum.astype(np.float64).reshape(g.shape) + 1e-30
+    tol = SUM_RTOL * np.asarray(abs_sum, dtype=np.float64).reshape(g.shape) + 1e-30
     both_nan = np.isnan(g) & np.isnan(c)
     same_inf = np.isinf(g) & (g == c)
-    ok = (np.abs(g - c) <= tol) | both_nan | same_inf
+    with np.errstate(invalid="ignore"):
+        ok = (np.abs(g - c) <= tol) | both_nan | same_inf
+        if exact is not None:
+            e = np.asarray(exact, dtype=np.float64).reshape(g.shape)
+            ok |= (np.abs(g - e) <= tol) & (np.abs(g - c) <= np.abs(c - e) + tol)
     if not ok.all():
         i = np.argwhere(~ok)[0]
         raise AssertionError(f"{what}: {np.count_nonzero(~ok)} outputs outside 1e-5*sum|x|; first {tuple(i)}: "
@@ -104,6 +124,6 @@ def ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     bi = b.astype(np.float32).view(np.int32).astype(np.int64)
     ai = np.where(ai < 0, -(ai & 0x7FFFFFFF), ai)
     bi = np.where(bi < 0, -(bi & 0x7FFFFFFF), bi)
-    d = np.abs(ai - bi)
-    d[np.isnan(a) & np.isnan(b)] = 0
+    d = np.atleast_1d(np.abs(ai - bi))
+    d[np.atleast_1d(np.isnan(a) & np.isnan(b))] = 0
     return d
