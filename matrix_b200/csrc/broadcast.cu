@@ -28,6 +28,7 @@ namespace mtxc {
 namespace {
 
 constexpr int kBlock = 256;
+constexpr uint32_t kSegVecs = 4096;
 
 template <int OP, typename T>
 __device__ __forceinline__ T apply(T x, T y) {
@@ -62,7 +63,9 @@ struct RowArgs {
     const void* b;
     uint32_t rows;       // number of innermost rows
     uint32_t vec_per_row;
-    uint32_t tpr;        // threads per row (power of two, <= kBlock)
+    uint32_t seg_vecs;   // 16-byte vectors per work unit (a row is cut into segments of this size)
+    uint32_t segs;       // segments per row
+    uint32_t tpr;        // threads per unit (power of two, <= kBlock)
     uint32_t a_inner;    // innermost stride of a (0 or 1)
     uint32_t b_inner;
     Dims d;              // outer axes: shape (fast divisors), a strides in s0, b strides in s1
@@ -78,9 +81,12 @@ __global__ void __launch_bounds__(kBlock) broadcast_rows_kernel(const RowArgs ar
     const T* __restrict__ pb = static_cast<const T*>(args.b);
     T* __restrict__ pr = static_cast<T*>(args.r);
     const uint64_t row_len = (uint64_t)args.vec_per_row * V;
+    const uint64_t units = (uint64_t)args.rows * args.segs;
 
-    for (uint64_t row = (uint64_t)blockIdx.x * rows_per_block + sub; row < args.rows;
-         row += (uint64_t)gridDim.x * rows_per_block) {
+    for (uint64_t u = (uint64_t)blockIdx.x * rows_per_block + sub; u < units; u += (uint64_t)gridDim.x * rows_per_block) {
+        const uint64_t row = u / args.segs;
+        const uint32_t seg = (uint32_t)(u - row * args.segs);
+        const uint32_t c_end = min(args.vec_per_row, (seg + 1) * args.seg_vecs);
         uint64_t oa = 0, ob = 0;
         uint32_t rem = (uint32_t)row;
 #pragma unroll 1
@@ -106,7 +112,7 @@ __global__ void __launch_bounds__(kBlock) broadcast_rows_kernel(const RowArgs ar
             for (int j = 0; j < V; ++j) sb.v[j] = v;
         }
 #pragma unroll 4
-        for (uint32_t c = lane; c < args.vec_per_row; c += args.tpr) {
+        for (uint32_t c = seg * args.seg_vecs + lane; c < c_end; c += args.tpr) {
             const Vec16<T> xa = args.a_inner ? load_cached(ra + (uint64_t)c * V) : sa;
             const Vec16<T> xb = args.b_inner ? load_cached(rb + (uint64_t)c * V) : sb;
             Vec16<T> out;
@@ -178,10 +184,13 @@ int launch_broadcast(void* r, const void* a, const void* b, uint32_t cdims, cons
     const uint64_t total = product(shape, cdims);
     if (total == 0) return MTXC_OK;
     const uint32_t k = cdims - 1;
+    // An operand read with 16-byte vectors (inner stride 1) needs aligned row starts; one that
+    // is broadcast along the row (inner stride 0) is read as a single element per row.
     bool rows_ok = is_row_major(shape, sr, cdims) && sr[k] == 1 && (sa[k] <= 1) && (sb[k] <= 1) &&
-                   shape[k] % V == 0 && aligned16(r) && aligned16(a) && aligned16(b) && total / shape[k] < (1ull << 32);
+                   shape[k] % V == 0 && aligned16(r) && (sa[k] == 0 || aligned16(a)) &&
+                   (sb[k] == 0 || aligned16(b)) && total / shape[k] < (1ull << 32);
     for (uint32_t i = 0; i < k && rows_ok; ++i)
-        rows_ok = shape[i] == 1 || (sa[i] % V == 0 && sb[i] % V == 0);
+        rows_ok = shape[i] == 1 || ((sa[k] == 0 || sa[i] % V == 0) && (sb[k] == 0 || sb[i] % V == 0));
     if (rows_ok) {
         RowArgs args{};
         args.r = r;
@@ -189,8 +198,11 @@ int launch_broadcast(void* r, const void* a, const void* b, uint32_t cdims, cons
         args.b = b;
         args.rows = (uint32_t)(total / shape[k]);
         args.vec_per_row = shape[k] / V;
+        // long rows are cut into segments of kSegVecs vectors so the grid has work for every SM
+        args.seg_vecs = std::min<uint32_t>(args.vec_per_row, kSegVecs);
+        args.segs = (args.vec_per_row + args.seg_vecs - 1) / args.seg_vecs;
         uint32_t tpr = 1;
-        while (tpr < args.vec_per_row && tpr < (uint32_t)kBlock) tpr <<= 1;
+        while (tpr < args.seg_vecs && tpr < (uint32_t)kBlock) tpr <<= 1;
         args.tpr = tpr;
         args.a_inner = sa[k];
         args.b_inner = sb[k];
@@ -202,7 +214,8 @@ int launch_broadcast(void* r, const void* a, const void* b, uint32_t cdims, cons
             args.d.fdiv[i] = FastDiv(shape[i]);
         }
         const uint32_t rows_per_block = kBlock / tpr;
-        uint64_t blocks = (args.rows + rows_per_block - 1) / rows_per_block;
+        const uint64_t units = (uint64_t)args.rows * args.segs;
+        uint64_t blocks = (units + rows_per_block - 1) / rows_per_block;
         blocks = std::min<uint64_t>(blocks, (uint64_t)sm_count * 8);
         broadcast_rows_kernel<OP, T><<<(unsigned)blocks, kBlock, 0, stream>>>(args);
         return check_launch("broadcast_rows_kernel");

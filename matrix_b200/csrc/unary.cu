@@ -13,12 +13,15 @@ namespace mtxc {
 namespace {
 
 constexpr int kBlock = 256;
+constexpr uint32_t kSegVecs = 4096;
 
 struct UnaryRows {
     float* dst;
     const float* src;
     uint32_t rows;
     uint32_t vec_per_row;
+    uint32_t seg_vecs;  // vectors per work unit (rows are cut into segments of this size)
+    uint32_t segs;      // segments per row
     uint32_t tpr;
     Dims d;  // outer axes: shape (fast divisors), dst strides in s0, src strides in s1
 };
@@ -27,8 +30,11 @@ __global__ void __launch_bounds__(kBlock) exp_rows_kernel(const UnaryRows a) {
     const uint32_t rows_per_block = kBlock / a.tpr;
     const uint32_t sub = threadIdx.x / a.tpr;
     const uint32_t lane = threadIdx.x % a.tpr;
-    for (uint64_t row = (uint64_t)blockIdx.x * rows_per_block + sub; row < a.rows;
-         row += (uint64_t)gridDim.x * rows_per_block) {
+    const uint64_t units = (uint64_t)a.rows * a.segs;
+    for (uint64_t u = (uint64_t)blockIdx.x * rows_per_block + sub; u < units; u += (uint64_t)gridDim.x * rows_per_block) {
+        const uint64_t row = u / a.segs;
+        const uint32_t seg = (uint32_t)(u - row * a.segs);
+        const uint32_t c_end = min(a.vec_per_row, (seg + 1) * a.seg_vecs);
         uint64_t od = 0, os = 0;
         uint32_t rem = (uint32_t)row;
 #pragma unroll 1
@@ -42,7 +48,7 @@ __global__ void __launch_bounds__(kBlock) exp_rows_kernel(const UnaryRows a) {
         const float* ps = a.src + os;
         float* pd = a.dst + od;
 #pragma unroll 4
-        for (uint32_t c = lane; c < a.vec_per_row; c += a.tpr) {
+        for (uint32_t c = seg * a.seg_vecs + lane; c < c_end; c += a.tpr) {
             Vec16<float> x = load_stream(ps + (uint64_t)c * 4);
 #pragma unroll
             for (int j = 0; j < 4; ++j) x.v[j] = expf(x.v[j]);
@@ -94,8 +100,10 @@ int launch_exp(float* dst, const float* src, uint32_t cdims, const uint32_t* sha
         a.src = src;
         a.rows = (uint32_t)(total / shape[k]);
         a.vec_per_row = shape[k] / 4;
+        a.seg_vecs = std::min<uint32_t>(a.vec_per_row, kSegVecs);
+        a.segs = (a.vec_per_row + a.seg_vecs - 1) / a.seg_vecs;
         uint32_t tpr = 1;
-        while (tpr < a.vec_per_row && tpr < (uint32_t)kBlock) tpr <<= 1;
+        while (tpr < a.seg_vecs && tpr < (uint32_t)kBlock) tpr <<= 1;
         a.tpr = tpr;
         a.d.n = k;
         for (uint32_t i = 0; i < k; ++i) {
@@ -105,7 +113,8 @@ int launch_exp(float* dst, const float* src, uint32_t cdims, const uint32_t* sha
             a.d.fdiv[i] = FastDiv(shape[i]);
         }
         const uint32_t rpb = kBlock / tpr;
-        const uint64_t blocks = std::min<uint64_t>((a.rows + rpb - 1) / rpb, (uint64_t)sm_count * 8);
+        const uint64_t units = (uint64_t)a.rows * a.segs;
+        const uint64_t blocks = std::min<uint64_t>((units + rpb - 1) / rpb, (uint64_t)sm_count * 8);
         exp_rows_kernel<<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         return check_launch("exp_rows_kernel");
     }

@@ -182,3 +182,21 @@ def test_softmax_trace_matches_oracle(gpu, port):
     y = yd.cpu().numpy()
     np.testing.assert_allclose(y, y_cpu, rtol=1e-5, atol=0)
     assert_bits_equal(md.cpu().numpy(), m, "softmax max")
+
+
+def test_long_rows_are_segmented(gpu, port):
+    """Fully collapsed contiguous operands form one long row, which the row kernels cut into
+    segments; a column operand (inner stride 0) keeps the vector path."""
+    rng = np.random.default_rng(8)
+    n = 3 * (1 << 20) + 4 * 37  # several segments plus a partial one
+    a = make_values(rng, n, np.float32, "uniform")
+    b = make_values(rng, n, np.float32, "uniform")
+    for op in ("add", "div"):
+        check_binary(gpu, port, op, a, [n], [1], 0, b, [n], [1], 0, "one long row")
+    col = make_values(rng, 96, np.float32, "uniform")
+    big = make_values(rng, 96 * 70000, np.float32, "uniform")
+    for op in ("sub", "div"):
+        check_binary(gpu, port, op, big, [96, 70000], [70000, 1], 0, col, [96, 1], [1, 1], 0, "column operand")
+        check_binary(gpu, port, op, col, [95, 1], [1, 1], 1, big, [95, 70000], [70000, 1], 0, "column first")
+    check_exp(gpu, port, a, [n], [1], 0, "one long row")
+    check_exp(gpu, port, big, [96, 70000], [70000, 1], 0, "rows")
