@@ -193,6 +193,32 @@ int mtxc_promote_types(int a, int b);
 int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
                 uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides, const uint32_t* src_strides);
 
+/* mtxc_reduce for callers that cannot allocate device memory.  No counterpart in the reference.
+ *
+ * Some callers of this library may not call cudaMalloc: code that runs inside another framework's
+ * memory manager (which owns every byte of device memory and forbids side allocations), latency-
+ * critical loops that cannot afford the device-wide synchronisation cudaMalloc / cudaFree imply, or
+ * deployments whose memory budget is fixed up front.  mtxc_reduce needs scratch memory when it splits a
+ * reduced axis across CTAs (the per-split partials), and takes it from the thread's workspace, which
+ * mtxc_init allocates.  This entry point computes the same reduction, with the same kernels, the same
+ * arguments and the same results, but keeps the partials in a statically sized array that is part of
+ * the library's device image (MTXC_NOALLOC_SCRATCH_BYTES, 4 MiB; every GPU that loads the library
+ * holds it until the process exits).  It calls no allocator: no cudaMalloc, cudaFree or library
+ * routine that allocates.  (Call mtxc_init with MTXC_WORKSPACE_MB=0 in the environment to keep the
+ * runtime from allocating its own workspace as well.)
+ *
+ *   - A reduction whose partials would need more than MTXC_NOALLOC_SCRATCH_BYTES is rejected with
+ *     MTXC_ERR_WORKSPACE and a message giving both sizes; mtxc_reduce_workspace_bytes tells in advance.
+ *   - The first call on each device looks up the array's device address with that device current
+ *     (cudaGetSymbolAddress) and caches it; make that first call before any stream capture.
+ *   - All calls on a device share the one array, and it keeps whatever the last call left in it.
+ *     Nothing in it has to start at zero (every partial is written before it is read), but calls that
+ *     overlap on the GPU -- on different streams or from different threads -- race on it: order them. */
+#define MTXC_NOALLOC_SCRATCH_BYTES (4u << 20)
+int mtxc_reduce_noalloc(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride,
+                        uint32_t reduce_len, uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides,
+                        const uint32_t* src_strides);
+
 /* Broadcasted binary op.  Replaces add/subtract/multiply/divide_gpu_brodcasted
  * (Matrix.mm:7709-8239) and the METAL branch of matrix::max / min(other, result, dev)
  * (Matrix.mm:13396-13450, 14701-14755), binding the primitive's collapsed_dims_3:

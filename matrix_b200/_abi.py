@@ -74,6 +74,7 @@ def lib() -> C.CDLL:
             "mtxc_broadcast_shapes": (i32, [U32P, U32P, i32, U32P, U32P, i32, U32P, U32P, U32P, U32P, U32P, U32P]),
             "mtxc_promote_types": (i32, [i32, i32]),
             "mtxc_reduce": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P]),
+            "mtxc_reduce_noalloc": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P]),
             "mtxc_broadcast_binary": (i32, [i32, i32, vp, vp, vp, u32, U32P, U32P, U32P, U32P]),
             "mtxc_unary": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),
             "mtxc_graph_begin": (i32, []),

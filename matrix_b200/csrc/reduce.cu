@@ -686,3 +686,79 @@ extern "C" int mtxc_reduce_workspace_bytes(int op, int dtype, uint32_t reduce_st
     *bytes = b;
     return MTXC_OK;
 }
+
+// ------------------------------------------------------------------------------------------
+// mtxc_reduce_noalloc: mtxc_reduce with its split partials in a static device array, for callers
+// that cannot allocate device memory.
+// ------------------------------------------------------------------------------------------
+
+// The scratch itself.  It is part of this library's device image: every GPU that loads the library
+// holds it until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MTXC_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxNoallocDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_address[kMaxNoallocDevices] = {};
+
+// In host code `g_noalloc_scratch` is only a host-side stand-in for the array; handing it to a kernel
+// would fault (or, where the GPU can reach host memory, silently use the wrong memory).  Its device
+// address is looked up once per device, with that device current, and cached.
+int noalloc_scratch_address(int device, void** out) {
+    if (device < 0 || device >= kMaxNoallocDevices)
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_noalloc: device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_address[device]) {
+        int current = -1;
+        cudaError_t err = cudaGetDevice(&current);
+        if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+        if (current != device && (err = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+        void* p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (current != device) cudaSetDevice(current);
+        if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(noalloc scratch)");
+        g_noalloc_address[device] = p;
+    }
+    *out = g_noalloc_address[device];
+    return MTXC_OK;
+}
+
+}  // namespace
+
+extern "C" int mtxc_reduce_noalloc(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride,
+                                   uint32_t reduce_len, uint32_t cdims, const uint32_t* shape,
+                                   const uint32_t* dst_strides, const uint32_t* src_strides) {
+    if (int rc = require_init()) return rc;
+    if (op < MTXC_REDUCE_SUM || op > MTXC_REDUCE_ARGMIN)
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_noalloc: unknown op");
+    Meta m;
+    if (int rc = make_meta(cdims, shape, dst_strides, src_strides, m)) return rc;
+    if (product(m.shape, m.cdims) == 0) return MTXC_OK;
+    if (!dst || (!src && reduce_len)) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_noalloc: null buffer");
+    ThreadCtx& c = ctx();
+    size_t need = 0;
+    const bool known = dispatch_dtype(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        need = partial_bytes_op<T>(op, m, src, reduce_stride, reduce_len, c.sm_count);
+    });
+    if (!known)
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE,
+                    std::string("mtxc_reduce_noalloc: no kernel for dtype ") + dtype_name(dtype));
+    if (need > MTXC_NOALLOC_SCRATCH_BYTES)
+        return fail(MTXC_ERR_WORKSPACE, "mtxc_reduce_noalloc: this reduction splits into " + std::to_string(need) +
+                                            " bytes of partials, more than the " +
+                                            std::to_string(MTXC_NOALLOC_SCRATCH_BYTES) +
+                                            "-byte static scratch; use mtxc_reduce with a workspace");
+    void* scratch = nullptr;
+    if (need) {
+        if (int rc = noalloc_scratch_address(c.device, &scratch)) return rc;
+    }
+    int rc = MTXC_OK;
+    dispatch_dtype(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        rc = launch_reduce_op<T>(op, m, dst, src, reduce_stride, reduce_len, scratch,
+                                 scratch ? (size_t)MTXC_NOALLOC_SCRATCH_BYTES : 0, c.sm_count, c.stream());
+    });
+    return rc;
+}
