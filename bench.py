@@ -411,6 +411,98 @@ def run_ours(args):
     return 0
 
 
+# ------------------------------------------------------------------------------------------
+# sharded reductions (configs 4 and 5b): the reduced axis is the sharded one
+# ------------------------------------------------------------------------------------------
+def run_sharded(args):
+    """C5b: full Sum of f32 2^32 elements (as [8, 2^29], 16 GiB), or C4: Sum over axes (0, 2) of f32
+    [32, 4096, 2048], with axis 0 sharded over the GPUs (strong scaling: the total is fixed).  A step
+    is the local kernels, the NCCL all-gather of the per-rank partials and the ordered merge."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from matrix_b200 import _abi, backend
+    from matrix_b200.shard import reduce_sharded, shard_range
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    else:  # one rank: an in-process store, nothing to rendezvous with
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+    backend.init(local)
+    stream = torch.cuda.current_stream(dev)
+    if args.workload == "c5b":
+        rows, cols = 8, 1 << 29
+        shape = (rows, cols)
+        desc = "C5b: full Sum of f32 2^32 ~ N(0,1) as [8, 2^29] (16 GiB), rows sharded, all-gather + ordered merge"
+    else:
+        rows, cols = 32, 4096 * 2048
+        shape = (32, 4096, 2048)
+        desc = "C4: Sum over axes (0,2) of f32 [32,4096,2048] ~ N(0,1), axis 0 sharded, all-gather + ordered merge"
+    lo, hi = shard_range(rows, world, rank)
+    x = torch.empty((hi - lo, *shape[1:]), device=dev)
+    g = torch.Generator(device=dev)
+    for r in range(lo, hi):  # every global row from its own seed: the tensor does not depend on N
+        g.manual_seed(1000 + r)
+        x[r - lo].normal_(generator=g)
+    total_bytes = rows * cols * 4
+
+    def step():
+        if args.workload == "c5b":
+            part = backend.reduce("sum", x, 1)                    # local axis: no collective
+            return reduce_sharded("sum", part, 0, rows)           # sharded axis: gather + merge
+        part = backend.reduce("sum", x, 2)                        # [rows_local, 4096]
+        return reduce_sharded("sum", part, 0, rows)               # [4096]
+
+    result = step()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        result = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev if world > 1 else "cpu")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    # correctness: the fp64 sum of the same tensor (torch, as a reference value only)
+    dims = tuple(range(1, x.dim())) if args.workload == "c5b" else (0, 2)
+    ref = x.sum(dim=dims, dtype=torch.float64)
+    absum = x.abs().sum(dim=dims, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ref)
+        dist.all_reduce(absum)
+    ref = ref.sum() if args.workload == "c5b" else ref
+    absum = absum.sum() if args.workload == "c5b" else absum
+    ok = bool(((result.double() - ref).abs() <= 1e-5 * absum + 1e-30).all())
+    if rank == 0:
+        peak, _ = measured_peak()
+        value = total_bytes * args.steps / (ms / 1e3) / 1e9
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) per row)",
+                "config": {"workload": desc, "parallelism": f"axis 0 sharded over {world} GPU(s)",
+                           "l2": "input larger than L2"},
+                "frac_of_hbm_peak": round(value / world / peak, 4), "within_tolerance_of_fp64": ok}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if ok else 1
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -422,11 +514,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--rows", type=int, default=256, help="leading rows of a per rank (256 = C2; smaller for ncu)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--workload", choices=["c2", "c4", "c5b"], default="c2",
+                    help="c2 (default headline) or a sharded reduction over the GPUs (c4, c5b)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "c2":
+        return run_sharded(args)
     return run_ours(args)
 
 

@@ -193,6 +193,27 @@ int mtxc_promote_types(int a, int b);
 int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
                 uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides, const uint32_t* src_strides);
 
+/* Max and ArgMax (op MAX or ARGMAX) or Min and ArgMin (op MIN or ARGMIN) from a single read of the
+ * input: dst_values receives exactly what mtxc_reduce(MAX / MIN) writes and dst_indices exactly what
+ * mtxc_reduce(ARGMAX / ARGMIN) writes, for the same metadata.  Serves the reference's
+ * `x.max(axis)` + `x.argmax(axis)` pair (config 3) with half the HBM traffic, and the per-shard
+ * partials of a sharded ArgMax. */
+int mtxc_reduce_pair(int op, int dtype, void* dst_values, int32_t* dst_indices, const void* src,
+                     uint32_t reduce_stride, uint32_t reduce_len, uint32_t cdims, const uint32_t* shape,
+                     const uint32_t* dst_strides, const uint32_t* src_strides);
+
+/* Merges the partial results of `parts` shards of a reduced axis, in shard order (the cross-GPU step
+ * when the sharded axis is the reduced one).  part_values holds parts x outputs results, part-major
+ * (dtype `dtype`; for ARGMAX / ARGMIN the shards' extreme values, from mtxc_reduce_pair).  SUM adds
+ * them in order; MAX / MIN keep the first shard's value unless a later one is strictly better;
+ * ARGMAX / ARGMIN pick the shard the same way and write part_indices[p][j] + index_offsets[p]
+ * (index_offsets: host array, the first element of each shard's slice) to dst_indices, and the value to
+ * dst unless dst is NULL.  parts <= 256.  Results equal the unsharded reduction's (float sums within
+ * rounding). */
+int mtxc_merge_partials(int op, int dtype, void* dst, int32_t* dst_indices, const void* part_values,
+                        const int32_t* part_indices, const int64_t* index_offsets, uint32_t parts,
+                        uint64_t outputs);
+
 /* mtxc_reduce for callers that cannot allocate device memory.  No counterpart in the reference.
  *
  * Some callers of this library may not call cudaMalloc: code that runs inside another framework's
@@ -239,6 +260,19 @@ int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, const void*
  * (Matrix.mm:6934-7065).  EXP on float: CUDA expf, within 2 ulp of the CPU's std::exp. */
 int mtxc_unary(int op, int dtype, void* dst, const void* src, uint32_t cdims, const uint32_t* shape,
                const uint32_t* dst_strides, const uint32_t* src_strides);
+
+/* Fused evaluation of the reference's softmax trace over the last axis of contiguous float rows
+ *     m = x.max(-1, true); e = matrix::exp(x - m); y = e / e.sum(-1, true)
+ * (MaxReduction, Subtraction, Exp, Sum and Division primitives; BASELINE config 5a): x is read once
+ * and y written once.  Element-wise identical to the trace (same max, x - m, expf, one division)
+ * except for the order of the fp32 additions in the row sum.  Rows start row_stride elements apart;
+ * row_len must be a multiple of 4, rows 16-byte aligned and row_len <= MTXC_SOFTMAX_MAX_ROW, else
+ * MTXC_ERR_INVALID_ARGUMENT (evaluate the unfused trace instead).  A compiled trace substitutes it
+ * for those five primitives when their shapes match (no counterpart kernel in the reference, which
+ * runs the five primitives one by one). */
+#define MTXC_SOFTMAX_MAX_ROW 65536u
+int mtxc_softmax_lastdim(int dtype, void* dst, const void* src, uint64_t rows, uint32_t row_len,
+                         uint64_t src_row_stride, uint64_t dst_row_stride);
 
 /* ------------------------------------------------------------------------------------------
  * Compiled trace: record the kernels one execute pass enqueues and replay them.  The B200

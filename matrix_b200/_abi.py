@@ -75,8 +75,11 @@ def lib() -> C.CDLL:
             "mtxc_promote_types": (i32, [i32, i32]),
             "mtxc_reduce": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P]),
             "mtxc_reduce_noalloc": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P]),
+            "mtxc_reduce_pair": (i32, [i32, i32, vp, vp, vp, u32, u32, u32, U32P, U32P, U32P]),
+            "mtxc_merge_partials": (i32, [i32, i32, vp, vp, vp, vp, vp, u32, u64]),
             "mtxc_broadcast_binary": (i32, [i32, i32, vp, vp, vp, u32, U32P, U32P, U32P, U32P]),
             "mtxc_unary": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),
+            "mtxc_softmax_lastdim": (i32, [i32, vp, vp, u64, u32, u64, u64]),
             "mtxc_graph_begin": (i32, []),
             "mtxc_graph_end": (i32, [C.POINTER(vp)]),
             "mtxc_graph_launch": (i32, [vp]),

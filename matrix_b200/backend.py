@@ -204,3 +204,59 @@ def exp(x: torch.Tensor, out: torch.Tensor | None = None, meta: UnaryMeta | None
     shape, so, si = meta.arrays
     check(lib().mtxc_unary(_abi.UNARY_OPS["exp"], code, out.data_ptr(), x.data_ptr(), meta.cdims, shape, so, si))
     return out
+
+
+def softmax_lastdim(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's softmax trace over the last axis (max, sub, exp, sum, div) fused into one
+    kernel (mtxc_softmax_lastdim).  x: contiguous rows of float32."""
+    if x.dim() == 0 or x.stride(-1) != 1:
+        raise ValueError("softmax_lastdim needs unit-stride rows")
+    code = dtype_code(x.dtype)
+    n = x.shape[-1]
+    rows = x.numel() // n if n else 0
+    row_stride = x.stride(-2) if x.dim() > 1 else n
+    if x.dim() > 2 and not x.is_contiguous():
+        raise ValueError("softmax_lastdim needs rows at a constant stride")
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    out_stride = out.stride(-2) if out.dim() > 1 else n
+    check(lib().mtxc_softmax_lastdim(code, out.data_ptr(), x.data_ptr(), rows, n, row_stride, out_stride))
+    return out
+
+
+def reduce_pair(op: str, x: torch.Tensor, axis: int, keepdims: bool = False, meta: ReduceMeta | None = None):
+    """(x.max(axis), x.argmax(axis)) -- or min / argmin -- from one read (mtxc_reduce_pair)."""
+    code = dtype_code(x.dtype)
+    if meta is None:
+        meta = reduce_meta(list(x.shape), _check_strides(x), axis, keepdims)
+    vals = torch.empty(meta.out_shape, dtype=x.dtype, device=x.device)
+    idx = torch.empty(meta.out_shape, dtype=torch.int32, device=x.device)
+    shape, s_out, s_in = meta.arrays
+    check(lib().mtxc_reduce_pair(_abi.REDUCE_OPS[op], code, vals.data_ptr(), idx.data_ptr(), x.data_ptr(),
+                                 meta.rstride & 0xFFFFFFFF, meta.rlen, meta.cdims, shape, s_out, s_in))
+    return vals, idx
+
+
+def merge_partials(op: str, values: torch.Tensor, indices: torch.Tensor | None = None, offsets=None):
+    """Merges shard partials stacked on axis 0 ([parts, ...]) in shard order (mtxc_merge_partials).
+    Returns the merged values (sum / max / min) or (values, global indices) (argmax / argmin)."""
+    import ctypes
+
+    parts = values.shape[0]
+    outputs = values[0].numel()
+    code = dtype_code(values.dtype)
+    values = values.contiguous()
+    if op in ("argmax", "argmin"):
+        if indices is None or offsets is None:
+            raise ValueError("argmax / argmin merges need the shards' indices and index offsets")
+        indices = indices.contiguous()
+        out_v = torch.empty(values.shape[1:], dtype=values.dtype, device=values.device)
+        out_i = torch.empty(values.shape[1:], dtype=torch.int32, device=values.device)
+        offs = (ctypes.c_int64 * parts)(*[int(o) for o in offsets])
+        check(lib().mtxc_merge_partials(_abi.REDUCE_OPS[op], code, out_v.data_ptr(), out_i.data_ptr(),
+                                        values.data_ptr(), indices.data_ptr(), offs, parts, outputs))
+        return out_v, out_i
+    out = torch.empty(values.shape[1:], dtype=values.dtype, device=values.device)
+    check(lib().mtxc_merge_partials(_abi.REDUCE_OPS[op], code, out.data_ptr(), None, values.data_ptr(), None, None,
+                                    parts, outputs))
+    return out

@@ -76,6 +76,18 @@ __device__ __forceinline__ T shfl_xor(T v, int mask) {
     }
 }
 
+// Where a reduction writes: values (T, or int32 indices for ArgMax / ArgMin) and, for the
+// (value, index) pair ops, the indices as well.
+struct Out {
+    void* v;
+    int32_t* i;
+};
+
+// Internal op codes beyond the public ones: ArgMax / ArgMin writing both the extreme value and its
+// first index (mtxc_reduce_pair).
+constexpr int kPairMax = 5;
+constexpr int kPairMin = 6;
+
 template <int OP, typename T>
 struct Reducer;
 
@@ -92,7 +104,7 @@ struct Reducer<MTXC_REDUCE_SUM, T> {
         else s = (State)(s + o);
     }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
-    __device__ static void store(void* dst, uint64_t gid, const State& s) { static_cast<T*>(dst)[gid] = (T)s; }
+    __device__ static void store(const Out& o, uint64_t gid, const State& s) { static_cast<T*>(o.v)[gid] = (T)s; }
 };
 
 // Extremum with index (floats for Max / Min; every type for ArgMax / ArgMin).
@@ -123,34 +135,50 @@ struct ValueExtremum {
     }
     __device__ static void merge(State& s, const State& o) { fold(s, o, 0); }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
-    __device__ static void store(void* dst, uint64_t gid, const State& s) { static_cast<T*>(dst)[gid] = s; }
+    __device__ static void store(const Out& o, uint64_t gid, const State& s) { static_cast<T*>(o.v)[gid] = s; }
 };
 
 template <typename T>
 struct Reducer<MTXC_REDUCE_MAX, T>
     : std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, true>, ValueExtremum<T, true>> {
     using Base = std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, true>, ValueExtremum<T, true>>;
-    __device__ static void store(void* dst, uint64_t gid, const typename Base::State& s) {
-        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(dst)[gid] = s.v;
-        else static_cast<T*>(dst)[gid] = s;
+    __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
+        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(o.v)[gid] = s.v;
+        else static_cast<T*>(o.v)[gid] = s;
     }
 };
 template <typename T>
 struct Reducer<MTXC_REDUCE_MIN, T>
     : std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, false>, ValueExtremum<T, false>> {
     using Base = std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, false>, ValueExtremum<T, false>>;
-    __device__ static void store(void* dst, uint64_t gid, const typename Base::State& s) {
-        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(dst)[gid] = s.v;
-        else static_cast<T*>(dst)[gid] = s;
+    __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
+        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(o.v)[gid] = s.v;
+        else static_cast<T*>(o.v)[gid] = s;
     }
 };
 template <typename T>
 struct Reducer<MTXC_REDUCE_ARGMAX, T> : PairExtremum<T, true> {
-    __device__ static void store(void* dst, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(dst)[gid] = s.i; }
+    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(o.v)[gid] = s.i; }
 };
 template <typename T>
 struct Reducer<MTXC_REDUCE_ARGMIN, T> : PairExtremum<T, false> {
-    __device__ static void store(void* dst, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(dst)[gid] = s.i; }
+    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(o.v)[gid] = s.i; }
+};
+// Max / Min value and its first index in one pass: exactly the Max and ArgMax (Min and ArgMin)
+// results, since a (value, index) state that was never updated holds (initial value, 0).
+template <typename T>
+struct Reducer<kPairMax, T> : PairExtremum<T, true> {
+    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) {
+        static_cast<T*>(o.v)[gid] = s.v;
+        o.i[gid] = s.i;
+    }
+};
+template <typename T>
+struct Reducer<kPairMin, T> : PairExtremum<T, false> {
+    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) {
+        static_cast<T*>(o.v)[gid] = s.v;
+        o.i[gid] = s.i;
+    }
 };
 
 template <typename R>
@@ -179,7 +207,7 @@ __device__ __forceinline__ uint64_t run_offset(uint32_t row, const Dims& d) {
 // rows: contiguous reduced axis
 // ------------------------------------------------------------------------------------------
 struct RowArgs {
-    void* dst;
+    Out out;
     const void* src;
     void* partials;     // S * M states when split > 1
     uint32_t len;       // elements per run
@@ -256,7 +284,7 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
             __syncthreads();
         }
         if (lane == 0) {
-            if (a.split == 1) R::store(a.dst, row, st[0]);
+            if (a.split == 1) R::store(a.out, row, st[0]);
             else static_cast<S*>(a.partials)[(uint64_t)part * a.rows + row] = st[0];
         }
     }
@@ -266,7 +294,7 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
 // cols: strided reduced axis, contiguous innermost output axis
 // ------------------------------------------------------------------------------------------
 struct ColArgs {
-    void* dst;
+    Out out;
     const void* src;
     void* partials;
     uint32_t len;         // reduced axis length
@@ -345,7 +373,7 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
         const uint64_t gid = (uint64_t)o * a.inner + col;
 #pragma unroll
         for (int j = 0; j < V; ++j) {
-            if (a.split == 1) R::store(a.dst, gid + j, st[j]);
+            if (a.split == 1) R::store(a.out, gid + j, st[j]);
             else static_cast<S*>(a.partials)[(uint64_t)part * a.outputs + gid + j] = st[j];
         }
     }
@@ -355,7 +383,7 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
 // finalize: merge split partials in split order
 // ------------------------------------------------------------------------------------------
 template <int OP, typename T>
-__global__ void __launch_bounds__(kBlock) reduce_finalize_kernel(void* dst, const void* partials, uint64_t outputs,
+__global__ void __launch_bounds__(kBlock) reduce_finalize_kernel(const Out dst, const void* partials, uint64_t outputs,
                                                                  uint32_t split) {
     using R = Reducer<OP, T>;
     using S = typename R::State;
@@ -372,7 +400,7 @@ __global__ void __launch_bounds__(kBlock) reduce_finalize_kernel(void* dst, cons
 // generic: one thread per output, the reference CPU loop (Matrix.mm:15193-15205)
 // ------------------------------------------------------------------------------------------
 struct GenericArgs {
-    void* dst;
+    Out out;
     const void* src;
     uint64_t outputs;
     uint32_t len;
@@ -396,7 +424,7 @@ __global__ void __launch_bounds__(kBlock) reduce_generic_kernel(const GenericArg
         typename R::State s = R::init();
         const T* p = src + off;
         for (uint32_t i = 0; i < a.len; ++i) R::fold(s, p[(uint64_t)i * a.rstride], i);
-        R::store(a.dst, gid, s);
+        R::store(a.out, gid, s);
     }
 }
 
@@ -515,7 +543,7 @@ ReducePlan plan_reduce(const Meta& m, const void* src, uint32_t rstride, uint32_
 }
 
 template <int OP, typename T>
-int launch_reduce(const Meta& m, void* dst, const void* src, uint32_t rstride, uint32_t len, void* workspace,
+int launch_reduce(const Meta& m, const Out dst, const void* src, uint32_t rstride, uint32_t len, void* workspace,
                   size_t workspace_bytes, int sm_count, cudaStream_t stream) {
     const ReducePlan p = plan_reduce<OP, T>(m, src, rstride, len, workspace_bytes, sm_count);
     if (p.outputs == 0) return MTXC_OK;
@@ -525,7 +553,7 @@ int launch_reduce(const Meta& m, void* dst, const void* src, uint32_t rstride, u
     const uint32_t k = m.cdims - 1;
     if (p.kind == Plan::kRows) {
         RowArgs a{};
-        a.dst = dst;
+        a.out = dst;
         a.src = src;
         a.partials = workspace;
         a.len = len;
@@ -547,7 +575,7 @@ int launch_reduce(const Meta& m, void* dst, const void* src, uint32_t rstride, u
         if (int rc = check_launch("reduce_rows_kernel")) return rc;
     } else if (p.kind == Plan::kCols) {
         ColArgs a{};
-        a.dst = dst;
+        a.out = dst;
         a.src = src;
         a.partials = workspace;
         a.len = len;
@@ -572,7 +600,7 @@ int launch_reduce(const Meta& m, void* dst, const void* src, uint32_t rstride, u
         if (int rc = check_launch("reduce_cols_kernel")) return rc;
     } else {
         GenericArgs a{};
-        a.dst = dst;
+        a.out = dst;
         a.src = src;
         a.outputs = p.outputs;
         a.len = len;
@@ -595,7 +623,7 @@ int launch_reduce(const Meta& m, void* dst, const void* src, uint32_t rstride, u
 }
 
 template <typename T>
-int launch_reduce_op(int op, const Meta& m, void* dst, const void* src, uint32_t rstride, uint32_t len, void* ws,
+int launch_reduce_op(int op, const Meta& m, const Out dst, const void* src, uint32_t rstride, uint32_t len, void* ws,
                      size_t wsb, int sms, cudaStream_t st) {
     switch (op) {
         case MTXC_REDUCE_SUM: return launch_reduce<MTXC_REDUCE_SUM, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
@@ -603,6 +631,8 @@ int launch_reduce_op(int op, const Meta& m, void* dst, const void* src, uint32_t
         case MTXC_REDUCE_MIN: return launch_reduce<MTXC_REDUCE_MIN, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
         case MTXC_REDUCE_ARGMAX: return launch_reduce<MTXC_REDUCE_ARGMAX, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
         case MTXC_REDUCE_ARGMIN: return launch_reduce<MTXC_REDUCE_ARGMIN, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case kPairMax: return launch_reduce<kPairMax, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case kPairMin: return launch_reduce<kPairMin, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
         default: return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: unknown op");
     }
 }
@@ -615,6 +645,8 @@ size_t partial_bytes_op(int op, const Meta& m, const void* src, uint32_t rstride
         case MTXC_REDUCE_MAX: return plan_reduce<MTXC_REDUCE_MAX, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
         case MTXC_REDUCE_MIN: return plan_reduce<MTXC_REDUCE_MIN, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
         case MTXC_REDUCE_ARGMAX: return plan_reduce<MTXC_REDUCE_ARGMAX, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+        case kPairMax: return plan_reduce<kPairMax, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+        case kPairMin: return plan_reduce<kPairMin, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
         default: return plan_reduce<MTXC_REDUCE_ARGMIN, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
     }
 }
@@ -659,7 +691,7 @@ extern "C" int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32
     int rc = MTXC_OK;
     const bool known = dispatch_dtype(dtype, [&](auto* tag) {
         using T = std::remove_pointer_t<decltype(tag)>;
-        rc = launch_reduce_op<T>(op, m, dst, src, reduce_stride, reduce_len, c.workspace, c.workspace_bytes, c.sm_count,
+        rc = launch_reduce_op<T>(op, m, Out{dst, nullptr}, src, reduce_stride, reduce_len, c.workspace, c.workspace_bytes, c.sm_count,
                                  c.stream());
     });
     if (!known)
@@ -757,8 +789,36 @@ extern "C" int mtxc_reduce_noalloc(int op, int dtype, void* dst, const void* src
     int rc = MTXC_OK;
     dispatch_dtype(dtype, [&](auto* tag) {
         using T = std::remove_pointer_t<decltype(tag)>;
-        rc = launch_reduce_op<T>(op, m, dst, src, reduce_stride, reduce_len, scratch,
+        rc = launch_reduce_op<T>(op, m, Out{dst, nullptr}, src, reduce_stride, reduce_len, scratch,
                                  scratch ? (size_t)MTXC_NOALLOC_SCRATCH_BYTES : 0, c.sm_count, c.stream());
     });
+    return rc;
+}
+
+// ------------------------------------------------------------------------------------------
+// mtxc_reduce_pair: Max and ArgMax (Min and ArgMin) from one read of the input.
+// ------------------------------------------------------------------------------------------
+extern "C" int mtxc_reduce_pair(int op, int dtype, void* dst_values, int32_t* dst_indices, const void* src,
+                                uint32_t reduce_stride, uint32_t reduce_len, uint32_t cdims, const uint32_t* shape,
+                                const uint32_t* dst_strides, const uint32_t* src_strides) {
+    if (int rc = require_init()) return rc;
+    int pair_op;
+    if (op == MTXC_REDUCE_MAX || op == MTXC_REDUCE_ARGMAX) pair_op = kPairMax;
+    else if (op == MTXC_REDUCE_MIN || op == MTXC_REDUCE_ARGMIN) pair_op = kPairMin;
+    else return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_pair: op must be MAX / ARGMAX or MIN / ARGMIN");
+    Meta m;
+    if (int rc = make_meta(cdims, shape, dst_strides, src_strides, m)) return rc;
+    if (product(m.shape, m.cdims) == 0) return MTXC_OK;
+    if (!dst_values || !dst_indices || (!src && reduce_len))
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_pair: null buffer");
+    ThreadCtx& c = ctx();
+    int rc = MTXC_OK;
+    const bool known = dispatch_dtype(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        rc = launch_reduce_op<T>(pair_op, m, Out{dst_values, dst_indices}, src, reduce_stride, reduce_len, c.workspace,
+                                 c.workspace_bytes, c.sm_count, c.stream());
+    });
+    if (!known)
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_reduce_pair: no kernel for dtype ") + dtype_name(dtype));
     return rc;
 }

@@ -121,6 +121,9 @@ def run_all(dev, stream):
     n = 8192 * 32768 * 4
     out.append(_line("C5a-trace", "softmax trace max,sub,exp,sum,div f32 [8192,32768] (5 kernels)", 2 * n, ms, peak,
                      moved_bytes=8 * n))
+    ms = _time(lambda: backend.softmax_lastdim(x, out=t), stream)
+    out.append(_line("C5a-fused", "softmax trace fused (mtxc_softmax_lastdim) f32 [8192,32768]", 2 * n, ms, peak,
+                     moved_bytes=2 * n))
     del x, t
 
     # C5b: full Sum of 2^32 f32 ~ N(0,1) as [8, 2^29] (16 GiB): sum(1) then sum(0)

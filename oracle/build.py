@@ -9,12 +9,11 @@ box's host as well.  ``-ffp-contract=off`` keeps the float loops one rounding pe
 """
 from __future__ import annotations
 
+import importlib.util
 import subprocess
-import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, str(HERE))
 
 LIB = HERE / "liboracle.so"
 
@@ -29,8 +28,9 @@ def build_port() -> Path:
 
 def build(quiet: bool = True) -> None:
     build_port()
-    import build_ref  # noqa: E402  (sibling module)
-
+    spec = importlib.util.spec_from_file_location("oracle_build_ref", HERE / "build_ref.py")
+    build_ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(build_ref)
     build_ref.build(build_ref.reference_root(None), quiet=quiet)
 
 

@@ -1,0 +1,102 @@
+"""The cross-shard kernels on one GPU, and the sharded path on real GPU ranks when there are two.
+
+* mtxc_reduce_pair: the (Max, ArgMax) / (Min, ArgMin) pair from one read must equal the separate
+  reductions (and hence the oracle) bit for bit.
+* mtxc_merge_partials: a tensor is cut along axis 0 into uneven "shards" on one device, each shard
+  is reduced on its own, the partials are stacked in shard order and merged; the result must equal
+  the oracle's reduction of the whole tensor (bit for bit, float sums within the usual tolerance).
+* With two GPUs, matrix_b200.shard.reduce_sharded runs under torchrun with NCCL and must agree with
+  the oracle on every rank.
+"""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from tests.helpers import assert_bits_equal, assert_sum_close, make_values
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("op", ["max", "min"])
+def test_reduce_pair_equals_separate_reductions(gpu, port, op):
+    import torch
+
+    rng = np.random.default_rng(3)
+    for shape, axis in (([64, 8192, 64], 1), ([33, 1000], 1), ([4, 70000], 1), ([300, 9, 40], 0), ([5, 1 << 20], 1)):
+        x = make_values(rng, int(np.prod(shape)), np.float32, "ties").reshape(shape)
+        x.reshape(-1)[::97] = np.nan
+        xd = torch.from_numpy(x).cuda()
+        v, i = gpu.reduce_pair(op, xd, axis)
+        gpu.sync()
+        assert_bits_equal(v.cpu().numpy(), port.reduce(op, x, axis), f"pair value {op} {shape}")
+        assert_bits_equal(i.cpu().numpy(), port.reduce("arg" + op, x, axis), f"pair index {op} {shape}")
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.int32, np.int64], ids=["f32", "i32", "i64"])
+@pytest.mark.parametrize("op", ["sum", "max", "min", "argmax", "argmin"])
+def test_merge_partials_of_simulated_shards(gpu, port, op, dtype):
+    import torch
+
+    rng = np.random.default_rng(5)
+    shape = [13, 300, 70]
+    if dtype == np.float32:
+        x = (np.floor(rng.standard_normal(shape) * 4) / 4).astype(np.float32)
+        x[2, 5, :] = np.nan
+        x[:, 7, 3] = -0.0
+        x[6:, 7, 3] = 0.0
+        x[:, 9, :] = -np.inf
+    else:
+        x = make_values(rng, int(np.prod(shape)), dtype, "full").reshape(shape)
+    xd = torch.from_numpy(x).cuda()
+    bounds = [0, 3, 4, 9, 13]  # uneven shards along axis 0
+    parts_v, parts_i = [], []
+    for lo, hi in zip(bounds[:-1], bounds[1:]):
+        if op in ("argmax", "argmin"):
+            v, i = gpu.reduce_pair(op, xd[lo:hi], 0)
+            parts_v.append(v)
+            parts_i.append(i)
+        else:
+            parts_v.append(gpu.reduce(op, xd[lo:hi], 0))
+    vals = torch.stack(parts_v)
+    if op in ("argmax", "argmin"):
+        mv, mi = gpu.merge_partials(op, vals, torch.stack(parts_i), bounds[:-1])
+        gpu.sync()
+        assert_bits_equal(mi.cpu().numpy(), port.reduce(op, x, 0), f"merged {op}")
+        assert_bits_equal(mv.cpu().numpy(), port.reduce(op[3:], x, 0), f"merged {op} value")
+        return
+    m = gpu.merge_partials(op, vals)
+    gpu.sync()
+    want = port.reduce(op, x, 0)
+    if op == "sum" and dtype == np.float32:
+        x64 = x.astype(np.float64)
+        assert_sum_close(m.cpu().numpy(), want, np.abs(x64).sum(0), "merged sum", exact=x64.sum(0))
+    else:
+        assert_bits_equal(m.cpu().numpy(), want, f"merged {op}")
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_reduce_sharded_on_two_gpus():
+    """torchrun, 2 ranks, NCCL: every op over the sharded and a local axis (skipped on 1 GPU)."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=repo)
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(repo, "tests", "multirank_shard_check.py")]
+    res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert res.stdout.count("rank ok") == 2, res.stdout[-2000:]
