@@ -2,8 +2,11 @@
 m = x.max(-1, true); e = exp(x - m); y = e / e.sum(-1, true), primitive by primitive on the CPU.
 
 Element-wise the fused kernel performs the same operations as the trace; only the fp32 summation
-order of the row sum differs, so outputs agree to a relative 1e-5 (the sum's relative error bound at
-these lengths is far below that; exp adds at most 2 ulp)."""
+order of the row sum differs.  Outputs must agree with the trace to a relative 1e-5.  The trace's own
+sequential fp32 row sum can drift further than that from the exact sum on long rows (tens of
+thousands of positive terms); there the fused result is accepted when it is within 1e-5 of the exact
+(fp64) softmax and no further from the trace than the trace is from exact -- the rule the float-sum
+tests use (tests/helpers.py)."""
 import numpy as np
 import pytest
 
@@ -25,8 +28,16 @@ def check(gpu, port, x, what=""):
     g = y.cpu().numpy()
     assert g.shape == y_cpu.shape
     both_nan = np.isnan(g) & np.isnan(y_cpu)
-    with np.errstate(invalid="ignore"):
+    with np.errstate(invalid="ignore", over="ignore"):
         ok = both_nan | (np.abs(g - y_cpu) <= 1e-5 * np.abs(y_cpu))
+        if not ok.all():
+            x64 = x.astype(np.float64)
+            m = np.max(np.where(np.isnan(x64), -np.inf, x64), axis=-1, keepdims=True)
+            m = np.maximum(m, -np.finfo(np.float32).max)
+            e = np.exp(x64 - m)
+            y64 = e / e.sum(-1, keepdims=True)
+            tol = 1e-5 * np.abs(y64)
+            ok |= (np.abs(g - y64) <= tol) & (np.abs(g - y_cpu) <= np.abs(y_cpu - y64) + 1e-5 * np.abs(y_cpu))
     assert ok.all(), f"{what}: {np.count_nonzero(~ok)} mismatches, first {np.argwhere(~ok)[0]}"
 
 
