@@ -24,7 +24,15 @@ int cuda_fail(cudaError_t err, const char* what) {
 }
 
 int require_init() {
-    if (ctx().device < 0) return fail(MTXC_ERR_NOT_INITIALIZED, "mtxc_init was not called on this thread");
+    ThreadCtx& c = ctx();
+    if (c.device < 0) return fail(MTXC_ERR_NOT_INITIALIZED, "mtxc_init was not called on this thread");
+    // Other code in the process (another library, another runtime) may have made a different
+    // device current on this thread since mtxc_init; launches and copies must go to the bound one.
+    int current = -1;
+    if (cudaGetDevice(&current) != cudaSuccess || current != c.device) {
+        cudaError_t err = cudaSetDevice(c.device);
+        if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+    }
     return MTXC_OK;
 }
 
