@@ -21,6 +21,8 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIBDIR = PKG / "lib"
 LIB = LIBDIR / "libmtxc.so"
+HOST = PKG / "host"
+HOST_LIB = LIBDIR / "libmtx.so"
 INCLUDE = REPO / "include"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -77,6 +79,11 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
                 print(out, file=sys.stderr)
     if jobs or not LIB.exists() or _stale(LIB, objs):
         run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)])
+    # the C++ host mirror of the reference API (mtx.hpp), a plain C++ library over the C ABI
+    host_srcs = sorted(HOST.glob("*.cpp"))
+    if host_srcs and (not HOST_LIB.exists() or _stale(HOST_LIB, [*host_srcs, *HOST.glob("*.hpp"), LIB, *headers])):
+        run(["g++", "-O2", "-std=c++17", "-fPIC", "-Wall", "-shared", "-I", str(INCLUDE), "-I", str(HOST),
+             "-o", str(HOST_LIB), *map(str, host_srcs), "-L", str(LIBDIR), "-lmtxc", "-Wl,-rpath,$ORIGIN"])
     return LIB
 
 

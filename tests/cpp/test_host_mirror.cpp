@@ -1,0 +1,287 @@
+// Tests of the C++ host mirror (matrix_b200/host/mtx.hpp) on a GPU, written the way a user of the
+// reference writes matrix code: build lazy expressions, eval() / compile() / execute() them, read
+// the results back.  Expected values come from the CPU oracle (oracle/liboracle.so), which restates
+// the reference's CPU eval; comparison rules as in tests/helpers.py (bit-exact, all NaNs equal;
+// float sums within 1e-5 * sum|x|; exp within 2 ulp; softmax within a relative 1e-5).
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "mtx.hpp"
+
+extern "C" {
+uint32_t orc_collapse3(const uint32_t*, const uint32_t*, const uint32_t*, const uint32_t*, uint32_t, uint64_t, uint32_t*,
+                       uint32_t*, uint32_t*, uint32_t*);
+uint32_t orc_collapse_reduce2(const uint32_t*, const uint32_t*, const uint32_t*, uint32_t, int, int, int, uint64_t,
+                              uint32_t*, uint32_t*, uint32_t*);
+int orc_broadcast_shapes(const uint32_t*, const uint32_t*, int, const uint32_t*, const uint32_t*, int, uint32_t*,
+                         uint32_t*, uint32_t*, uint32_t*, uint32_t*, uint32_t*);
+int orc_reduce(int, int, void*, const void*, uint32_t, uint32_t, uint32_t, const uint32_t*, const uint32_t*,
+               const uint32_t*, uint64_t, int);
+int orc_broadcast(int, int, void*, const void*, const void*, uint32_t, const uint32_t*, const uint32_t*, const uint32_t*,
+                  uint64_t, int);
+}
+
+using mtx::dtype;
+using mtx::matrix;
+using mtx::size_m;
+
+static int checks = 0, failures = 0;
+
+#define EXPECT(cond, ...)                          \
+    do {                                           \
+        ++checks;                                  \
+        if (!(cond)) {                             \
+            ++failures;                            \
+            std::printf("FAIL %s:%d: ", __FILE__, __LINE__); \
+            std::printf(__VA_ARGS__);              \
+            std::printf("\n");                     \
+        }                                          \
+    } while (0)
+
+static std::vector<size_m> row_major(const std::vector<size_m>& shape) {
+    std::vector<size_m> s(shape.size());
+    size_m acc = 1;
+    for (int i = (int)shape.size() - 1; i >= 0; --i) {
+        s[i] = acc;
+        acc *= shape[i];
+    }
+    return s;
+}
+
+static uint64_t total(const std::vector<size_m>& s) {
+    uint64_t p = 1;
+    for (auto e : s) p *= e;
+    return p;
+}
+
+// Oracle: x.op(axis, keepdims) on host data with the given view strides
+template <typename T>
+static std::vector<uint8_t> oracle_reduce(int op, const std::vector<T>& base, const std::vector<size_m>& shape,
+                                          const std::vector<size_m>& strides, int axis, bool keep, int dtype_code) {
+    const uint32_t dims = (uint32_t)shape.size();
+    std::vector<size_m> out_shape = shape;
+    if (keep) out_shape[axis] = 1;
+    else out_shape.erase(out_shape.begin() + axis);
+    std::vector<size_m> so = row_major(out_shape);
+    so.resize(dims, 0);
+    uint32_t cs[8], sa[8], sb[8];
+    uint32_t k = orc_collapse_reduce2(shape.data(), so.data(), strides.data(), dims, axis, 0, keep ? 0 : 1, 0xFFFFFFFFu,
+                                      cs, sa, sb);
+    const uint64_t n = total(out_shape);
+    const size_t es = op >= 3 ? 4 : sizeof(T);
+    std::vector<uint8_t> out(std::max<uint64_t>(n, 1) * es);
+    orc_reduce(op, dtype_code, out.data(), base.data(), strides[axis], shape[axis], k, cs, sa, sb, n, 1);
+    out.resize(n * es);
+    return out;
+}
+
+template <typename T>
+static std::vector<uint8_t> oracle_binary(int op, const std::vector<T>& a, const std::vector<size_m>& ash,
+                                          const std::vector<T>& b, const std::vector<size_m>& bsh, int dtype_code) {
+    std::vector<size_m> ast = row_major(ash), bst = row_major(bsh);
+    const int od = (int)std::max(ash.size(), bsh.size());
+    uint32_t os[8], ost[8], as_[8], ast2[8], bs_[8], bst2[8];
+    orc_broadcast_shapes(ash.data(), ast.data(), (int)ash.size(), bsh.data(), bst.data(), (int)bsh.size(), os, ost, as_,
+                         ast2, bs_, bst2);
+    uint32_t cs[8], ca[8], cb[8], cr[8];
+    uint32_t k = orc_collapse3(as_, ast2, bst2, ost, od, 0x7FFFFFFFu, cs, ca, cb, cr);
+    const uint64_t n = total(std::vector<size_m>(os, os + od));
+    std::vector<uint8_t> out(std::max<uint64_t>(n, 1) * sizeof(T));
+    orc_broadcast(op, dtype_code, out.data(), a.data(), b.data(), k, cr, ca, cb, n, 1);
+    out.resize(n * sizeof(T));
+    return out;
+}
+
+static bool same_bits_f32(const std::vector<uint8_t>& g, const std::vector<uint8_t>& c) {
+    if (g.size() != c.size()) return false;
+    const float* x = reinterpret_cast<const float*>(g.data());
+    const float* y = reinterpret_cast<const float*>(c.data());
+    for (size_t i = 0; i < g.size() / 4; ++i) {
+        if (std::isnan(x[i]) && std::isnan(y[i])) continue;
+        if (std::memcmp(&x[i], &y[i], 4) != 0) return false;
+    }
+    return true;
+}
+
+static std::vector<float> random_ties(size_t n, std::mt19937& rng) {
+    std::normal_distribution<float> d(0.f, 1.f);
+    std::vector<float> v(n);
+    for (auto& x : v) x = std::floor(d(rng) * 8.f) / 8.f;
+    return v;
+}
+
+static void test_reductions(std::mt19937& rng) {
+    std::vector<size_m> shape = {4, 37, 129};
+    std::vector<float> host = random_ties(total(shape), rng);
+    host[5] = NAN;
+    matrix x = matrix::from_host(host.data(), shape, dtype::Float);
+    for (int op = 0; op < 5; ++op) {
+        for (int axis = 0; axis < 3; ++axis) {
+            for (bool keep : {false, true}) {
+                matrix y;
+                switch (op) {
+                    case 0: y = x.sum(axis, keep); break;
+                    case 1: y = x.max(axis, keep); break;
+                    case 2: y = x.min(axis, keep); break;
+                    case 3: y = x.argmax(axis, keep); break;
+                    default: y = x.argmin(axis, keep); break;
+                }
+                y.eval();
+                std::vector<uint8_t> g = y.to_host_bytes();
+                std::vector<uint8_t> c = oracle_reduce(op, host, shape, x.strides(), axis, keep, 0);
+                if (op == 0) {
+                    const float* gf = reinterpret_cast<const float*>(g.data());
+                    const float* cf = reinterpret_cast<const float*>(c.data());
+                    bool ok = g.size() == c.size();
+                    for (size_t i = 0; ok && i < c.size() / 4; ++i)
+                        ok = (std::isnan(gf[i]) && std::isnan(cf[i])) || std::fabs(gf[i] - cf[i]) <= 1e-3f;
+                    EXPECT(ok, "sum axis %d keep %d", axis, keep);
+                } else {
+                    EXPECT(same_bits_f32(g, c), "reduce op %d axis %d keep %d", op, axis, keep);
+                }
+                const std::vector<size_m>& s = y.shape();
+                EXPECT(s.size() == (keep ? 3u : 2u), "output rank");
+            }
+        }
+    }
+    // a transposed view (strided input) and a full reduction
+    matrix xt = x.transpose(0, 2);
+    matrix yt = xt.argmax(1);
+    yt.eval();
+    EXPECT(yt.to_host_bytes() == oracle_reduce(3, host, xt.shape(), xt.strides(), 1, false, 0), "argmax of a transpose");
+    matrix all = x.max(0).max(0).max(0);
+    all.eval();
+    std::vector<float> a = all.to_host<float>();
+    float ref = -3.4e38f;
+    for (float v : host) ref = (ref < v) ? v : ref;
+    EXPECT(a.size() == 1 && a[0] == ref, "global max");
+    std::vector<int32_t> ih(total(shape));
+    for (auto& v : ih) v = (int32_t)(rng() & 0x7FFFFFFF) - (1 << 30);
+    matrix xi = matrix::from_host(ih.data(), shape, dtype::Int32);
+    matrix si = xi.sum();
+    si.eval();
+    int32_t want = 0;
+    for (auto v : ih) want = (int32_t)((uint32_t)want + (uint32_t)v);
+    EXPECT(si.to_host<int32_t>()[0] == want, "int32 full sum wraps like the reference");
+}
+
+static void test_binary(std::mt19937& rng) {
+    std::vector<size_m> ash = {4, 1, 129}, bsh = {1, 37, 129};
+    std::vector<float> a = random_ties(total(ash), rng), b = random_ties(total(bsh), rng);
+    for (auto& v : b)
+        if (v == 0.f) v = 0.5f;
+    matrix A = matrix::from_host(a.data(), ash, dtype::Float);
+    matrix B = matrix::from_host(b.data(), bsh, dtype::Float);
+    matrix r[6] = {A + B, A - B, A * B, A / B, matrix::max(A, B), matrix::min(A, B)};
+    for (int op = 0; op < 6; ++op) {
+        r[op].eval();
+        EXPECT(r[op].shape() == std::vector<size_m>({4, 37, 129}), "broadcast shape");
+        EXPECT(same_bits_f32(r[op].to_host_bytes(), oracle_binary(op, a, ash, b, bsh, 0)), "binary op %d", op);
+    }
+    std::vector<int32_t> ia(total(ash)), ib(total(bsh));
+    for (auto& v : ia) v = (int32_t)rng();
+    for (auto& v : ib) v = (int32_t)(rng() | 1);
+    matrix IA = matrix::from_host(ia.data(), ash, dtype::Int32), IB = matrix::from_host(ib.data(), bsh, dtype::Int32);
+    matrix prod = IA * IB;
+    prod.eval();
+    EXPECT(prod.to_host_bytes() == oracle_binary(2, ia, ash, ib, bsh, 3), "int32 mul wraps");
+    // incompatible shapes throw std::invalid_argument, as Matrix.mm:220 does
+    bool threw = false;
+    try {
+        std::vector<float> c(5 * 7);
+        matrix C = matrix::from_host(c.data(), {5, 7}, dtype::Float);
+        matrix bad = C + B;
+    } catch (const std::invalid_argument&) {
+        threw = true;
+    }
+    EXPECT(threw, "incompatible broadcast throws invalid_argument");
+    threw = false;
+    try {
+        matrix bad = A.sum(3);
+    } catch (const std::invalid_argument&) {
+        threw = true;
+    }
+    EXPECT(threw, "axis out of range throws invalid_argument");
+}
+
+// the softmax trace, unfused (eval) and fused (compile + execute), with the leaf changed between
+// executes (the recorded graph is replayed on the new data)
+static void test_trace(std::mt19937& rng) {
+    const std::vector<size_m> shape = {64, 4096};
+    std::vector<float> host(total(shape));
+    std::normal_distribution<float> d(0.f, 2.f);
+    for (auto& v : host) v = d(rng);
+    matrix x = matrix::from_host(host.data(), shape, dtype::Float);
+    auto build = [](const matrix& in) {
+        matrix m = in.max(-1, true);
+        matrix e = matrix::exp(in - m);
+        return e / e.sum(-1, true);
+    };
+    auto reference = [&](const std::vector<float>& h) {
+        std::vector<float> y(h.size());
+        for (size_t r = 0; r < shape[0]; ++r) {
+            const float* row = &h[r * shape[1]];
+            float m = -3.4e38f;
+            for (size_t c = 0; c < shape[1]; ++c) m = (m < row[c]) ? row[c] : m;
+            double s = 0;
+            for (size_t c = 0; c < shape[1]; ++c) s += std::exp((double)row[c] - m);
+            for (size_t c = 0; c < shape[1]; ++c) y[r * shape[1] + c] = (float)(std::exp((double)row[c] - m) / s);
+        }
+        return y;
+    };
+    auto close = [](const std::vector<float>& g, const std::vector<float>& c) {
+        if (g.size() != c.size()) return false;
+        for (size_t i = 0; i < g.size(); ++i)
+            if (!(std::fabs(g[i] - c[i]) <= 1e-5f * std::fabs(c[i]) + 1e-30f)) return false;
+        return true;
+    };
+    matrix unfused = build(x);
+    unfused.eval();
+    EXPECT(std::string(unfused.tape()->name()) == "Division", "eval() keeps the five primitives");
+    EXPECT(close(unfused.to_host<float>(), reference(host)), "unfused softmax trace");
+
+    matrix fused = build(x);
+    fused.compile();
+    EXPECT(std::string(fused.tape()->name()) == "FusedSoftmax", "compile() fuses the softmax trace");
+    fused.execute();
+    EXPECT(close(fused.to_host<float>(), reference(host)), "fused softmax, first execute");
+    for (auto& v : host) v = d(rng);
+    x.upload(host.data());
+    fused.execute();  // replays the recorded graph on the new leaf contents
+    EXPECT(close(fused.to_host<float>(), reference(host)), "fused softmax, replayed graph");
+
+    // a reduction graph compiled once, executed twice
+    std::vector<size_m> bsh = {1, 4096};
+    std::vector<float> bias(4096, 0.25f);
+    matrix b = matrix::from_host(bias.data(), bsh, dtype::Float);
+    matrix z = (x + b).sum(1);
+    z.compile();
+    z.execute();
+    z.execute();
+    std::vector<float> zs = z.to_host<float>();
+    bool ok = zs.size() == shape[0];
+    for (size_t r = 0; ok && r < shape[0]; ++r) {
+        double s = 0, abs = 0;
+        for (size_t c = 0; c < shape[1]; ++c) {
+            const float v = host[r * shape[1] + c] + 0.25f;
+            s += v;
+            abs += std::fabs(v);
+        }
+        ok = std::fabs(zs[r] - s) <= 1e-5 * abs;
+    }
+    EXPECT(ok, "compiled reduction graph");
+}
+
+int main() {
+    mtx::init(0);
+    std::mt19937 rng(1234);
+    test_reductions(rng);
+    test_binary(rng);
+    test_trace(rng);
+    std::printf("host mirror: %d checks, %d failures\n", checks, failures);
+    return failures ? 1 : 0;
+}
