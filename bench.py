@@ -66,12 +66,15 @@ def measured_peak():
 
 
 def profile_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
-    p = REPO / "profiles" / "broadcast_rows_c2.json"
+    """DRAM bytes (read + write) per launch of the dominant kernel, from the committed ncu summary."""
+    p = REPO / "profiles" / "broadcast_rows_c2_traffic.txt"
     try:
-        return float(json.loads(p.read_text())["dram_bytes_per_launch"])
-    except Exception:
-        return None
+        for line in p.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
 
 
 # ------------------------------------------------------------------------------------------
@@ -403,7 +406,8 @@ def run_ours(args):
         if args.suite:
             from matrix_b200 import suite
 
-            for extra in suite.run_all(dev, stream):
+            cfgs = args.suite_configs.split(",") if args.suite_configs else None
+            for extra in suite.run_all(dev, stream, cfgs, args.suite_scale):
                 print(json.dumps(extra), flush=True)
     if world > 1:
         dist.barrier()
@@ -510,6 +514,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--suite", action="store_true", help="also time the other BASELINE configs")
+    ap.add_argument("--suite-configs", default="", help="comma-separated subset of C1,C3,C4,C5a,C5b")
+    ap.add_argument("--suite-scale", type=int, default=1, help="divide the configs' leading extent (small cases)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--rows", type=int, default=256, help="leading rows of a per rank (256 = C2; smaller for ncu)")

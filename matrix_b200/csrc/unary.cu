@@ -22,7 +22,9 @@ struct UnaryRows {
     uint32_t vec_per_row;
     uint32_t seg_vecs;  // vectors per work unit (rows are cut into segments of this size)
     uint32_t segs;      // segments per row
+    uint32_t units;     // rows * segs (< 2^31)
     uint32_t tpr;
+    FastDiv seg_div;    // divides a unit index by segs
     Dims d;  // outer axes: shape (fast divisors), dst strides in s0, src strides in s1
 };
 
@@ -30,13 +32,12 @@ __global__ void __launch_bounds__(kBlock) exp_rows_kernel(const UnaryRows a) {
     const uint32_t rows_per_block = kBlock / a.tpr;
     const uint32_t sub = threadIdx.x / a.tpr;
     const uint32_t lane = threadIdx.x % a.tpr;
-    const uint64_t units = (uint64_t)a.rows * a.segs;
-    for (uint64_t u = (uint64_t)blockIdx.x * rows_per_block + sub; u < units; u += (uint64_t)gridDim.x * rows_per_block) {
-        const uint64_t row = u / a.segs;
-        const uint32_t seg = (uint32_t)(u - row * a.segs);
+    for (uint32_t u = blockIdx.x * rows_per_block + sub; u < a.units; u += gridDim.x * rows_per_block) {
+        uint32_t row = u, seg = 0;
+        if (a.segs > 1) a.seg_div.divmod(u, row, seg);
         const uint32_t c_end = min(a.vec_per_row, (seg + 1) * a.seg_vecs);
         uint64_t od = 0, os = 0;
-        uint32_t rem = (uint32_t)row;
+        uint32_t rem = row;
 #pragma unroll 1
         for (int i = (int)a.d.n - 1; i >= 0; --i) {
             uint32_t q, idx;
@@ -92,7 +93,7 @@ int launch_exp(float* dst, const float* src, uint32_t cdims, const uint32_t* sha
     if (total == 0) return MTXC_OK;
     const uint32_t k = cdims - 1;
     bool rows_ok = sd[k] == 1 && ss[k] == 1 && shape[k] % 4 == 0 && aligned16(dst) && aligned16(src) &&
-                   total / shape[k] < (1ull << 32);
+                   (total / shape[k]) * ((shape[k] / 4 + kSegVecs - 1) / kSegVecs) < (1ull << 31);
     for (uint32_t i = 0; i < k && rows_ok; ++i) rows_ok = shape[i] == 1 || (sd[i] % 4 == 0 && ss[i] % 4 == 0);
     if (rows_ok) {
         UnaryRows a{};
@@ -102,6 +103,7 @@ int launch_exp(float* dst, const float* src, uint32_t cdims, const uint32_t* sha
         a.vec_per_row = shape[k] / 4;
         a.seg_vecs = std::min<uint32_t>(a.vec_per_row, kSegVecs);
         a.segs = (a.vec_per_row + a.seg_vecs - 1) / a.seg_vecs;
+        a.seg_div = FastDiv(a.segs);
         uint32_t tpr = 1;
         while (tpr < a.seg_vecs && tpr < (uint32_t)kBlock) tpr <<= 1;
         a.tpr = tpr;
@@ -114,6 +116,7 @@ int launch_exp(float* dst, const float* src, uint32_t cdims, const uint32_t* sha
         }
         const uint32_t rpb = kBlock / tpr;
         const uint64_t units = (uint64_t)a.rows * a.segs;
+        a.units = (uint32_t)units;
         const uint64_t blocks = std::min<uint64_t>((units + rpb - 1) / rpb, (uint64_t)sm_count * 8);
         exp_rows_kernel<<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         return check_launch("exp_rows_kernel");

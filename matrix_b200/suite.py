@@ -52,12 +52,30 @@ def _line(name, workload, nbytes, ms, peak, **extra):
     return d
 
 
-def run_all(dev, stream):
+def run_all(dev, stream, configs=None, scale=1):
+    """configs: names to run (default all: C1 C3 C4 C5a C5b); scale: divide each config's leading
+    extent by this (small cases for profiling)."""
     peak = _peak()
     g = torch.Generator(device=dev)
     out = []
+    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b"}
 
     # C1: Sum over the last axis of f32 [1024, 4096] ~ N(0,1)
+    if "C1" in want:
+        _c1(out, dev, stream, g, peak)
+    if "C3" in want:
+        _c3(out, dev, stream, g, peak, scale)
+    if "C4" in want:
+        _c4(out, dev, stream, g, peak, scale)
+    if "C5a" in want:
+        _c5a(out, dev, stream, g, peak, scale)
+    if "C5b" in want:
+        _c5b(out, dev, stream, g, peak, scale)
+    torch.cuda.empty_cache()
+    return out
+
+
+def _c1(out, dev, stream, g, peak):
     g.manual_seed(0)
     x = torch.randn(1024, 4096, generator=g, device=dev)
     y = torch.empty(1024, device=dev)
@@ -71,27 +89,36 @@ def run_all(dev, stream):
                      peak))
     del x, y, scratch
 
+
+def _c3(out, dev, stream, g, peak, scale):
     # C3: Max and ArgMax along axis 1 of f32 [64, 8192, 1024], values k/256
+    b0 = max(1, 64 // scale)
     g.manual_seed(2)
-    x = torch.floor(torch.rand(64, 8192, 1024, generator=g, device=dev) * 256) / 256
-    m = backend.reduce_meta([64, 8192, 1024], list(x.stride()), 1)
-    vmax = torch.empty(64, 1024, device=dev)
-    imax = torch.empty(64, 1024, dtype=torch.int32, device=dev)
-    nbytes = 64 * 8192 * 1024 * 4 + 64 * 1024 * 4
+    x = torch.floor(torch.rand(b0, 8192, 1024, generator=g, device=dev) * 256) / 256
+    m = backend.reduce_meta([b0, 8192, 1024], list(x.stride()), 1)
+    vmax = torch.empty(b0, 1024, device=dev)
+    imax = torch.empty(b0, 1024, dtype=torch.int32, device=dev)
+    nbytes = b0 * 8192 * 1024 * 4 + b0 * 1024 * 4
     ms = _time(lambda: backend.reduce("max", x, 1, out=vmax, meta=m), stream)
     out.append(_line("C3-max", "Max(axis=1) f32 [64,8192,1024]", nbytes, ms, peak))
     ms = _time(lambda: backend.reduce("argmax", x, 1, out=imax, meta=m), stream)
     out.append(_line("C3-argmax", "ArgMax(axis=1) f32 [64,8192,1024]", nbytes, ms, peak))
+    ms = _time(lambda: backend.reduce_pair("max", x, 1, meta=m), stream)
+    out.append(_line("C3-max+argmax", "Max and ArgMax(axis=1) from one read (mtxc_reduce_pair)", nbytes + b0 * 1024 * 4,
+                     ms, peak, ops_served=2))
     del x
 
+
+def _c4(out, dev, stream, g, peak, scale):
     # C4: Sum over axes (0, 2) of [32, 4096, 2048], f32 N(0,1) and i32 U{-1000..1000}
+    b0 = max(1, 32 // scale)
     g.manual_seed(3)
-    for name, x in (("C4-f32", torch.randn(32, 4096, 2048, generator=g, device=dev)),
-                    ("C4-i32", torch.randint(-1000, 1001, (32, 4096, 2048), generator=g, device=dev,
+    for name, x in (("C4-f32", torch.randn(b0, 4096, 2048, generator=g, device=dev)),
+                    ("C4-i32", torch.randint(-1000, 1001, (b0, 4096, 2048), generator=g, device=dev,
                                              dtype=torch.int32))):
-        m2 = backend.reduce_meta([32, 4096, 2048], list(x.stride()), 2)
-        mid = torch.empty(32, 4096, dtype=x.dtype, device=dev)
-        m0 = backend.reduce_meta([32, 4096], [4096, 1], 0)
+        m2 = backend.reduce_meta([b0, 4096, 2048], list(x.stride()), 2)
+        mid = torch.empty(b0, 4096, dtype=x.dtype, device=dev)
+        m0 = backend.reduce_meta([b0, 4096], [4096, 1], 0)
         fin = torch.empty(4096, dtype=x.dtype, device=dev)
 
         def c4():
@@ -99,19 +126,22 @@ def run_all(dev, stream):
             backend.reduce("sum", mid, 0, out=fin, meta=m0)
 
         ms = _time(c4, stream)
-        out.append(_line(name, "x.sum(2).sum(0) [32,4096,2048]", 32 * 4096 * 2048 * 4 + 4096 * 4, ms, peak,
-                         moved_bytes=32 * 4096 * 2048 * 4 + 2 * 32 * 4096 * 4 + 4096 * 4))
+        out.append(_line(name, "x.sum(2).sum(0) [32,4096,2048]", b0 * 4096 * 2048 * 4 + 4096 * 4, ms, peak,
+                         moved_bytes=b0 * 4096 * 2048 * 4 + 2 * b0 * 4096 * 4 + 4096 * 4))
         del x, mid
 
+
+def _c5a(out, dev, stream, g, peak, scale):
     # C5a: softmax trace on f32 [8192, 32768] ~ N(0, 4): max, sub, exp, sum, div (5 kernels)
+    rows = max(1, 8192 // scale)
     g.manual_seed(4)
-    x = torch.randn(8192, 32768, generator=g, device=dev) * 2
-    mx = torch.empty(8192, 1, device=dev)
+    x = torch.randn(rows, 32768, generator=g, device=dev) * 2
+    mx = torch.empty(rows, 1, device=dev)
     t = torch.empty_like(x)
-    s = torch.empty(8192, 1, device=dev)
-    mm = backend.reduce_meta([8192, 32768], [32768, 1], -1, True)
-    msub = backend.binary_meta([8192, 32768], [32768, 1], [8192, 1], [1, 1])
-    mexp = backend.unary_meta([8192, 32768], [32768, 1])
+    s = torch.empty(rows, 1, device=dev)
+    mm = backend.reduce_meta([rows, 32768], [32768, 1], -1, True)
+    msub = backend.binary_meta([rows, 32768], [32768, 1], [rows, 1], [1, 1])
+    mexp = backend.unary_meta([rows, 32768], [32768, 1])
     mdiv = msub
 
     def trace():
@@ -122,7 +152,7 @@ def run_all(dev, stream):
         backend.binary("div", t, s, out=t, meta=mdiv)
 
     ms = _time(trace, stream)
-    n = 8192 * 32768 * 4
+    n = rows * 32768 * 4
     out.append(_line("C5a-trace", "softmax trace max,sub,exp,sum,div f32 [8192,32768] (5 kernels)", 2 * n, ms, peak,
                      moved_bytes=8 * n))
     ms = _time(lambda: backend.softmax_lastdim(x, out=t), stream)
@@ -130,12 +160,15 @@ def run_all(dev, stream):
                      moved_bytes=2 * n))
     del x, t
 
+
+def _c5b(out, dev, stream, g, peak, scale):
     # C5b: full Sum of 2^32 f32 ~ N(0,1) as [8, 2^29] (16 GiB): sum(1) then sum(0)
+    cols = (1 << 29) // scale
     g.manual_seed(5)
-    x = torch.randn(8, 1 << 29, generator=g, device=dev)
+    x = torch.randn(8, cols, generator=g, device=dev)
     r1 = torch.empty(8, device=dev)
     r0 = torch.empty((), device=dev)
-    m1 = backend.reduce_meta([8, 1 << 29], [1 << 29, 1], 1)
+    m1 = backend.reduce_meta([8, cols], [cols, 1], 1)
     m0 = backend.reduce_meta([8], [1], 0)
 
     def c5b():
@@ -143,7 +176,5 @@ def run_all(dev, stream):
         backend.reduce("sum", r1, 0, out=r0, meta=m0)
 
     ms = _time(c5b, stream, reps=5)
-    out.append(_line("C5b", "full Sum f32 2^32 as [8,2^29] (1 GPU)", 16 * GiB, ms, peak))
+    out.append(_line("C5b", "full Sum f32 2^32 as [8,2^29] (1 GPU)", 8 * cols * 4, ms, peak))
     del x
-    torch.cuda.empty_cache()
-    return out
