@@ -130,13 +130,16 @@ struct alignas(16) Vec16 {
     T v[N];
 };
 
-// Streaming read that bypasses L1 (data read once).
+// Streaming read that bypasses L1 (data read once).  Not volatile: the compiler may schedule it
+// freely, e.g. hoist several loads ahead of their first use.  Every kernel here reads an element
+// before anything writes it (in-place exp writes an element only with a value computed from its own
+// load), so no ordering against stores is needed.
 template <typename T>
 __device__ __forceinline__ Vec16<T> load_stream(const T* p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
     Vec16<T> out;
     memcpy(&out, &r, 16);
     return out;

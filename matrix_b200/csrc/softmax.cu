@@ -43,7 +43,9 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-template <int C, int VPT>
+// FULL: the row fills the cluster exactly (row_len == C * 256 * 4 * VPT), so no vector needs a bounds
+// predicate.
+template <int C, int VPT, bool FULL>
 __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
     softmax_rows_kernel(float* __restrict__ dst, const float* __restrict__ src, uint32_t row_len,
                         uint64_t src_row_stride, uint64_t dst_row_stride) {
@@ -60,19 +62,26 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
     // vectors of this thread: rank * (256 * VPT) + k * 256 + threadIdx.x, k < VPT (coalesced per k)
+    // all VPT loads are issued before any is used, so each thread keeps VPT 16-byte loads in flight
     float4 v[VPT];
-    float m = lowest_value<float>();
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const uint32_t c = rank * (kThreads * VPT) + k * kThreads + threadIdx.x;
-        if (c < nvec) {
+        if (FULL || c < nvec) {
             const Vec16<float> t = load_stream(x + (uint64_t)c * 4);
             v[k] = make_float4(t.v[0], t.v[1], t.v[2], t.v[3]);
-            m = (m < v[k].x) ? v[k].x : m;
-            m = (m < v[k].y) ? v[k].y : m;
-            m = (m < v[k].z) ? v[k].z : m;
-            m = (m < v[k].w) ? v[k].w : m;
+        } else {
+            v[k] = make_float4(lowest_value<float>(), lowest_value<float>(), lowest_value<float>(),
+                               lowest_value<float>());
         }
+    }
+    float m = lowest_value<float>();
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        m = (m < v[k].x) ? v[k].x : m;
+        m = (m < v[k].y) ? v[k].y : m;
+        m = (m < v[k].z) ? v[k].z : m;
+        m = (m < v[k].w) ? v[k].w : m;
     }
     m = warp_max(m);
     if (lane == 0) warp_part[warp] = m;
@@ -94,7 +103,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const uint32_t c = rank * (kThreads * VPT) + k * kThreads + threadIdx.x;
-        if (c < nvec) {
+        if (FULL || c < nvec) {
             v[k].x = expf(__fsub_rn(v[k].x, m));
             v[k].y = expf(__fsub_rn(v[k].y, m));
             v[k].z = expf(__fsub_rn(v[k].z, m));
@@ -119,7 +128,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const uint32_t c = rank * (kThreads * VPT) + k * kThreads + threadIdx.x;
-        if (c < nvec) {
+        if (FULL || c < nvec) {
             Vec16<float> o;
             o.v[0] = __fdiv_rn(v[k].x, s);
             o.v[1] = __fdiv_rn(v[k].y, s);
@@ -142,18 +151,24 @@ __global__ void __launch_bounds__(kThreads) softmax_warp_rows_kernel(float* __re
         const float* x = src + row * src_row_stride;
         float* y = dst + row * dst_row_stride;
         float4 v[VPL];
-        float m = lowest_value<float>();
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
             const uint32_t c = k * 32 + lane;
             if (c < nvec) {
                 const Vec16<float> t = load_stream(x + (uint64_t)c * 4);
                 v[k] = make_float4(t.v[0], t.v[1], t.v[2], t.v[3]);
-                m = (m < v[k].x) ? v[k].x : m;
-                m = (m < v[k].y) ? v[k].y : m;
-                m = (m < v[k].z) ? v[k].z : m;
-                m = (m < v[k].w) ? v[k].w : m;
+            } else {
+                v[k] = make_float4(lowest_value<float>(), lowest_value<float>(), lowest_value<float>(),
+                                   lowest_value<float>());
             }
+        }
+        float m = lowest_value<float>();
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            m = (m < v[k].x) ? v[k].x : m;
+            m = (m < v[k].y) ? v[k].y : m;
+            m = (m < v[k].z) ? v[k].z : m;
+            m = (m < v[k].w) ? v[k].w : m;
         }
         m = warp_max(m);
         float s = 0.0f;
@@ -196,7 +211,10 @@ int launch_softmax(float* dst, const float* src, uint64_t rows, uint32_t len, ui
                    cudaStream_t stream) {
     const uint64_t blocks = rows * C;
     if (blocks >= (1ull << 31)) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_softmax_lastdim: too many rows");
-    softmax_rows_kernel<C, VPT><<<(unsigned)blocks, kThreads, 0, stream>>>(dst, src, len, ss, ds);
+    if (len == (uint32_t)C * kThreads * 4 * VPT)
+        softmax_rows_kernel<C, VPT, true><<<(unsigned)blocks, kThreads, 0, stream>>>(dst, src, len, ss, ds);
+    else
+        softmax_rows_kernel<C, VPT, false><<<(unsigned)blocks, kThreads, 0, stream>>>(dst, src, len, ss, ds);
     return check_launch("softmax_rows_kernel");
 }
 

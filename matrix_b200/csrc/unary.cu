@@ -48,8 +48,20 @@ __global__ void __launch_bounds__(kBlock) exp_rows_kernel(const UnaryRows a) {
         }
         const float* ps = a.src + os;
         float* pd = a.dst + od;
-#pragma unroll 4
-        for (uint32_t c = seg * a.seg_vecs + lane; c < c_end; c += a.tpr) {
+        uint32_t c = seg * a.seg_vecs + lane;
+        // four loads in flight per thread before the first is used
+        for (; c + 3 * a.tpr < c_end; c += 4 * a.tpr) {
+            Vec16<float> x[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[k] = load_stream(ps + (uint64_t)(c + k * a.tpr) * 4);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) x[k].v[j] = expf(x[k].v[j]);
+                store_stream(pd + (uint64_t)(c + k * a.tpr) * 4, x[k]);
+            }
+        }
+        for (; c < c_end; c += a.tpr) {
             Vec16<float> x = load_stream(ps + (uint64_t)c * 4);
 #pragma unroll
             for (int j = 0; j < 4; ++j) x.v[j] = expf(x.v[j]);
