@@ -189,7 +189,10 @@ int mtxc_promote_types(int a, int b);
  * dtype_lowest / dtype_max, and never select NaN; ArgMax / ArgMin write int32 indices, the
  * first one on ties, 0 when no element beats the initial value.  Float sums are summed in a
  * different order (tree instead of sequential), so they agree within rounding.
- * dtypes: float, int32, uint32, int64, uint64, int16, uint16, int8, uint8. */
+ * dtypes: every reference dtype except Complex64 (MTXC_ERR_UNSUPPORTED_DTYPE): float, float16,
+ * bfloat16, bool and the eight integer types.  Float16 / BFloat16 sums accumulate in fp32 and round
+ * once, where the reference rounds every partial sum to the half type; Bool sums are a logical or
+ * (C++ bool arithmetic). */
 int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
                 uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides, const uint32_t* src_strides);
 
@@ -251,6 +254,8 @@ int mtxc_reduce_noalloc(int op, int dtype, void* dst, const void* src, uint32_t 
  * are bit-exact with the reference CPU (one IEEE-rounded op per element, no contraction);
  * Max / Min keep `a` unless `b` is strictly greater / smaller (std::max / std::min).
  * Integer results wrap; integer division by zero is undefined, as in the reference.
+ * Float16 / BFloat16 ops compute in fp32 and round once, which is the correctly rounded half result
+ * (bit-exact with the reference CPU); Bool follows C++ bool arithmetic.
  * Both operands have dtype `dtype` (the reference promotes with astype first). */
 int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, const void* b, uint32_t cdims,
                           const uint32_t* shape, const uint32_t* r_strides, const uint32_t* a_strides,

@@ -20,8 +20,8 @@ UINT32_MAX = 0xFFFFFFFF
 INT32_MAX = 0x7FFFFFFF
 
 TORCH_DTYPES = {
-    torch.float32: 0, torch.uint8: 2, torch.int32: 3, torch.int16: 4, torch.uint32: 5,
-    torch.uint16: 6, torch.int8: 8, torch.int64: 11, torch.uint64: 12,
+    torch.float32: 0, torch.float16: 1, torch.uint8: 2, torch.int32: 3, torch.int16: 4, torch.uint32: 5,
+    torch.uint16: 6, torch.bool: 7, torch.int8: 8, torch.bfloat16: 10, torch.int64: 11, torch.uint64: 12,
 }
 
 

@@ -35,12 +35,16 @@ __global__ void __launch_bounds__(kBlock) merge_partials_kernel(const MergeArgs 
     for (uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < a.outputs;
          gid += (uint64_t)gridDim.x * blockDim.x) {
         if constexpr (OP == MTXC_REDUCE_SUM) {
-            if constexpr (std::is_same_v<T, float>) {
-                float s = v[gid];
-                for (uint32_t p = 1; p < a.parts; ++p) s = __fadd_rn(s, v[(uint64_t)p * a.outputs + gid]);
-                static_cast<T*>(a.dst)[gid] = s;
+            if constexpr (Traits<T>::kFloat) {
+                float s = to_float(v[gid]);
+                for (uint32_t p = 1; p < a.parts; ++p) s = __fadd_rn(s, to_float(v[(uint64_t)p * a.outputs + gid]));
+                static_cast<T*>(a.dst)[gid] = from_float<T>(s);
+            } else if constexpr (Traits<T>::kBool) {
+                bool s = false;
+                for (uint32_t p = 0; p < a.parts; ++p) s = s || (uint8_t)v[(uint64_t)p * a.outputs + gid];
+                static_cast<T*>(a.dst)[gid] = mbool(s);
             } else {
-                using W = std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>;
+                using W = typename Traits<T>::Acc;
                 W s = (W)v[gid];
                 for (uint32_t p = 1; p < a.parts; ++p) s = (W)(s + (W)v[(uint64_t)p * a.outputs + gid]);
                 static_cast<T*>(a.dst)[gid] = (T)s;
@@ -51,7 +55,7 @@ __global__ void __launch_bounds__(kBlock) merge_partials_kernel(const MergeArgs 
             uint32_t from = 0;
             for (uint32_t p = 1; p < a.parts; ++p) {
                 const T x = v[(uint64_t)p * a.outputs + gid];
-                if (kMax ? (best < x) : (x < best)) {
+                if (kMax ? less(best, x) : less(x, best)) {
                     best = x;
                     from = p;
                 }

@@ -2,6 +2,8 @@
 // error reporting, dtype dispatch, 32-bit fast division and the 128-bit memory helpers.
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstring>
@@ -38,12 +40,69 @@ int require_init();
 int check_launch(const char* what);
 
 // ------------------------------------------------------------------------------------------
-// dtype dispatch.  The functor receives a null pointer of the element type.
+// Element types.  The reference's Bool (dtype 7) is a 1-byte 0/1 value with C++ bool semantics: a
+// scoped enum over uint8 keeps it distinct from UInt8 in every template below.
 // ------------------------------------------------------------------------------------------
+enum class mbool : uint8_t {};
+
+template <typename T>
+struct Traits {  // integers
+    static constexpr bool kFloat = false, kBool = false;
+    using Acc = std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>;  // wrap-around accumulator
+};
+template <>
+struct Traits<float> {
+    static constexpr bool kFloat = true, kBool = false;
+    using Acc = float;
+};
+template <>
+struct Traits<__half> {
+    static constexpr bool kFloat = true, kBool = false;
+    using Acc = float;
+};
+template <>
+struct Traits<__nv_bfloat16> {
+    static constexpr bool kFloat = true, kBool = false;
+    using Acc = float;
+};
+template <>
+struct Traits<mbool> {
+    static constexpr bool kFloat = false, kBool = true;
+    using Acc = uint32_t;
+};
+
+// Exact widening of a float-like element to float (identity for float).
+template <typename T>
+__host__ __device__ __forceinline__ float to_float(T v) {
+    if constexpr (std::is_same_v<T, float>) return v;
+    else if constexpr (std::is_same_v<T, __half>) return __half2float(v);
+    else return __bfloat162float(v);
+}
+// Round-to-nearest-even narrowing of a float to a float-like element.
+template <typename T>
+__host__ __device__ __forceinline__ T from_float(float v) {
+    if constexpr (std::is_same_v<T, float>) return v;
+    else if constexpr (std::is_same_v<T, __half>) return __float2half_rn(v);
+    else return __float2bfloat16_rn(v);
+}
+// a < b in the element's own order (float-likes compare as floats: exact, NaN is unordered).
+template <typename T>
+__host__ __device__ __forceinline__ bool less(T a, T b) {
+    if constexpr (Traits<T>::kFloat) return to_float(a) < to_float(b);
+    else return a < b;
+}
+template <typename T>
+__host__ __device__ __forceinline__ bool equal(T a, T b) {
+    if constexpr (Traits<T>::kFloat) return to_float(a) == to_float(b);
+    else return a == b;
+}
+
 template <typename Fn>
 bool dispatch_dtype(int dtype, Fn&& fn) {
     switch (dtype) {
         case MTXC_FLOAT: fn((float*)nullptr); return true;
+        case MTXC_FLOAT16: fn((__half*)nullptr); return true;
+        case MTXC_BFLOAT16: fn((__nv_bfloat16*)nullptr); return true;
         case MTXC_INT32: fn((int32_t*)nullptr); return true;
         case MTXC_UINT32: fn((uint32_t*)nullptr); return true;
         case MTXC_INT64: fn((int64_t*)nullptr); return true;
@@ -52,21 +111,29 @@ bool dispatch_dtype(int dtype, Fn&& fn) {
         case MTXC_UINT16: fn((uint16_t*)nullptr); return true;
         case MTXC_INT8: fn((int8_t*)nullptr); return true;
         case MTXC_UINT8: fn((uint8_t*)nullptr); return true;
+        case MTXC_BOOL: fn((mbool*)nullptr); return true;
         default: return false;
     }
 }
 const char* dtype_name(int dtype);
 
-// Smallest / largest finite value: dtype_lowest / dtype_max (matrix.h:271-282).
+// Smallest / largest finite value: dtype_lowest / dtype_max (matrix.h:271-282), with the half types'
+// finite extremes (+-65504, +-0x1.fep127) and bool's false / true.
 template <typename T>
-__host__ __device__ constexpr T lowest_value() {
+__host__ __device__ inline T lowest_value() {
     if constexpr (std::is_same_v<T, float>) return -3.402823466e+38f;
+    else if constexpr (std::is_same_v<T, __half>) return __ushort_as_half((unsigned short)0xFBFFu);
+    else if constexpr (std::is_same_v<T, __nv_bfloat16>) return __ushort_as_bfloat16((unsigned short)0xFF7Fu);
+    else if constexpr (std::is_same_v<T, mbool>) return mbool(0);
     else if constexpr (std::is_signed_v<T>) return T(T(1) << (sizeof(T) * 8 - 1));
     else return T(0);
 }
 template <typename T>
-__host__ __device__ constexpr T highest_value() {
+__host__ __device__ inline T highest_value() {
     if constexpr (std::is_same_v<T, float>) return 3.402823466e+38f;
+    else if constexpr (std::is_same_v<T, __half>) return __ushort_as_half((unsigned short)0x7BFFu);
+    else if constexpr (std::is_same_v<T, __nv_bfloat16>) return __ushort_as_bfloat16((unsigned short)0x7F7Fu);
+    else if constexpr (std::is_same_v<T, mbool>) return mbool(1);
     else if constexpr (std::is_signed_v<T>) return T(~(T(1) << (sizeof(T) * 8 - 1)));
     else return T(~T(0));
 }

@@ -49,10 +49,6 @@ struct Pair {
 };
 
 template <typename T>
-using SumAcc = std::conditional_t<std::is_same_v<T, float>, float,
-                                  std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>>;
-
-template <typename T>
 __device__ __forceinline__ T shfl_xor(T v, int mask) {
     if constexpr (sizeof(T) == 8) {
         unsigned long long x;
@@ -61,18 +57,14 @@ __device__ __forceinline__ T shfl_xor(T v, int mask) {
         T r;
         memcpy(&r, &x, 8);
         return r;
-    } else if constexpr (sizeof(T) == 4) {
-        unsigned x;
-        memcpy(&x, &v, 4);
+    } else {
+        // 1-, 2- and 4-byte values travel in the low bytes of a 32-bit register
+        unsigned x = 0;
+        memcpy(&x, &v, sizeof(T));
         x = __shfl_xor_sync(0xffffffffu, x, mask);
         T r;
-        memcpy(&r, &x, 4);
+        memcpy(&r, &x, sizeof(T));
         return r;
-    } else {
-        // 8- and 16-bit values travel sign- or zero-extended in a 32-bit register
-        int x = (int)v;
-        x = __shfl_xor_sync(0xffffffffu, x, mask);
-        return (T)x;
     }
 }
 
@@ -91,28 +83,37 @@ constexpr int kPairMin = 6;
 template <int OP, typename T>
 struct Reducer;
 
+// Sum: float-likes accumulate in fp32 (rounded to T once, at the end); integers in the unsigned
+// type of the accumulator width (wrap-around, as the reference's T accumulator); Bool as C++ bool
+// does, where `acc += x` is a logical or.
 template <typename T>
 struct Reducer<MTXC_REDUCE_SUM, T> {
-    using State = SumAcc<T>;
+    using State = typename Traits<T>::Acc;
     __device__ static State init() { return State(0); }
     __device__ static void fold(State& s, T v, uint32_t) {
-        if constexpr (std::is_same_v<T, float>) s = __fadd_rn(s, v);
+        if constexpr (Traits<T>::kFloat) s = __fadd_rn(s, to_float(v));
+        else if constexpr (Traits<T>::kBool) s |= (State)(uint8_t)v;
         else s = (State)(s + (State)v);
     }
     __device__ static void merge(State& s, const State& o) {
-        if constexpr (std::is_same_v<T, float>) s = __fadd_rn(s, o);
+        if constexpr (Traits<T>::kFloat) s = __fadd_rn(s, o);
+        else if constexpr (Traits<T>::kBool) s |= o;
         else s = (State)(s + o);
     }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
-    __device__ static void store(const Out& o, uint64_t gid, const State& s) { static_cast<T*>(o.v)[gid] = (T)s; }
+    __device__ static void store(const Out& o, uint64_t gid, const State& s) {
+        if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = from_float<T>(s);
+        else if constexpr (Traits<T>::kBool) static_cast<T*>(o.v)[gid] = mbool(s != 0);
+        else static_cast<T*>(o.v)[gid] = (T)s;
+    }
 };
 
-// Extremum with index (floats for Max / Min; every type for ArgMax / ArgMin).
+// Extremum with index (float-likes for Max / Min; every type for ArgMax / ArgMin).
 template <typename T, bool kMax>
 struct PairExtremum {
     using State = Pair<T>;
     __device__ static State init() { return State{kMax ? lowest_value<T>() : highest_value<T>(), 0}; }
-    __device__ static bool beats(T a, T b) { return kMax ? (a > b) : (a < b); }
+    __device__ static bool beats(T a, T b) { return kMax ? less(b, a) : less(a, b); }
     __device__ static void fold(State& s, T v, uint32_t i) {
         if (beats(v, s.v)) {
             s.v = v;
@@ -120,39 +121,40 @@ struct PairExtremum {
         }
     }
     __device__ static void merge(State& s, const State& o) {
-        if (beats(o.v, s.v) || (o.v == s.v && o.i < s.i)) s = o;
+        if (beats(o.v, s.v) || (equal(o.v, s.v) && o.i < s.i)) s = o;
     }
     __device__ static State shfl(const State& s, int m) { return State{shfl_xor(s.v, m), shfl_xor(s.i, m)}; }
 };
 
-// Integer Max / Min: equal values are indistinguishable, so no index is needed.
+// Integer and Bool Max / Min: equal values are indistinguishable, so no index is needed.
 template <typename T, bool kMax>
 struct ValueExtremum {
     using State = T;
     __device__ static State init() { return kMax ? lowest_value<T>() : highest_value<T>(); }
     __device__ static void fold(State& s, T v, uint32_t) {
-        if (kMax ? (s < v) : (v < s)) s = v;
+        if (kMax ? less(s, v) : less(v, s)) s = v;
     }
     __device__ static void merge(State& s, const State& o) { fold(s, o, 0); }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
     __device__ static void store(const Out& o, uint64_t gid, const State& s) { static_cast<T*>(o.v)[gid] = s; }
 };
 
+template <typename T, bool kMax>
+using ExtremumOf = std::conditional_t<Traits<T>::kFloat, PairExtremum<T, kMax>, ValueExtremum<T, kMax>>;
+
 template <typename T>
-struct Reducer<MTXC_REDUCE_MAX, T>
-    : std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, true>, ValueExtremum<T, true>> {
-    using Base = std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, true>, ValueExtremum<T, true>>;
+struct Reducer<MTXC_REDUCE_MAX, T> : ExtremumOf<T, true> {
+    using Base = ExtremumOf<T, true>;
     __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
-        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(o.v)[gid] = s.v;
+        if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = s.v;
         else static_cast<T*>(o.v)[gid] = s;
     }
 };
 template <typename T>
-struct Reducer<MTXC_REDUCE_MIN, T>
-    : std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, false>, ValueExtremum<T, false>> {
-    using Base = std::conditional_t<std::is_floating_point_v<T>, PairExtremum<T, false>, ValueExtremum<T, false>>;
+struct Reducer<MTXC_REDUCE_MIN, T> : ExtremumOf<T, false> {
+    using Base = ExtremumOf<T, false>;
     __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
-        if constexpr (std::is_floating_point_v<T>) static_cast<T*>(o.v)[gid] = s.v;
+        if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = s.v;
         else static_cast<T*>(o.v)[gid] = s;
     }
 };

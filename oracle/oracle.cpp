@@ -56,9 +56,9 @@ template <typename T> inline T highest_of() {
     else return std::numeric_limits<T>::max();
 }
 
-// Runs fn(T*) for the element type of `code`; returns false for codes the
-// hot path does not evaluate (Bool, Complex64), mirroring dispatch_type's
-// refusal of Complex64 (matrix.h:284-334).
+// Runs fn(T*) for the element type of `code`; returns false for Complex64,
+// mirroring dispatch_type's refusal of it (matrix.h:284-334).  Bool runs with
+// C++ bool arithmetic: the int result of `a + b` etc. converted back to bool.
 template <typename Fn> bool with_type(int code, Fn&& fn) {
     switch (code) {
         case kFloat: fn((float*)nullptr); return true;
@@ -69,6 +69,7 @@ template <typename Fn> bool with_type(int code, Fn&& fn) {
         case kUInt32: fn((uint32_t*)nullptr); return true;
         case kUInt16: fn((uint16_t*)nullptr); return true;
         case kInt8: fn((int8_t*)nullptr); return true;
+        case kBool: fn((bool*)nullptr); return true;
         case kBFloat16: fn((__bf16*)nullptr); return true;
         case kInt64: fn((int64_t*)nullptr); return true;
         case kUInt64: fn((uint64_t*)nullptr); return true;
@@ -79,7 +80,9 @@ template <typename Fn> bool with_type(int code, Fn&& fn) {
 // Integer addition in the reference wraps (two's complement); do it in the
 // unsigned type of the same width so the restatement has no signed overflow.
 template <typename T> inline T add_wrap(T a, T b) {
-    if constexpr (std::is_integral_v<T>) {
+    if constexpr (std::is_same_v<T, bool>) {
+        return static_cast<bool>(int(a) + int(b));
+    } else if constexpr (std::is_integral_v<T>) {
         using U = std::make_unsigned_t<T>;
         return static_cast<T>(static_cast<U>(static_cast<U>(a) + static_cast<U>(b)));
     } else {
@@ -87,7 +90,9 @@ template <typename T> inline T add_wrap(T a, T b) {
     }
 }
 template <typename T> inline T sub_wrap(T a, T b) {
-    if constexpr (std::is_integral_v<T>) {
+    if constexpr (std::is_same_v<T, bool>) {
+        return static_cast<bool>(int(a) - int(b));
+    } else if constexpr (std::is_integral_v<T>) {
         using U = std::make_unsigned_t<T>;
         return static_cast<T>(static_cast<U>(static_cast<U>(a) - static_cast<U>(b)));
     } else {
@@ -95,7 +100,9 @@ template <typename T> inline T sub_wrap(T a, T b) {
     }
 }
 template <typename T> inline T mul_wrap(T a, T b) {
-    if constexpr (std::is_integral_v<T>) {
+    if constexpr (std::is_same_v<T, bool>) {
+        return static_cast<bool>(int(a) * int(b));
+    } else if constexpr (std::is_integral_v<T>) {
         using U = std::make_unsigned_t<T>;
         // promote narrow unsigned types to unsigned int before multiplying so
         // the product itself cannot overflow a signed int
@@ -491,7 +498,9 @@ int orc_broadcast(int op, int dtype, void* out, const void* a, const void* b, ui
                 case 0: return add_wrap<T>(x, y);
                 case 1: return sub_wrap<T>(x, y);
                 case 2: return mul_wrap<T>(x, y);
-                case 3: return static_cast<T>(x / y);
+                case 3:
+                    if constexpr (std::is_same_v<T, bool>) return static_cast<bool>(int(x) / int(y));
+                    else return static_cast<T>(x / y);
                 case 4: return std::max(x, y);
                 default: return std::min(x, y);
             }

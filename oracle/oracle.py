@@ -31,8 +31,9 @@ INT32_MAX = 0x7FFFFFFF
 DTYPES = {
     np.dtype(np.float32): 0, np.dtype(np.uint8): 2, np.dtype(np.int32): 3, np.dtype(np.int16): 4,
     np.dtype(np.uint32): 5, np.dtype(np.uint16): 6, np.dtype(np.int8): 8, np.dtype(np.int64): 11,
-    np.dtype(np.uint64): 12, np.dtype(np.float16): 1,
+    np.dtype(np.uint64): 12, np.dtype(np.float16): 1, np.dtype(np.bool_): 7,
 }
+BF16 = 10  # numpy has no bfloat16: its bits travel as uint16 with an explicit dtype code
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
 BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5}
 
@@ -156,29 +157,32 @@ class CpuEval:
     def _thr(self):
         return [self.threads] if self.threaded else []
 
-    def reduce_raw(self, op, x_base: np.ndarray, offset: int, meta, out_dtype=None):
+    def reduce_raw(self, op, x_base: np.ndarray, offset: int, meta, dtype_code=None):
         total = int(np.prod(meta["out_shape"], dtype=np.int64)) if meta["out_shape"] else 1
         opc = REDUCE_OPS[op]
         odt = np.int32 if opc >= 3 else x_base.dtype
         out = np.empty(max(total, 1), dtype=odt)
         ptr = x_base.ctypes.data + offset * x_base.itemsize
-        rc = self._f["reduce"](opc, DTYPES[x_base.dtype], out.ctypes.data, ptr, meta["rstride"] & 0xFFFFFFFF,
+        code = DTYPES[x_base.dtype] if dtype_code is None else dtype_code
+        rc = self._f["reduce"](opc, code, out.ctypes.data, ptr, meta["rstride"] & 0xFFFFFFFF,
                                meta["rlen"], meta["cdims"], _arr(meta["shape"]), _arr(meta["s_out"]),
                                _arr(meta["s_in"]), total, *self._thr())
         if rc != 0:
             raise RuntimeError(f"{self.prefix}reduce failed")
         return out[:total].reshape(meta["out_shape"])
 
-    def reduce(self, op, x: np.ndarray, axis: int, keepdims=False):
-        """x.op(axis, keepdims).eval_cpu() for a (possibly strided) numpy view x."""
+    def reduce(self, op, x: np.ndarray, axis: int, keepdims=False, dtype_code=None):
+        """x.op(axis, keepdims).eval_cpu() for a (possibly strided) numpy view x.  dtype_code
+        overrides the code numpy's dtype implies (BF16 data held as uint16)."""
         base, offset = _base_and_offset(x)
         meta = self.reduce_meta(list(x.shape), elem_strides(x), axis, keepdims)
-        return self.reduce_raw(op, base, offset, meta)
+        return self.reduce_raw(op, base, offset, meta, dtype_code)
 
-    def binary_raw(self, op, a_base, a_off, b_base, b_off, meta):
+    def binary_raw(self, op, a_base, a_off, b_base, b_off, meta, dtype_code=None):
         total = int(np.prod(meta["out_shape"], dtype=np.int64)) if meta["out_shape"] else 1
         out = np.empty(max(total, 1), dtype=a_base.dtype)
-        rc = self._f["broadcast"](BINARY_OPS[op], DTYPES[a_base.dtype], out.ctypes.data,
+        code = DTYPES[a_base.dtype] if dtype_code is None else dtype_code
+        rc = self._f["broadcast"](BINARY_OPS[op], code, out.ctypes.data,
                                   a_base.ctypes.data + a_off * a_base.itemsize,
                                   b_base.ctypes.data + b_off * b_base.itemsize, meta["cdims"], _arr(meta["sr"]),
                                   _arr(meta["sa"]), _arr(meta["sb"]), total, *self._thr())
@@ -186,13 +190,13 @@ class CpuEval:
             raise RuntimeError(f"{self.prefix}broadcast failed")
         return out[:total].reshape(meta["out_shape"])
 
-    def binary(self, op, a: np.ndarray, b: np.ndarray):
+    def binary(self, op, a: np.ndarray, b: np.ndarray, dtype_code=None):
         """(a op b).eval_cpu() with both operands already of the same dtype."""
         assert a.dtype == b.dtype
         ab, ao = _base_and_offset(a)
         bb, bo = _base_and_offset(b)
         meta = self.binary_meta(list(a.shape), elem_strides(a), list(b.shape), elem_strides(b))
-        return self.binary_raw(op, ab, ao, bb, bo, meta)
+        return self.binary_raw(op, ab, ao, bb, bo, meta, dtype_code)
 
     def exp(self, x: np.ndarray):
         base, offset = _base_and_offset(x)

@@ -63,5 +63,7 @@ def test_workspace_query_is_host_only():
     # [131072, 2048] row sums: one warp per row, no partials
     assert lib.mtxc_reduce_workspace_bytes(0, 0, 1, 2048, 1, arr([131072]), arr([1]), arr([2048]), C.byref(b)) == 0
     assert b.value == 0
-    assert lib.mtxc_reduce_workspace_bytes(0, 1, 1, 2048, 1, arr([16]), arr([1]), arr([2048]), C.byref(b)) == \
+    # Float16 (code 1) is evaluated; Complex64 (code 9) is refused like dispatch_type refuses it
+    assert lib.mtxc_reduce_workspace_bytes(0, 1, 1, 2048, 1, arr([16]), arr([1]), arr([2048]), C.byref(b)) == 0
+    assert lib.mtxc_reduce_workspace_bytes(0, 9, 1, 2048, 1, arr([16]), arr([1]), arr([2048]), C.byref(b)) == \
         _abi.ERR_UNSUPPORTED_DTYPE

@@ -151,6 +151,42 @@ def test_broadcast_loops_match_reference(port, ref, dtype):
             assert x.shape == y.shape and x.tobytes() == y.tobytes(), (op, sa, sb)
 
 
+def _bf16_bits(rng, n):
+    """Random bfloat16 values as uint16 bits: normals with ties, and NaN, +-inf, +-0."""
+    v = (np.floor(rng.standard_normal(n) * 8) / 8).astype(np.float32)
+    pick = rng.integers(0, 16, n)
+    v[pick == 0], v[pick == 1], v[pick == 2], v[pick == 3] = np.nan, np.inf, -np.inf, -0.0
+    return (v.view(np.uint32) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("kind", ["bool", "bfloat16"])
+def test_bool_and_bfloat16_loops_match_reference(port, ref, kind):
+    """Bool (code 7) and BFloat16 (code 10, carried as uint16 bits) through the same loops."""
+    rng = np.random.default_rng(7)
+    code = 7 if kind == "bool" else 10
+
+    def values(n):
+        return rng.integers(0, 2, n).astype(np.bool_) if kind == "bool" else _bf16_bits(rng, n)
+
+    for trial in range(120):
+        _, shape, strides, off = random_view(rng, np.float32)
+        need = off + sum((e - 1) * s for e, s in zip(shape, strides)) + 1
+        x = strided_view(values(need), shape, strides, off)
+        axis = int(rng.integers(0, len(shape)))
+        for op in ("sum", "max", "min", "argmax", "argmin"):
+            a = port.reduce(op, x, axis, dtype_code=code)
+            b = ref.reduce(op, x, axis, dtype_code=code)
+            assert a.shape == b.shape and a.tobytes() == b.tobytes(), (kind, op, shape, strides, off, axis)
+        sa = [int(v) for v in rng.integers(1, 6, 3)]
+        sb = [sa[0], 1, sa[2]] if rng.random() < 0.5 else [1, sa[1], 1]
+        a, b = values(int(np.prod(sa))).reshape(sa), values(int(np.prod(sb))).reshape(sb)
+        for op in ("add", "sub", "mul", "div", "max", "min"):
+            bb = np.ones_like(b) if (kind == "bool" and op == "div") else b  # bool / false traps on x86
+            x1 = port.binary(op, a, bb, dtype_code=code)
+            y1 = ref.binary(op, a, bb, dtype_code=code)
+            assert x1.shape == y1.shape and x1.tobytes() == y1.tobytes(), (kind, op, sa, sb)
+
+
 def test_exp_loop_matches_reference(port, ref):
     rng = np.random.default_rng(4)
     for trial in range(100):
