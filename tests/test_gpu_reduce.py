@@ -186,9 +186,11 @@ def test_unsupported_dtype_is_an_error(gpu):
     out = torch.zeros(1, dtype=torch.float32, device="cuda")
     meta = gpu.reduce_meta([16], [1], 0)
     shape, so, si = meta.arrays
-    rc = _abi.lib().mtxc_reduce(0, 1, out.data_ptr(), x.data_ptr(), 1, 16, meta.cdims, shape, so, si)  # Float16
+    rc = _abi.lib().mtxc_reduce(0, 9, out.data_ptr(), x.data_ptr(), 1, 16, meta.cdims, shape, so, si)  # Complex64
     assert rc == _abi.ERR_UNSUPPORTED_DTYPE
-    assert b"Float16" in _abi.lib().mtxc_last_error()
+    assert b"Complex64" in _abi.lib().mtxc_last_error()
+    rc = _abi.lib().mtxc_reduce(0, 13, out.data_ptr(), x.data_ptr(), 1, 16, meta.cdims, shape, so, si)
+    assert rc == _abi.ERR_UNSUPPORTED_DTYPE
     rc = _abi.lib().mtxc_reduce(9, 0, out.data_ptr(), x.data_ptr(), 1, 16, meta.cdims, shape, so, si)
     assert rc == _abi.ERR_INVALID_ARGUMENT
 
