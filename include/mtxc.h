@@ -70,12 +70,17 @@ enum {
  * ArgMinPrimitive (primitives.cpp:2825-2971, 1967-2252, 7584-7799). */
 enum { MTXC_REDUCE_SUM = 0, MTXC_REDUCE_MAX = 1, MTXC_REDUCE_MIN = 2, MTXC_REDUCE_ARGMAX = 3, MTXC_REDUCE_ARGMIN = 4 };
 
-/* Broadcast binary ops: Addition/Subtraction/Multiplication/DivisionPrimitive and
- * Max/MinPrimitive (primitives.cpp:397-1046, 2515-2823). */
-enum { MTXC_BINARY_ADD = 0, MTXC_BINARY_SUB = 1, MTXC_BINARY_MUL = 2, MTXC_BINARY_DIV = 3, MTXC_BINARY_MAX = 4, MTXC_BINARY_MIN = 5 };
+/* Broadcast binary ops: Addition/Subtraction/Multiplication/DivisionPrimitive,
+ * Max/MinPrimitive (primitives.cpp:397-1046, 2515-2823) and EqualPrimitive (matrix::equal). */
+enum { MTXC_BINARY_ADD = 0, MTXC_BINARY_SUB = 1, MTXC_BINARY_MUL = 2, MTXC_BINARY_DIV = 3, MTXC_BINARY_MAX = 4, MTXC_BINARY_MIN = 5,
+       MTXC_BINARY_EQUAL = 6 };
 
-/* Unary ops: ExpPrimitive (primitives.cpp:5332-5463). */
-enum { MTXC_UNARY_EXP = 0 };
+/* Unary ops: ExpPrimitive (primitives.cpp:5332-5463), SqrtPrimitive. */
+enum { MTXC_UNARY_EXP = 0, MTXC_UNARY_SQRT = 1 };
+
+/* The make_pointwise family (Matrix.mm:13511-13604): GreaterPrimitive, LessPrimitive,
+ * LogicalAndPrimitive, WherePrimitive, FloorPrimitive, FullPrimitive. */
+enum { MTXC_PW_GREATER = 0, MTXC_PW_LESS = 1, MTXC_PW_LOGICAL_AND = 2, MTXC_PW_WHERE = 3, MTXC_PW_FLOOR = 4, MTXC_PW_FULL = 5 };
 
 /* ------------------------------------------------------------------------------------------
  * Runtime.  Replaces GPUManager's device / queue / per-thread command buffer layer
@@ -170,6 +175,19 @@ int mtxc_broadcast_shapes(const uint32_t* shape1, const uint32_t* strides1, int 
  * for an out-of-range code. */
 int mtxc_promote_types(int a, int b);
 
+/* The make_pointwise collapse (Matrix.mm:13537-13555): axes of extent 1 are dropped, and an axis is
+ * merged into the previous kept one when every input is contiguous across the two (stride of the
+ * previous = stride * extent; stride-0 broadcasts merge) and the merged extent stays <= INT32_MAX.
+ * out_shape: the output shape (out_dims entries).  in_strides: n_inputs rows of out_dims strides,
+ * right-aligned to the output rank with 0 on broadcast axes (what make_pointwise builds as
+ * all_strides).  Writes the collapsed shape (MTXC_MAX_DIMS entries) and n_inputs rows of
+ * MTXC_MAX_DIMS collapsed strides (row i at out_strides + i * MTXC_MAX_DIMS); returns the collapsed
+ * rank (0 for an empty output, as the reference skips the collapse when the count is 0, and for a
+ * single element), or UINT32_MAX where the reference throws (out_dims > MTXC_MAX_DIMS, more than 2^32 - 1
+ * output elements) and for n_inputs > 3 or null pointers. */
+uint32_t mtxc_pointwise_collapse(const uint32_t* out_shape, uint32_t out_dims, const uint32_t* in_strides,
+                                 uint32_t n_inputs, uint32_t* out_cshape, uint32_t* out_strides);
+
 /* ------------------------------------------------------------------------------------------
  * Hot path.
  * ---------------------------------------------------------------------------------------- */
@@ -262,9 +280,37 @@ int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, const void*
                           const uint32_t* b_strides);
 
 /* Elementwise unary op over collapse_dims(shape, out strides, in strides) metadata
- * (Matrix.mm:6934-7065).  EXP on float: CUDA expf, within 2 ulp of the CPU's std::exp. */
+ * (Matrix.mm:6798-6925, 6934-7065), on Float or Float16 (the frontends promote other dtypes first).
+ * EXP: CUDA expf, within 2 ulp of the CPU's std::exp (Float16: that result rounded once).  SQRT: the
+ * correctly rounded square root, bit-exact with std::sqrt. */
 int mtxc_unary(int op, int dtype, void* dst, const void* src, uint32_t cdims, const uint32_t* shape,
                const uint32_t* dst_strides, const uint32_t* src_strides);
+
+/* Element type conversion and strided copy: matrix::astype(output, type, ...) (Matrix.mm:8400-8412)
+ * through copyGPUinplace / copyGPUinplaceTypeCasted (Matrix.mm:1699-1922).  Metadata:
+ * collapse_dims(in.shape, out.strides, in.strides, INT32_MAX), as the reference computes it
+ * (matrix.h:1481).  Element gid's position is decoded from shape; dst[sum idx*dst_strides] =
+ * dtype_cast<Dst>(src[sum idx*src_strides]) (matrix.h:260-267): integers wrap, conversions to a
+ * float-like type round to nearest even (half <-> bfloat16 through float), conversions to Bool test
+ * x != 0, float-likes truncate toward zero into integers (defined when the result fits; outside the
+ * destination's range the low bits of the 64-bit truncation are written).  Every dtype pair except
+ * Complex64; dst_dtype == src_dtype is a copy. */
+int mtxc_astype(int dst_dtype, int src_dtype, void* dst, const void* src, uint32_t cdims, const uint32_t* shape,
+                const uint32_t* dst_strides, const uint32_t* src_strides);
+
+/* The make_pointwise family over mtxc_pointwise_collapse metadata.  The output is contiguous (element
+ * gid at dst[gid]); input k's element is at inputs[k][sum idx_i * strides[k * MTXC_MAX_DIMS + i]] (the
+ * layout of the reference's ElementwiseDims::strides[3][MAX_TENSOR_DIMS]).  cdims == 0 is one element
+ * at offset 0.  dtype is the inputs' common dtype (the frontends cast first):
+ *   GREATER, LESS (2 inputs of dtype)      -> Bool: a > b, a < b (greater/less_backend_cpu)
+ *   LOGICAL_AND (2 Bool inputs)             -> Bool: a && b
+ *   WHERE (Bool cond, a, b of dtype)        -> dtype: cond ? a : b (inputs ordered cond, a, b)
+ *   FLOOR (1 input)                         -> dtype: floor for float-likes, identity otherwise
+ *   FULL (1 input, the broadcast value)     -> dtype: the value
+ * Results are bit-exact with the CPU backends (Matrix.mm:13741-14166).  The output must not exceed
+ * 2^32 - 1 elements (make_pointwise's limit). */
+int mtxc_pointwise(int op, int dtype, void* dst, const void* const* inputs, uint32_t n_inputs, uint32_t cdims,
+                   const uint32_t* shape, const uint32_t* strides);
 
 /* Fused evaluation of the reference's softmax trace over the last axis of contiguous float rows
  *     m = x.max(-1, true); e = matrix::exp(x - m); y = e / e.sum(-1, true)

@@ -21,8 +21,9 @@ ERR_NOT_INITIALIZED = 6
 ERR_WORKSPACE = 7
 
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
-BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5}
-UNARY_OPS = {"exp": 0}
+BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5, "equal": 6}
+UNARY_OPS = {"exp": 0, "sqrt": 1}
+POINTWISE_OPS = {"greater": 0, "less": 1, "logical_and": 2, "where": 3, "floor": 4, "full": 5}
 
 
 class MtxcError(RuntimeError):
@@ -80,6 +81,9 @@ def lib() -> C.CDLL:
             "mtxc_broadcast_binary": (i32, [i32, i32, vp, vp, vp, u32, U32P, U32P, U32P, U32P]),
             "mtxc_unary": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),
             "mtxc_softmax_lastdim": (i32, [i32, vp, vp, u64, u32, u64, u64]),
+            "mtxc_astype": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),
+            "mtxc_pointwise_collapse": (u32, [U32P, u32, U32P, u32, U32P, U32P]),
+            "mtxc_pointwise": (i32, [i32, i32, vp, C.POINTER(vp), u32, u32, U32P, U32P]),
             "mtxc_graph_begin": (i32, []),
             "mtxc_graph_end": (i32, [C.POINTER(vp)]),
             "mtxc_graph_launch": (i32, [vp]),

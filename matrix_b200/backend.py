@@ -194,15 +194,92 @@ def binary(op: str, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None =
     return out
 
 
-def exp(x: torch.Tensor, out: torch.Tensor | None = None, meta: UnaryMeta | None = None) -> torch.Tensor:
-    """matrix::exp(x) evaluated through mtxc_unary."""
+def unary(op: str, x: torch.Tensor, out: torch.Tensor | None = None, meta: UnaryMeta | None = None) -> torch.Tensor:
+    """matrix::exp(x) / matrix::sqrt(x) on a float32 or float16 tensor, through mtxc_unary."""
     code = dtype_code(x.dtype)
     if meta is None:
         meta = unary_meta(list(x.shape), _check_strides(x))
     if out is None:
         out = torch.empty(meta.out_shape, dtype=x.dtype, device=x.device)
     shape, so, si = meta.arrays
-    check(lib().mtxc_unary(_abi.UNARY_OPS["exp"], code, out.data_ptr(), x.data_ptr(), meta.cdims, shape, so, si))
+    check(lib().mtxc_unary(_abi.UNARY_OPS[op], code, out.data_ptr(), x.data_ptr(), meta.cdims, shape, so, si))
+    return out
+
+
+def exp(x: torch.Tensor, out: torch.Tensor | None = None, meta: UnaryMeta | None = None) -> torch.Tensor:
+    """matrix::exp(x) evaluated through mtxc_unary."""
+    return unary("exp", x, out, meta)
+
+
+def astype(x: torch.Tensor, dtype: torch.dtype, make_contig: bool = True, out: torch.Tensor | None = None):
+    """x.astype(dtype, make_contig) evaluated through mtxc_astype (Matrix.mm:8384-8412).  Without
+    make_contig the output takes x's strides (broadcast axes included), as the promotion path does."""
+    shape, s_in = list(x.shape), _check_strides(x)
+    if out is None:
+        out = (torch.empty(shape, dtype=dtype, device=x.device) if make_contig
+               else torch.empty_strided(shape, s_in, dtype=dtype, device=x.device))
+    s_out = _check_strides(out)
+    o = [u32_array([]) for _ in range(3)]
+    k = lib().mtxc_collapse_dims2(u32_array(shape), u32_array(s_out), u32_array(s_in), len(shape), INT32_MAX, *o)
+    check(lib().mtxc_astype(dtype_code(dtype), dtype_code(x.dtype), out.data_ptr(), x.data_ptr(), k, *o))
+    return out
+
+
+@dataclass
+class PointwiseMeta:
+    out_shape: list
+    cdims: int
+    shape: list
+    strides: list
+    arrays: tuple = field(default=(), repr=False)
+
+
+def pointwise_meta(shapes, strides) -> PointwiseMeta:
+    """pointwise_shape + make_pointwise's collapse (Matrix.mm:13497-13556) for inputs given as
+    (shape, strides) lists: the broadcast output shape, each input's right-aligned strides (0 where
+    its extent is 1) collapsed by mtxc_pointwise_collapse."""
+    rank = max((len(sh) for sh in shapes), default=0)
+    out = [1] * rank
+    for sh in shapes:
+        for d, m in enumerate(sh):
+            n = out[rank - len(sh) + d]
+            if n == 1:
+                out[rank - len(sh) + d] = m
+            elif m != 1 and n != m:
+                raise _abi.MtxcError(_abi.ERR_SHAPE, "incompatible pointwise broadcast shapes")
+    rows = []
+    for sh, st in zip(shapes, strides):
+        r = [0] * rank
+        for d, (m, s) in enumerate(zip(sh, st)):
+            r[rank - len(sh) + d] = 0 if m == 1 else s
+        rows.extend(r)
+    n = len(shapes)
+    flat = u32_array(rows, max(1, len(rows)))
+    cshape = u32_array([])
+    cstr = u32_array([], 3 * _abi.MAX_DIMS)
+    k = lib().mtxc_pointwise_collapse(u32_array(out, max(rank, 1)), rank, flat, n, cshape, cstr)
+    if k == UINT32_MAX:
+        raise _abi.MtxcError(_abi.ERR_SHAPE, "pointwise output refused (rank or 32-bit size limit)")
+    st = [list(cstr[i * _abi.MAX_DIMS:i * _abi.MAX_DIMS + k]) for i in range(n)]
+    return PointwiseMeta(out, k, list(cshape[:k]), st, (cshape, cstr))
+
+
+def pointwise(op: str, inputs, out: torch.Tensor | None = None, meta: PointwiseMeta | None = None) -> torch.Tensor:
+    """greater / less / logical_and / where / floor / full through mtxc_pointwise.  inputs are device
+    tensors already in their common dtype (where: cond bool, then a and b)."""
+    import ctypes
+
+    if meta is None:
+        meta = pointwise_meta([list(t.shape) for t in inputs], [_check_strides(t) for t in inputs])
+    data = inputs[-1]
+    code = dtype_code(data.dtype)
+    odt = torch.bool if op in ("greater", "less", "logical_and") else data.dtype
+    if out is None:
+        out = torch.empty(meta.out_shape, dtype=odt, device=data.device)
+    ptrs = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in inputs])
+    cshape, cstr = meta.arrays
+    check(lib().mtxc_pointwise(_abi.POINTWISE_OPS[op], code, out.data_ptr(), ptrs, len(inputs), meta.cdims, cshape,
+                               cstr))
     return out
 
 

@@ -1,8 +1,9 @@
-// Broadcasted binary ops (Add, Sub, Mul, Divide, Max, Min) for sm_100a.
+// Broadcasted binary ops (Add, Sub, Mul, Divide, Max, Min, Equal) for sm_100a.
 //
 // Replaces ComputeShaders/Brodcasted{Add,Sub,Mul,Divide,Max,Min}.metal behind
-// add/subtract/multiply/divide_gpu_brodcasted (Matrix.mm:7709-8239) and the METAL branch of
-// matrix::max / min(other, result, dev) (Matrix.mm:13378-13476, 14683-14783).
+// add/subtract/multiply/divide_gpu_brodcasted (Matrix.mm:7709-8239), the METAL branch of
+// matrix::max / min(other, result, dev) (Matrix.mm:13378-13476, 14683-14783) and Equal.metal behind
+// matrix::equal_backend (Matrix.mm:14467-14539), which binds the same collapse_dims_3 metadata.
 //
 // Semantics follow the reference CPU loops (Matrix.mm:7475-7498 and siblings): result element
 // gid, decoded axis by axis with the result strides, reads a and b through their own strides
@@ -32,7 +33,11 @@ constexpr uint32_t kSegVecs = 4096;
 
 template <int OP, typename T>
 __device__ __forceinline__ T apply(T x, T y) {
-    if constexpr (OP == MTXC_BINARY_MAX) return less(x, y) ? y : x;       // std::max: x unless x < y
+    if constexpr (OP == MTXC_BINARY_EQUAL) {  // matrix::equal: T(1) or T(0) (Matrix.mm:14536)
+        if constexpr (Traits<T>::kFloat) return from_float<T>(equal(x, y) ? 1.0f : 0.0f);
+        else if constexpr (Traits<T>::kBool) return mbool(x == y);
+        else return equal(x, y) ? T(1) : T(0);
+    } else if constexpr (OP == MTXC_BINARY_MAX) return less(x, y) ? y : x;  // std::max: x unless x < y
     else if constexpr (OP == MTXC_BINARY_MIN) return less(y, x) ? y : x;  // std::min: x unless y < x
     else if constexpr (Traits<T>::kFloat) {
         // one round-to-nearest operation in fp32; for the half types the fp32 result rounded once to
@@ -289,6 +294,7 @@ int launch_broadcast_op(int op, void* r, const void* a, const void* b, uint32_t 
         case MTXC_BINARY_DIV: return launch_broadcast<MTXC_BINARY_DIV, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
         case MTXC_BINARY_MAX: return launch_broadcast<MTXC_BINARY_MAX, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
         case MTXC_BINARY_MIN: return launch_broadcast<MTXC_BINARY_MIN, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
+        case MTXC_BINARY_EQUAL: return launch_broadcast<MTXC_BINARY_EQUAL, T>(r, a, b, cdims, shape, sr, sa, sb, sms, st);
         default: return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: unknown op");
     }
 }
@@ -302,7 +308,7 @@ extern "C" int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, 
                                      const uint32_t* shape, const uint32_t* r_strides, const uint32_t* a_strides,
                                      const uint32_t* b_strides) {
     if (int rc = require_init()) return rc;
-    if (op < MTXC_BINARY_ADD || op > MTXC_BINARY_MIN)
+    if (op < MTXC_BINARY_ADD || op > MTXC_BINARY_EQUAL)
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: unknown op");
     if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary: cdims > MTXC_MAX_DIMS");
     if (cdims && (!shape || !r_strides || !a_strides || !b_strides))

@@ -193,4 +193,37 @@ int mtxc_promote_types(int a, int b) {
     return kPromote[a][b];
 }
 
+// make_pointwise's collapse (Matrix.mm:13537-13555).  Walks the output axes outermost first, skips
+// extent-1 axes, and folds an axis into the last kept one when the merged extent stays <= INT32_MAX
+// and, for every input, the kept axis' stride equals this axis' stride times its extent (64-bit
+// comparison, as in the reference).  The merged axis keeps the inner axis' strides.
+uint32_t mtxc_pointwise_collapse(const uint32_t* out_shape, uint32_t out_dims, const uint32_t* in_strides,
+                                 uint32_t n_inputs, uint32_t* out_cshape, uint32_t* out_strides) {
+    if (out_dims > MTXC_MAX_DIMS || n_inputs > 3) return UINT32_MAX;
+    if (out_dims && (!out_shape || (n_inputs && !in_strides))) return UINT32_MAX;
+    if (!out_cshape || (n_inputs && !out_strides)) return UINT32_MAX;
+    uint64_t count = 1;
+    for (uint32_t d = 0; d < out_dims; ++d) {
+        if (out_shape[d] && count > UINT32_MAX / out_shape[d]) return UINT32_MAX;  // overflow_error there
+        count *= out_shape[d];
+    }
+    for (uint32_t i = 0; i < MTXC_MAX_DIMS; ++i) {
+        out_cshape[i] = 0;
+        for (uint32_t k = 0; k < n_inputs; ++k) out_strides[k * MTXC_MAX_DIMS + i] = 0;
+    }
+    uint32_t n = 0;
+    if (count == 0) return 0;
+    for (uint32_t d = 0; d < out_dims; ++d) {
+        const uint32_t ext = out_shape[d];
+        if (ext == 1) continue;
+        bool merge = n > 0 && (uint64_t)out_cshape[n - 1] * ext <= INT32_MAX;
+        for (uint32_t k = 0; k < n_inputs && merge; ++k)
+            merge = (uint64_t)out_strides[k * MTXC_MAX_DIMS + n - 1] == (uint64_t)in_strides[k * out_dims + d] * ext;
+        const uint32_t t = merge ? n - 1 : n++;
+        out_cshape[t] = merge ? out_cshape[t] * ext : ext;
+        for (uint32_t k = 0; k < n_inputs; ++k) out_strides[k * MTXC_MAX_DIMS + t] = in_strides[k * out_dims + d];
+    }
+    return n;
+}
+
 }  // extern "C"

@@ -1,13 +1,18 @@
-// Elementwise unary ops for sm_100a: exp (ExpPrimitive, primitives.cpp:5332-5463).
+// Elementwise unary ops for sm_100a: exp (ExpPrimitive, primitives.cpp:5332-5463) and sqrt
+// (SqrtPrimitive).
 //
-// Replaces ComputeShaders/exp.metal behind matrix::exp(output, dev) (Matrix.mm:6949-7011).
-// The metadata is the primitive's collapse_dims(shape, output strides, input strides); the
-// element position is decoded from the collapsed shape, innermost axis fastest, as the CPU
-// branch does (Matrix.mm:7014-7063).  exp is CUDA's expf (full-range, <= 2 ulp), so results
-// agree with the CPU's std::exp within a few ulp rather than bit for bit.
+// Replaces ComputeShaders/exp.metal and sqrt.metal behind matrix::exp / matrix::sqrt(output, dev)
+// (Matrix.mm:6949-7011, 6813-6867).  Both ops take Float or Float16 (the frontends promote every other
+// dtype first: promote_types(type, Float16), Matrix.mm:6798-6811, 6934-6947).  The metadata is the
+// primitive's collapse_dims(shape, output strides, input strides); the element position is decoded
+// from the collapsed shape, innermost axis fastest, as the CPU branches do (Matrix.mm:6870-6925,
+// 7014-7063).  exp is CUDA's expf (full-range, <= 2 ulp), so results agree with the CPU's std::exp
+// within a few ulp rather than bit for bit; Float16 exp rounds that float result once.  sqrt is the
+// IEEE correctly rounded square root (sqrtf), bit-exact with std::sqrt; for Float16 the float root
+// rounded once is the correctly rounded half result.
 #include <algorithm>
 
-#include "mtxc_internal.cuh"
+#include "elementwise.cuh"
 
 namespace mtxc {
 namespace {
@@ -148,6 +153,26 @@ int launch_exp(float* dst, const float* src, uint32_t cdims, const uint32_t* sha
     return check_launch("exp_generic_kernel");
 }
 
+template <typename T>
+struct ExpOp {
+    using Out = T;
+    using In0 = T;
+    using In1 = T;
+    using In2 = T;
+    static constexpr int kArity = 1;
+    __device__ __forceinline__ T operator()(T x, T, T) const { return from_float<T>(expf(to_float(x))); }
+};
+
+template <typename T>
+struct SqrtOp {
+    using Out = T;
+    using In0 = T;
+    using In1 = T;
+    using In2 = T;
+    static constexpr int kArity = 1;
+    __device__ __forceinline__ T operator()(T x, T, T) const { return from_float<T>(sqrtf(to_float(x))); }
+};
+
 }  // namespace
 }  // namespace mtxc
 
@@ -156,14 +181,26 @@ using namespace mtxc;
 extern "C" int mtxc_unary(int op, int dtype, void* dst, const void* src, uint32_t cdims, const uint32_t* shape,
                           const uint32_t* dst_strides, const uint32_t* src_strides) {
     if (int rc = require_init()) return rc;
-    if (op != MTXC_UNARY_EXP) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: unknown op");
-    if (dtype != MTXC_FLOAT)
-        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_unary: exp has no kernel for dtype ") + dtype_name(dtype));
+    if (op != MTXC_UNARY_EXP && op != MTXC_UNARY_SQRT) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: unknown op");
+    if (dtype != MTXC_FLOAT && dtype != MTXC_FLOAT16)
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_unary: no kernel for dtype ") + dtype_name(dtype) +
+                                                    " (exp and sqrt take Float or Float16)");
     if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: cdims > MTXC_MAX_DIMS");
     if (cdims && (!shape || !dst_strides || !src_strides))
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: null metadata pointer");
     if (!dst || !src) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: null buffer");
     ThreadCtx& c = ctx();
-    return launch_exp(static_cast<float*>(dst), static_cast<const float*>(src), cdims, shape, dst_strides, src_strides,
-                      c.sm_count, c.stream());
+    if (op == MTXC_UNARY_EXP && dtype == MTXC_FLOAT)
+        return launch_exp(static_cast<float*>(dst), static_cast<const float*>(src), cdims, shape, dst_strides,
+                          src_strides, c.sm_count, c.stream());
+    ew::MapDesc m{};
+    m.dst = dst;
+    m.src[0] = src;
+    m.cdims = cdims;
+    m.shape = shape;
+    m.sd = dst_strides;
+    m.ss[0] = src_strides;
+    if (op == MTXC_UNARY_EXP) return ew::launch_map<ExpOp<__half>>(m, c.sm_count, c.stream());
+    if (dtype == MTXC_FLOAT) return ew::launch_map<SqrtOp<float>>(m, c.sm_count, c.stream());
+    return ew::launch_map<SqrtOp<__half>>(m, c.sm_count, c.stream());
 }

@@ -22,7 +22,14 @@ Pieces taken verbatim (file, anchor; the reference line numbers at the time of w
                      (161-232), CPU loops of sum (15188-15207), max (14895-14914), min
                      (15039-15058), argmax (16279-16302), argmin (16434-16457), broadcast
                      add/mul/sub/div lambdas (7475, 7546, 7614, 7683), max(a,b) (13459-13474),
-                     min(a,b) (14764-14781), exp (7014-7063)
+                     min(a,b) (14764-14781), exp (7014-7063), the sqrt lambda (6878-6925),
+                     the equal loop (14522-14538), make_pointwise's collapse (13544-13556), the
+                     CPU backends greater / less / logical_and / where / floor / full
+                     (13741-14166)
+  matrix.h           dtype_cast (260-267), copyCPUinplaceTypeCasted (1474-1544)
+  primitives.cpp     ElementwiseDims (6614-6618)
+The member functions are compiled as members of a small stand-in `matrix` struct and stand-in
+primitive structs that carry only the fields those functions read.
 
 Usage: ``python oracle/build_ref.py [--reference PATH]``.  The reference root defaults to the
 ``reference_path`` recorded in BASELINE.json at the repository root, or $MTX_REFERENCE_ROOT.
@@ -122,6 +129,9 @@ struct complex64 { float re, im; };
 // libstdc++ on x86 has no std::exp overload for _Float16 (the reference's fp16 exp evaluates in
 // float and rounds back); give it one so the fp16 instantiation of the exp loop compiles.
 namespace std { inline _Float16 exp(_Float16 x) { return (_Float16)::expf((float)x); } }
+// Same for sqrt: evaluated in float (correctly rounded) and rounded once to half, which is what the
+// reference's float16_t arithmetic does.
+namespace std { inline _Float16 sqrt(_Float16 x) { return (_Float16)::sqrtf((float)x); } }
 """
 
 WRAPPERS = r"""
@@ -157,6 +167,19 @@ static void ref_bmin_impl(dtype type, RefMat& result, void* buffer, RefMat& othe
 
 static void ref_exp_impl(dtype type, RefMat& output, void* buffer, CollapsedDims_2 res, uint32_t cdims,
                          size_t total_size) { @EXP@ }
+static void ref_sqrt_impl(dtype type, RefMat& output, void* buffer, CollapsedDims_2 res, uint32_t cdims,
+                          size_t total_size) { @SQRT@ dispatch_float_type(type, output.buffer, sqrt_cpu); }
+// matrix::equal_backend's CPU branch, after its rank-0 rule (Matrix.mm:14480-14486)
+static void ref_equal_impl(matrix& output, const matrix& a, const matrix& b, CollapsedDims_3 res) {
+    if (res.out_dims == 0) {
+        res.out_dims = 1;
+        res.shape[0] = 1;
+        res.stridesA[0] = res.stridesB[0] = res.stridesC[0] = 0;
+    }
+    uint32_t cdims = res.out_dims;
+    if (output.total_size == 0) return;
+    @EQUAL@
+}
 
 extern "C" {
 
@@ -300,6 +323,102 @@ int ref_broadcast_shapes(const uint32_t* shape1, const uint32_t* strides1, int d
 
 int ref_promote(int a, int b) { return (int)promote_types((dtype)a, (dtype)b); }
 
+int ref_unary(int op, int dtype_code, void* out, const void* in, uint32_t cdims, const uint32_t* shape,
+              const uint32_t* sOut, const uint32_t* sIn, uint64_t total) {
+    if (op == 0) return ref_exp(dtype_code, out, in, cdims, shape, sOut, sIn, total);
+    CollapsedDims_2 res{};
+    for (uint32_t i = 0; i < cdims && i < MAX_TENSOR_DIMS; ++i) {
+        res.shape[i] = shape[i]; res.stridesA[i] = sOut[i]; res.stridesB[i] = sIn[i];
+    }
+    res.out_dims = cdims;
+    RefMat output{out, (size_t)total};
+    try { ref_sqrt_impl((dtype)dtype_code, output, (void*)in, res, cdims, (size_t)total); }
+    catch (...) { return -1; }
+    return 0;
+}
+
+int ref_astype(int dst_code, int src_code, void* out, const void* in, uint32_t dims, const uint32_t* shape,
+               const uint32_t* sOut, const uint32_t* sIn, uint64_t total) {
+    matrix o, i;
+    o.type = (dtype)dst_code; o.buffer = out; o.total_size = (size_t)total; o.dims = dims;
+    i.type = (dtype)src_code; i.buffer = (void*)in; i.total_size = (size_t)total; i.dims = dims;
+    for (uint32_t k = 0; k < dims && k < MAX_TENSOR_DIMS; ++k) {
+        o.shp[k] = i.shp[k] = shape[k]; o.str[k] = sOut[k]; i.str[k] = sIn[k];
+    }
+    try { matrix::copyCPUinplaceTypeCasted(o, i, 0); } catch (...) { return -1; }
+    return 0;
+}
+
+uint32_t ref_pointwise_collapse(const uint32_t* out_shape, uint32_t out_dims, const uint32_t* in_strides,
+                                uint32_t n, uint32_t* cshape, uint32_t* cstrides) {
+    size_t count = 1;
+    for (uint32_t d = 0; d < out_dims; ++d) {
+        if (out_shape[d] && count > UINT32_MAX / out_shape[d]) return UINT32_MAX;
+        count *= out_shape[d];
+    }
+    matrix out;
+    out.dims = out_dims;
+    for (uint32_t d = 0; d < out_dims; ++d) out.shp[d] = out_shape[d];
+    PointwiseShim node;
+    PointwiseShim* prim = &node;
+    std::vector<int> inputs(n);
+    size_m all_strides[3][MAX_TENSOR_DIMS]{};
+    for (uint32_t i = 0; i < n; ++i)
+        for (uint32_t d = 0; d < out_dims; ++d) all_strides[i][d] = in_strides[i * out_dims + d];
+    @PWCOLLAPSE@
+    const auto& cd = prim->collapsed_dims;
+    for (uint32_t d = 0; d < MAX_TENSOR_DIMS; ++d) {
+        cshape[d] = cd.shape[d];
+        for (uint32_t i = 0; i < n; ++i) cstrides[i * MAX_TENSOR_DIMS + d] = cd.strides[i][d];
+    }
+    return cd.dims;
+}
+
+int ref_pointwise(int op, int dtype_code, void* out, const void* const* inputs, uint32_t n, uint32_t cdims,
+                  const uint32_t* shape, const uint32_t* strides, uint64_t total) {
+    static const uint32_t kArity[] = {2, 2, 2, 3, 1, 1};
+    if (op < 0 || op > 5 || n != kArity[op]) return -1;
+    ElementwiseDims cd{};
+    cd.dims = cdims;
+    for (uint32_t d = 0; d < cdims; ++d) {
+        cd.shape[d] = shape[d];
+        for (uint32_t i = 0; i < n; ++i) cd.strides[i][d] = strides[i * MAX_TENSOR_DIMS + d];
+    }
+    matrix in[3];
+    for (uint32_t i = 0; i < n; ++i) { in[i].type = (dtype)dtype_code; in[i].buffer = (void*)inputs[i]; }
+    matrix o;
+    o.buffer = out;
+    o.total_size = (size_t)total;
+    try {
+        switch (op) {
+            case 0: { GreaterPrimitive p; p.a = in[0]; p.b = in[1]; p.collapsed_dims = cd; o.tape = &p; o.greater_backend_cpu(o); break; }
+            case 1: { LessPrimitive p; p.a = in[0]; p.b = in[1]; p.collapsed_dims = cd; o.tape = &p; o.less_backend_cpu(o); break; }
+            case 2: { LogicalAndPrimitive p; p.a = in[0]; p.b = in[1]; p.collapsed_dims = cd; o.tape = &p; o.logical_and_backend_cpu(o); break; }
+            case 3: {
+                WherePrimitive p; in[0].type = dtype::Bool;
+                p.cond = in[0]; p.a = in[1]; p.b = in[2]; p.collapsed_dims = cd; o.tape = &p; o.where_backend_cpu(o); break;
+            }
+            case 4: { FloorPrimitive p; p.input = in[0]; p.collapsed_dims = cd; o.tape = &p; o.floor_backend_cpu(o); break; }
+            default: { FullPrimitive p; p.value = in[0]; p.collapsed_dims = cd; o.tape = &p; o.full_backend_cpu(o); break; }
+        }
+    } catch (...) { return -1; }
+    return 0;
+}
+
+int ref_equal(int dtype_code, void* out, const void* a_buf, const void* b_buf, uint32_t cdims, const uint32_t* shape,
+              const uint32_t* sA, const uint32_t* sB, const uint32_t* sR, uint64_t total) {
+    CollapsedDims_3 res{};
+    res.out_dims = cdims;
+    for (uint32_t i = 0; i < cdims && i < MAX_TENSOR_DIMS; ++i) {
+        res.shape[i] = shape[i]; res.stridesA[i] = sA[i]; res.stridesB[i] = sB[i]; res.stridesC[i] = sR[i];
+    }
+    matrix a, b, output;
+    a.buffer = (void*)a_buf; b.buffer = (void*)b_buf;
+    output.type = (dtype)dtype_code; output.buffer = out; output.total_size = (size_t)total;
+    try { ref_equal_impl(output, a, b, res); } catch (...) { return -1; }
+    return 0;
+}
+
 }  // extern "C"
 """
 
@@ -391,6 +510,61 @@ def extract(ref: Path) -> tuple[str, dict]:
          "dispatch_type(type, result.buffer, [&](auto *out_data) {", occurrence=2)
     frag("EXP", "void matrix::exp(matrix& output, ExecutionDevice exec_device)",
          "dispatch_float_type(type, output.buffer, [&](auto *out_data) {")
+
+    frag("SQRT", "void matrix::sqrt(matrix& output, ExecutionDevice exec_device)",
+         "auto sqrt_cpu = [&](auto *out_data) {")
+    frag("EQUAL", "void matrix::equal_backend(matrix& output, ExecutionDevice exec_device)",
+         "dispatch_type(output.type, output.buffer, [&](auto *out_data) {")
+    # make_pointwise's collapse: the `if (count) { ... }` block
+    mp = matrix_mm.find("matrix make_pointwise(const std::vector<matrix>& inputs,")
+    i = matrix_mm.find("if (count) {", after=mp)
+    s2, e2, text = matrix_mm.block(i, False)
+    manifest["PWCOLLAPSE"] = ["Matrix.mm", s2 + 1, e2 + 1]
+    frags["PWCOLLAPSE"] = f"\n// ---- Matrix.mm:{s2 + 1}-{e2 + 1} (make_pointwise collapse)\n{text}\n"
+
+    # dtype_cast (matrix.h) and ElementwiseDims (primitives.cpp)
+    i = matrix_h.find("inline Dst dtype_cast(Src v) {")
+    parts.append(f"{matrix_h.lines[i - 1]}\n" + take(matrix_h, "dtype_cast", i, False))
+    prim_cpp = Source(ref / "primitives.cpp")
+    parts.append(take(prim_cpp, "ElementwiseDims", prim_cpp.find("struct ElementwiseDims {"), True))
+
+    # stand-in matrix: the fields and no-op hooks the taken member functions use, with
+    # copyCPUinplaceTypeCasted (an inline member in matrix.h) pasted into the struct body
+    copy_cast = take(matrix_h, "copyCPUinplaceTypeCasted",
+                     matrix_h.find("static void copyCPUinplaceTypeCasted(matrix &outMat, const matrix &inMat,"), False)
+    # GCC 13 at -O3 miscompiles the vectorised Float16 <-> BFloat16 conversion loop (it stores the
+    # source bits unconverted); the loop vectoriser is kept off for the stand-in matrix's members.
+    parts.append(
+        "#include <vector>\n"
+        "#pragma GCC push_options\n"
+        "#pragma GCC optimize(\"no-tree-loop-vectorize\")\n"
+        "struct matrix {\n"
+        "    dtype type = dtype::Float; void* buffer = nullptr; size_t total_size = 0; void* tape = nullptr;\n"
+        "    uint32_t dims = 0; size_m shp[MAX_TENSOR_DIMS]{}; size_m str[MAX_TENSOR_DIMS]{};\n"
+        "    const size_m* shape() const { return shp; }\n"
+        "    const size_m* strides() const { return str; }\n"
+        "    void update_from_trace() {}\n"
+        "    void eval_cpu() {}\n"
+        + copy_cast +
+        "    void greater_backend_cpu(matrix& output); void less_backend_cpu(matrix& output);\n"
+        "    void logical_and_backend_cpu(matrix& output); void where_backend_cpu(matrix& output);\n"
+        "    void floor_backend_cpu(matrix& output); void full_backend_cpu(matrix& output);\n"
+        "};\n"
+        "#pragma GCC pop_options\n"
+        "struct GreaterPrimitive { matrix a, b; ElementwiseDims collapsed_dims; };\n"
+        "struct LessPrimitive { matrix a, b; ElementwiseDims collapsed_dims; };\n"
+        "struct LogicalAndPrimitive { matrix a, b; ElementwiseDims collapsed_dims; };\n"
+        "struct WherePrimitive { matrix cond, a, b; ElementwiseDims collapsed_dims; };\n"
+        "struct FloorPrimitive { matrix input; ElementwiseDims collapsed_dims; };\n"
+        "struct FullPrimitive { matrix value; ElementwiseDims collapsed_dims; };\n"
+        "struct PointwiseShim { ElementwiseDims collapsed_dims; };\n")
+    for key, pat in (("greater_backend_cpu", "void matrix::greater_backend_cpu(matrix& output) {"),
+                     ("less_backend_cpu", "void matrix::less_backend_cpu(matrix& output) {"),
+                     ("logical_and_backend_cpu", "void matrix::logical_and_backend_cpu(matrix& output) {"),
+                     ("where_backend_cpu", "void matrix::where_backend_cpu(matrix& output) {"),
+                     ("floor_backend_cpu", "void matrix::floor_backend_cpu(matrix& output) {"),
+                     ("full_backend_cpu", "void matrix::full_backend_cpu(matrix& output) {")):
+        parts.append(take(matrix_mm, key, matrix_mm.find(pat), False))
 
     wrappers = WRAPPERS
     for key, text in frags.items():

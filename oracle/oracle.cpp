@@ -113,6 +113,37 @@ template <typename T> inline T mul_wrap(T a, T b) {
     }
 }
 
+template <typename T> constexpr bool kFloatLike =
+    std::is_same_v<T, float> || std::is_same_v<T, _Float16> || std::is_same_v<T, __bf16>;
+
+// dtype_cast, matrix.h:260-267: a static_cast, through float between the two half types.  A
+// float-like value converted to an integer type is defined in C++ only when its truncation fits the
+// destination; the restatement gives such values the low bits of the 64-bit truncation (saturated at
+// the int64 range, NaN -> 0) instead of undefined behaviour, and the tests compare in-range values.
+template <typename D, typename S> inline D cast_elem(S v) {
+    if constexpr (std::is_same_v<D, S>) {
+        return v;
+    } else if constexpr (std::is_same_v<D, bool>) {
+        return static_cast<bool>(v);
+    } else if constexpr (kFloatLike<S> && std::is_integral_v<D>) {
+        const float f = static_cast<float>(v);
+        if constexpr (std::is_same_v<D, uint64_t>) {
+            if (f >= 0x1p63f) return f >= 0x1p64f ? UINT64_MAX : static_cast<uint64_t>(f);
+        }
+        int64_t t;
+        if (std::isnan(f)) t = 0;
+        else if (f >= 0x1p63f) t = INT64_MAX;
+        else if (f < -0x1p63f) t = INT64_MIN;
+        else t = static_cast<int64_t>(f);
+        return static_cast<D>(static_cast<uint64_t>(t));
+    } else if constexpr ((std::is_same_v<S, _Float16> && std::is_same_v<D, __bf16>) ||
+                         (std::is_same_v<S, __bf16> && std::is_same_v<D, _Float16>)) {
+        return static_cast<D>(static_cast<float>(v));
+    } else {
+        return static_cast<D>(v);
+    }
+}
+
 // Splits [0, n) into `threads` contiguous slices and runs body(lo, hi) on each.
 template <typename Body> void parallel_ranges(uint64_t n, int threads, Body&& body) {
     if (threads <= 1 || n < 4096) { body(uint64_t(0), n); return; }
@@ -476,10 +507,12 @@ int orc_reduce(int op, int dtype, void* out, const void* in, uint32_t rstride, u
 }
 
 // ---------------------------------------------------------------------------
-// Broadcast binary ops.  op: 0 Add, 1 Sub, 2 Mul, 3 Div, 4 Max, 5 Min.
+// Broadcast binary ops.  op: 0 Add, 1 Sub, 2 Mul, 3 Div, 4 Max, 5 Min, 6 Equal.
 //   add/mul/sub/div  Matrix.mm:7475-7498, 7546-7569, 7614-7637, 7683-7706
 //   max(a, b)        Matrix.mm:13459-13474  (std::max: a unless a < b)
 //   min(a, b)        Matrix.mm:14757-14781  (std::min: a unless b < a)
+//   equal(a, b)      Matrix.mm:14521-14538  (T(1) when a == b, else T(0); decoded there with the
+//                    collapsed shape, which gives the same positions for the contiguous result)
 // Output element gid is written at out[gid]; per collapsed axis the index is
 // rem / sR[i], scaled by sA[i] / sB[i] (stride 0 on broadcast axes).
 // cdims == 0 is the scalar case (Matrix.mm:7455-7464).  Integer division by
@@ -487,7 +520,7 @@ int orc_reduce(int op, int dtype, void* out, const void* in, uint32_t rstride, u
 // ---------------------------------------------------------------------------
 int orc_broadcast(int op, int dtype, void* out, const void* a, const void* b, uint32_t cdims, const uint32_t* sR,
                   const uint32_t* sA, const uint32_t* sB, uint64_t total, int threads) {
-    if (cdims > kMaxDims || op < 0 || op > 5) return -1;
+    if (cdims > kMaxDims || op < 0 || op > 6) return -1;
     const bool ok = with_type(dtype, [&](auto* tag) {
         using T = std::remove_pointer_t<decltype(tag)>;
         const T* pa = static_cast<const T*>(a);
@@ -502,7 +535,8 @@ int orc_broadcast(int op, int dtype, void* out, const void* a, const void* b, ui
                     if constexpr (std::is_same_v<T, bool>) return static_cast<bool>(int(x) / int(y));
                     else return static_cast<T>(x / y);
                 case 4: return std::max(x, y);
-                default: return std::min(x, y);
+                case 5: return std::min(x, y);
+                default: return x == y ? T(1) : T(0);
             }
         };
         if (cdims == 0) {
@@ -552,6 +586,177 @@ int orc_exp(int dtype, void* out, const void* in, uint32_t cdims, const uint32_t
         }
     });
     return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Elementwise exp / sqrt on Float or Float16 (op 0 exp, 1 sqrt): Matrix.mm:7014-7063 and
+// 6870-6925 (CPU branches).  The Float16 element is evaluated in float and rounded back, as
+// the reference's float16_t arithmetic does.  Same metadata as orc_exp.
+// ---------------------------------------------------------------------------
+int orc_unary(int op, int dtype, void* out, const void* in, uint32_t cdims, const uint32_t* shape,
+              const uint32_t* sOut, const uint32_t* sIn, uint64_t total, int threads) {
+    if ((dtype != kFloat && dtype != kFloat16) || cdims > kMaxDims || op < 0 || op > 1) return -1;
+    auto run = [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        const T* src = static_cast<const T*>(in);
+        T* dst = static_cast<T*>(out);
+        auto f = [op](T x) -> T {
+            const float v = static_cast<float>(x);
+            return static_cast<T>(op == 0 ? std::exp(v) : std::sqrt(v));
+        };
+        if (cdims == 0) {
+            dst[0] = f(src[0]);
+            return;
+        }
+        parallel_ranges(total, threads, [&](uint64_t lo, uint64_t hi) {
+            for (uint64_t gid = lo; gid < hi; ++gid) {
+                uint64_t si = 0, di = 0, rem = gid;
+                for (int i = (int)cdims - 1; i >= 0; --i) {
+                    const uint64_t idx = rem % shape[i];
+                    si += idx * sIn[i];
+                    di += idx * sOut[i];
+                    rem /= shape[i];
+                }
+                dst[di] = f(src[si]);
+            }
+        });
+    };
+    if (dtype == kFloat) run((float*)nullptr);
+    else run((_Float16*)nullptr);
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// astype / copy: copyCPUinplaceTypeCasted, matrix.h:1474-1544, over
+// collapse_dims(in.shape, out.strides, in.strides) (matrix.h:1481); element
+// conversion dtype_cast (cast_elem above).  The loops there walk the collapsed
+// shape innermost axis fastest; gid is decoded the same way here.
+// ---------------------------------------------------------------------------
+// (GCC 13 at -O3 miscompiles vectorised Float16 <-> BFloat16 conversion loops, storing the source
+// bits unconverted; the loop vectoriser is kept off here.)
+#pragma GCC push_options
+#pragma GCC optimize("no-tree-loop-vectorize")
+int orc_astype(int dst_dtype, int src_dtype, void* out, const void* in, uint32_t cdims, const uint32_t* shape,
+               const uint32_t* sOut, const uint32_t* sIn, uint64_t total, int threads) {
+    if (cdims > kMaxDims) return -1;
+    bool inner_ok = false;
+    const bool ok = with_type(dst_dtype, [&](auto* dtag) {
+        using D = std::remove_pointer_t<decltype(dtag)>;
+        inner_ok = with_type(src_dtype, [&](auto* stag) {
+            using S = std::remove_pointer_t<decltype(stag)>;
+            const S* src = static_cast<const S*>(in);
+            D* dst = static_cast<D*>(out);
+            if (cdims == 0) {
+                dst[0] = cast_elem<D, S>(src[0]);
+                return;
+            }
+            parallel_ranges(total, threads, [&](uint64_t lo, uint64_t hi) {
+                for (uint64_t gid = lo; gid < hi; ++gid) {
+                    uint64_t si = 0, di = 0, rem = gid;
+                    for (int i = (int)cdims - 1; i >= 0; --i) {
+                        const uint64_t idx = rem % shape[i];
+                        si += idx * sIn[i];
+                        di += idx * sOut[i];
+                        rem /= shape[i];
+                    }
+                    dst[di] = cast_elem<D, S>(src[si]);
+                }
+            });
+        });
+    });
+    return ok && inner_ok ? 0 : -1;
+}
+#pragma GCC pop_options
+
+// ---------------------------------------------------------------------------
+// make_pointwise's collapse: Matrix.mm:13537-13555.  Output axes outermost
+// first; extent-1 axes are skipped; an axis folds into the last kept one when
+// the merged extent stays <= INT32_MAX and every input's kept stride equals
+// its stride here times this extent (compared in 64 bits); the kept axis then
+// takes this axis' strides.  in_strides: n rows of out_dims entries; outputs:
+// the collapsed shape (kMaxDims entries) and n rows of kMaxDims strides.
+// Returns the collapsed rank, or UINT32_MAX where the reference throws.
+// ---------------------------------------------------------------------------
+uint32_t orc_pointwise_collapse(const uint32_t* out_shape, uint32_t out_dims, const uint32_t* in_strides,
+                                uint32_t n, uint32_t* cshape, uint32_t* cstrides) {
+    if (out_dims > kMaxDims || n > 3) return UINT32_MAX;
+    uint64_t count = 1;
+    for (uint32_t d = 0; d < out_dims; ++d) {
+        if (out_shape[d] && count > UINT32_MAX / out_shape[d]) return UINT32_MAX;
+        count *= out_shape[d];
+    }
+    std::fill(cshape, cshape + kMaxDims, 0u);
+    std::fill(cstrides, cstrides + n * kMaxDims, 0u);
+    uint32_t dims = 0;
+    if (!count) return 0;
+    for (uint32_t d = 0; d < out_dims; ++d) {
+        if (out_shape[d] == 1) continue;
+        bool merge = dims > 0 && uint64_t(cshape[dims - 1]) * out_shape[d] <= INT32_MAX;
+        if (merge) {
+            for (uint32_t i = 0; i < n; ++i) {
+                if (uint64_t(cstrides[i * kMaxDims + dims - 1]) != uint64_t(in_strides[i * out_dims + d]) * out_shape[d]) {
+                    merge = false;
+                    break;
+                }
+            }
+        }
+        const uint32_t target = merge ? dims - 1 : dims++;
+        if (merge) cshape[target] *= out_shape[d];
+        else cshape[target] = out_shape[d];
+        for (uint32_t i = 0; i < n; ++i) cstrides[i * kMaxDims + target] = in_strides[i * out_dims + d];
+    }
+    return dims;
+}
+
+// ---------------------------------------------------------------------------
+// The make_pointwise family's CPU backends: op 0 greater (Matrix.mm:13803-13874),
+// 1 less (13876-13947), 2 logical_and (13949-14020), 3 where (14022-14103),
+// 4 floor (13741-13801), 5 full (14105-14165).  The output is contiguous and
+// written in order (dst[i++]); input k is read at sum idx * strides[k][axis]
+// (kMaxDims entries per row).  dtype is the inputs' common dtype (Bool for
+// logical_and; the dtype of a and b for where, whose cond is Bool).  Greater,
+// less and logical_and write bool.  cdims == 0 is one element at offset 0.
+// ---------------------------------------------------------------------------
+int orc_pointwise(int op, int dtype, void* out, const void* const* inputs, uint32_t n, uint32_t cdims,
+                  const uint32_t* shape, const uint32_t* strides, uint64_t total, int threads) {
+    static const uint32_t kArity[] = {2, 2, 2, 3, 1, 1};
+    if (op < 0 || op > 5 || n != kArity[op] || cdims > kMaxDims) return -1;
+    if (op == 2 && dtype != kBool) return -1;
+    const bool ok = with_type(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        auto offset = [&](uint64_t gid, uint32_t k) {
+            uint64_t off = 0, rem = gid;
+            for (int i = (int)cdims - 1; i >= 0; --i) {
+                off += (rem % shape[i]) * strides[k * kMaxDims + i];
+                rem /= shape[i];
+            }
+            return off;
+        };
+        parallel_ranges(cdims == 0 ? 1 : total, threads, [&](uint64_t lo, uint64_t hi) {
+            for (uint64_t gid = lo; gid < hi; ++gid) {
+                if (op == 0 || op == 1 || op == 2) {
+                    const T* a = static_cast<const T*>(inputs[0]);
+                    const T* b = static_cast<const T*>(inputs[1]);
+                    const T x = a[offset(gid, 0)], y = b[offset(gid, 1)];
+                    bool r;
+                    if (op == 0) r = x > y;
+                    else if (op == 1) r = x < y;
+                    else r = bool(x) && bool(y);
+                    static_cast<bool*>(out)[gid] = r;
+                } else if (op == 3) {
+                    const bool* c = static_cast<const bool*>(inputs[0]);
+                    const T* a = static_cast<const T*>(inputs[1]);
+                    const T* b = static_cast<const T*>(inputs[2]);
+                    static_cast<T*>(out)[gid] = c[offset(gid, 0)] ? a[offset(gid, 1)] : b[offset(gid, 2)];
+                } else {
+                    const T x = static_cast<const T*>(inputs[0])[offset(gid, 0)];
+                    if (op == 5 || std::is_integral_v<T>) static_cast<T*>(out)[gid] = x;
+                    else static_cast<T*>(out)[gid] = cast_elem<T, float>(std::floor(static_cast<float>(x)));
+                }
+            }
+        });
+    });
+    return ok ? 0 : -1;
 }
 
 }  // extern "C"

@@ -35,7 +35,9 @@ DTYPES = {
 }
 BF16 = 10  # numpy has no bfloat16: its bits travel as uint16 with an explicit dtype code
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
-BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5}
+BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5, "equal": 6}
+UNARY_OPS = {"exp": 0, "sqrt": 1}
+POINTWISE_OPS = {"greater": 0, "less": 1, "logical_and": 2, "where": 3, "floor": 4, "full": 5}
 
 U32P = C.POINTER(C.c_uint32)
 
@@ -90,6 +92,12 @@ class CpuEval:
         fn("reduce", i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P, u64] + extra)
         fn("broadcast", i32, [i32, i32, vp, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
         fn("exp", i32, [i32, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
+        fn("unary", i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
+        fn("astype", i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
+        fn("pointwise_collapse", u32, [U32P, u32, U32P, u32, U32P, U32P])
+        fn("pointwise", i32, [i32, i32, vp, C.POINTER(vp), u32, u32, U32P, U32P, u64] + extra)
+        if prefix == "ref_":
+            fn("equal", i32, [i32, vp, vp, vp, u32, U32P, U32P, U32P, U32P, u64])
 
     # -- shape folding ---------------------------------------------------------------------
     def collapse(self, shape, *strides, cap=INT32_MAX):
@@ -182,10 +190,15 @@ class CpuEval:
         total = int(np.prod(meta["out_shape"], dtype=np.int64)) if meta["out_shape"] else 1
         out = np.empty(max(total, 1), dtype=a_base.dtype)
         code = DTYPES[a_base.dtype] if dtype_code is None else dtype_code
-        rc = self._f["broadcast"](BINARY_OPS[op], code, out.ctypes.data,
-                                  a_base.ctypes.data + a_off * a_base.itemsize,
-                                  b_base.ctypes.data + b_off * b_base.itemsize, meta["cdims"], _arr(meta["sr"]),
-                                  _arr(meta["sa"]), _arr(meta["sb"]), total, *self._thr())
+        pa = a_base.ctypes.data + a_off * a_base.itemsize
+        pb = b_base.ctypes.data + b_off * b_base.itemsize
+        if op == "equal" and self.prefix == "ref_":
+            # the reference's own equal loop (matrix::equal_backend), same collapse_dims_3 metadata
+            rc = self._f["equal"](code, out.ctypes.data, pa, pb, meta["cdims"], _arr(meta["shape"]),
+                                  _arr(meta["sa"]), _arr(meta["sb"]), _arr(meta["sr"]), total)
+        else:
+            rc = self._f["broadcast"](BINARY_OPS[op], code, out.ctypes.data, pa, pb, meta["cdims"], _arr(meta["sr"]),
+                                      _arr(meta["sa"]), _arr(meta["sb"]), total, *self._thr())
         if rc != 0:
             raise RuntimeError(f"{self.prefix}broadcast failed")
         return out[:total].reshape(meta["out_shape"])
@@ -208,6 +221,109 @@ class CpuEval:
         if rc != 0:
             raise RuntimeError(f"{self.prefix}exp failed")
         return out[:total].reshape(x.shape)
+
+
+    def unary(self, op, x: np.ndarray, dtype_code=None):
+        """matrix::exp / matrix::sqrt on a Float or Float16 view (the frontends promote other
+        dtypes with astype first)."""
+        base, offset = _base_and_offset(x)
+        meta = self.unary_meta(list(x.shape), elem_strides(x))
+        total = int(np.prod(x.shape, dtype=np.int64)) if x.shape else 1
+        out = np.empty(max(total, 1), dtype=x.dtype)
+        code = DTYPES[x.dtype] if dtype_code is None else dtype_code
+        rc = self._f["unary"](UNARY_OPS[op], code, out.ctypes.data, base.ctypes.data + offset * base.itemsize,
+                              meta["cdims"], _arr(meta["shape"]), _arr(meta["s_out"]), _arr(meta["s_in"]), total,
+                              *self._thr())
+        if rc != 0:
+            raise RuntimeError(f"{self.prefix}unary failed")
+        return out[:total].reshape(x.shape)
+
+    def astype(self, x: np.ndarray, dst, make_contig=True, src_code=None, dst_code=None):
+        """x.astype(dst, make_contig).eval_cpu() (Matrix.mm:8384-8398, 8400-8412).  With make_contig
+        the output is row-major; otherwise it takes the input's strides (broadcast axes included),
+        as the promotion path's astype(common) does.  dst: a numpy dtype (the output's storage);
+        src_code / dst_code override the dtype codes (BFloat16 bits held as uint16)."""
+        base, offset = _base_and_offset(x)
+        shape, s_in = list(x.shape), elem_strides(x)
+        s_out = row_major(shape) if make_contig else list(s_in)
+        total = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        span = 1 + sum((e - 1) * st for e, st in zip(shape, s_out)) if total else 0
+        out = np.zeros(max(span, 1), dtype=dst)
+        sc = DTYPES[x.dtype] if src_code is None else src_code
+        dc = DTYPES[np.dtype(dst)] if dst_code is None else dst_code
+        src_ptr = base.ctypes.data + offset * base.itemsize
+        if self.prefix == "ref_":  # copyCPUinplaceTypeCasted collapses the metadata itself
+            rc = self._f["astype"](dc, sc, out.ctypes.data, src_ptr, len(shape), _arr(shape), _arr(s_out),
+                                   _arr(s_in), total)
+        else:
+            k, (cshape, so, si) = self.collapse(shape, s_out, s_in, cap=INT32_MAX)
+            rc = self._f["astype"](dc, sc, out.ctypes.data, src_ptr, k, _arr(cshape), _arr(so), _arr(si), total,
+                                   *self._thr())
+        if rc != 0:
+            raise RuntimeError(f"{self.prefix}astype failed")
+        if total == 0:
+            return np.zeros(shape, dtype=dst)
+        return np.lib.stride_tricks.as_strided(out, shape=shape, strides=[st * out.itemsize for st in s_out])
+
+    def pointwise_collapse(self, out_shape, in_strides):
+        """make_pointwise's collapse (Matrix.mm:13537-13555); in_strides: one list per input,
+        right-aligned to the output rank, 0 on broadcast axes."""
+        n, d = len(in_strides), len(out_shape)
+        flat = (C.c_uint32 * max(1, n * d))(*[int(v) & 0xFFFFFFFF for row in in_strides for v in row])
+        cshape = _arr([])
+        cstr = (C.c_uint32 * (3 * MAX_DIMS))()
+        k = self._f["pointwise_collapse"](_arr(out_shape, max(d, 1)), d, flat, n, cshape, cstr)
+        if k == UINT32_MAX:
+            raise ValueError("pointwise collapse refused the shape")
+        return k, list(cshape[:k]), [list(cstr[i * MAX_DIMS:i * MAX_DIMS + k]) for i in range(n)]
+
+    def pointwise_meta(self, inputs):
+        """pointwise_shape + make_pointwise (Matrix.mm:13497-13556) for numpy views: the broadcast
+        output shape, each input's right-aligned strides (0 where its extent is 1) and the collapse."""
+        rank = max((x.ndim for x in inputs), default=0)
+        shape = [1] * rank
+        for x in inputs:
+            for d, m in enumerate(x.shape):
+                n = shape[rank - x.ndim + d]
+                if n == 1:
+                    shape[rank - x.ndim + d] = m
+                elif m != 1 and n != m:
+                    raise ValueError("incompatible pointwise broadcast shapes")
+        rows = []
+        for x in inputs:
+            st = [0] * rank
+            for d, (m, s) in enumerate(zip(x.shape, elem_strides(x))):
+                st[rank - x.ndim + d] = 0 if m == 1 else s
+            rows.append(st)
+        k, cshape, cstr = self.pointwise_collapse(shape, rows)
+        return dict(out_shape=shape, cdims=k, shape=cshape, strides=cstr)
+
+    def pointwise(self, op, inputs, dtype_code=None):
+        """greater / less / logical_and / where / floor / full over numpy views already cast to their
+        common dtype (cond of where: bool).  Returns the contiguous output."""
+        meta = self.pointwise_meta(inputs)
+        total = int(np.prod(meta["out_shape"], dtype=np.int64)) if meta["out_shape"] else 1
+        data = inputs[-1]
+        odt = np.bool_ if op in ("greater", "less", "logical_and") else data.dtype
+        out = np.zeros(max(total, 1), dtype=odt)
+        code = DTYPES[data.dtype] if dtype_code is None else dtype_code
+        if op == "logical_and":
+            code = DTYPES[np.dtype(np.bool_)]
+        ptrs = []
+        for x in inputs:
+            b, o = _base_and_offset(x)
+            ptrs.append(b.ctypes.data + o * b.itemsize)
+        arr = (C.c_void_p * 3)(*ptrs)
+        st = (C.c_uint32 * (3 * MAX_DIMS))()
+        for i, row in enumerate(meta["strides"]):
+            for j, v in enumerate(row):
+                st[i * MAX_DIMS + j] = v
+        if total:
+            rc = self._f["pointwise"](POINTWISE_OPS[op], code, out.ctypes.data, arr, len(inputs), meta["cdims"],
+                                      _arr(meta["shape"]), st, total, *self._thr())
+            if rc != 0:
+                raise RuntimeError(f"{self.prefix}pointwise failed")
+        return out[:total].reshape(meta["out_shape"])
 
 
 def _base_and_offset(x: np.ndarray):

@@ -17,7 +17,8 @@ def declared_functions():
 def test_header_declares_the_hot_path():
     names = declared_functions()
     for must in ("mtxc_init", "mtxc_reduce", "mtxc_broadcast_binary", "mtxc_unary", "mtxc_collapse_dims_reduce2",
-                 "mtxc_broadcast_shapes", "mtxc_sync", "mtxc_graph_begin"):
+                 "mtxc_broadcast_shapes", "mtxc_sync", "mtxc_graph_begin", "mtxc_astype", "mtxc_pointwise",
+                 "mtxc_pointwise_collapse"):
         assert must in names
 
 
