@@ -308,7 +308,9 @@ int mtxc_astype(int dst_dtype, int src_dtype, void* dst, const void* src, uint32
  *   FLOOR (1 input)                         -> dtype: floor for float-likes, identity otherwise
  *   FULL (1 input, the broadcast value)     -> dtype: the value
  * Results are bit-exact with the CPU backends (Matrix.mm:13741-14166).  The output must not exceed
- * 2^32 - 1 elements (make_pointwise's limit). */
+ * 2^32 - 1 elements (make_pointwise's limit).  An empty output needs no call: its collapsed rank is 0,
+ * as for a single element, and the reference's backends return before reading anything
+ * (`if (!output.total_size) return;`). */
 int mtxc_pointwise(int op, int dtype, void* dst, const void* const* inputs, uint32_t n_inputs, uint32_t cdims,
                    const uint32_t* shape, const uint32_t* strides);
 

@@ -94,6 +94,11 @@ extern "C" int mtxc_astype(int dst_dtype, int src_dtype, void* dst, const void* 
     if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_astype: cdims > MTXC_MAX_DIMS");
     if (cdims && (!shape || !dst_strides || !src_strides))
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_astype: null metadata pointer");
+    auto known = [](int code) { return dispatch_dtype(code, [](auto*) {}); };
+    if (!known(dst_dtype) || !known(src_dtype))
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_astype: no kernel for ") + dtype_name(src_dtype) +
+                                                    " -> " + dtype_name(dst_dtype));
+    if (cdims && product(shape, cdims) == 0) return MTXC_OK;  // nothing to convert
     if (!dst || !src) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_astype: null buffer");
     ThreadCtx& c = ctx();
     ew::MapDesc m{};

@@ -188,6 +188,7 @@ extern "C" int mtxc_unary(int op, int dtype, void* dst, const void* src, uint32_
     if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: cdims > MTXC_MAX_DIMS");
     if (cdims && (!shape || !dst_strides || !src_strides))
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: null metadata pointer");
+    if (cdims && product(shape, cdims) == 0) return MTXC_OK;
     if (!dst || !src) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_unary: null buffer");
     ThreadCtx& c = ctx();
     if (op == MTXC_UNARY_EXP && dtype == MTXC_FLOAT)

@@ -29,7 +29,7 @@ def dev(a: np.ndarray, code):
     """numpy storage -> device tensor of dtype `code`, keeping the view's shape and strides."""
     import torch
 
-    base = np.ascontiguousarray(a)
+    base = np.array(a, order="C", copy=True)  # (np.ascontiguousarray would make a 0-d array 1-d)
     t = torch.from_numpy(base).cuda()
     return t.view(torch.bfloat16) if code == 10 else t
 
@@ -153,7 +153,7 @@ def test_pointwise_family(gpu, port, code):
         cond = rng.integers(0, 2, int(np.prod(s2))).astype(np.bool_).reshape(s2)
         at = dev(a, code)
         # a transposed view of `a` exercises the generic decode with the same values
-        aT, atT = (a.T, at.T) if a.ndim >= 2 else (a, at)
+        aT, atT = (a.T, at.mT) if a.ndim == 2 else (a, at)
         d = values(rng, code, int(np.prod(s0)), special=True).reshape(aT.shape)
         cases = [("greater", [a, b]), ("less", [aT, d]), ("where", [cond, a, c]), ("floor", [aT]), ("full", [b])]
         if code == 7:
