@@ -214,6 +214,26 @@ uint32_t mtxc_pointwise_collapse(const uint32_t* out_shape, uint32_t out_dims, c
 int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
                 uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides, const uint32_t* src_strides);
 
+/* Fused statistics over one axis: matrix::mean / rms / norm (Matrix.mm:15220-15276), which the
+ * reference composes from its primitives:
+ *     MEAN  sum(x) / (float)n            RMS  sqrt(mean(x * x))            NORM  sqrt(sum(x * x))
+ * with n = reduce_len.  One read of x instead of the three to five kernels of the composition; the
+ * metadata is mtxc_reduce's.  The result is what the composition computes: x * x in the input dtype
+ * (wrapping for integers), the sum rounded to the input dtype (integer sums wrap), one division by
+ * (float)n converted to scalar_operand_type's dtype (matrix.h:1815-1846), one correctly rounded sqrt
+ * in promote_types(type, Float16).  The output dtype therefore depends on the input dtype (and for
+ * Float16 on n): mtxc_reduce_stat_dtype gives it.  Integer and Bool inputs give bit-exact results; float
+ * sums are summed in a different order (fp32 tree instead of the reference's sequential sum in T), so
+ * float results agree within rounding.  Workspace: as mtxc_reduce's SUM. */
+enum { MTXC_STAT_MEAN = 0, MTXC_STAT_RMS = 1, MTXC_STAT_NORM = 2 };
+int mtxc_reduce_stat(int stat, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
+                     uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides, const uint32_t* src_strides);
+/* The dtype code mtxc_reduce_stat writes for (stat, input dtype, reduce_len), or -1:
+ *   MEAN: Float -> Float, BFloat16 -> BFloat16, Float16 -> Float16 when n <= 65504 else Float, others -> Float
+ *   RMS:  Float16 -> Float16 when n <= 65504 else Float, every other dtype -> Float
+ *   NORM: Float16 and Bool -> Float16, every other dtype -> Float */
+int mtxc_reduce_stat_dtype(int stat, int dtype, uint32_t reduce_len);
+
 /* Max and ArgMax (op MAX or ARGMAX) or Min and ArgMin (op MIN or ARGMIN) from a single read of the
  * input: dst_values receives exactly what mtxc_reduce(MAX / MIN) writes and dst_indices exactly what
  * mtxc_reduce(ARGMAX / ARGMIN) writes, for the same metadata.  Serves the reference's

@@ -23,6 +23,7 @@ ERR_WORKSPACE = 7
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
 BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5, "equal": 6}
 UNARY_OPS = {"exp": 0, "sqrt": 1}
+STATS = {"mean": 0, "rms": 1, "norm": 2}
 POINTWISE_OPS = {"greater": 0, "less": 1, "logical_and": 2, "where": 3, "floor": 4, "full": 5}
 
 
@@ -82,6 +83,8 @@ def lib() -> C.CDLL:
             "mtxc_unary": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),
             "mtxc_softmax_lastdim": (i32, [i32, vp, vp, u64, u32, u64, u64]),
             "mtxc_astype": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),
+            "mtxc_reduce_stat": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P]),
+            "mtxc_reduce_stat_dtype": (i32, [i32, i32, u32]),
             "mtxc_pointwise_collapse": (u32, [U32P, u32, U32P, u32, U32P, U32P]),
             "mtxc_pointwise": (i32, [i32, i32, vp, C.POINTER(vp), u32, u32, U32P, U32P]),
             "mtxc_graph_begin": (i32, []),

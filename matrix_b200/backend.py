@@ -173,6 +173,23 @@ def reduce(op: str, x: torch.Tensor, axis: int, keepdims: bool = False, out: tor
     return out
 
 
+CODE_TO_TORCH = {v: k for k, v in TORCH_DTYPES.items()}
+
+
+def stat(kind: str, x: torch.Tensor, axis: int, keepdims: bool = False, meta: ReduceMeta | None = None):
+    """x.mean / rms / norm(axis, keepdims) in one pass (mtxc_reduce_stat).  The output dtype is the
+    one the reference's composition ends in (mtxc_reduce_stat_dtype)."""
+    code = dtype_code(x.dtype)
+    if meta is None:
+        meta = reduce_meta(list(x.shape), _check_strides(x), axis, keepdims)
+    oc = lib().mtxc_reduce_stat_dtype(_abi.STATS[kind], code, meta.rlen)
+    out = torch.empty(meta.out_shape, dtype=CODE_TO_TORCH[oc], device=x.device)
+    shape, s_out, s_in = meta.arrays
+    check(lib().mtxc_reduce_stat(_abi.STATS[kind], code, out.data_ptr(), x.data_ptr(), meta.rstride & 0xFFFFFFFF,
+                                 meta.rlen, meta.cdims, shape, s_out, s_in))
+    return out
+
+
 def binary_launch(op: str, a_ptr: int, b_ptr: int, dtype: int, out_ptr: int, meta: BinaryMeta) -> None:
     shape, sr, sa, sb = meta.arrays
     check(lib().mtxc_broadcast_binary(_abi.BINARY_OPS[op], dtype, out_ptr, a_ptr, b_ptr, meta.cdims, shape, sr, sa,

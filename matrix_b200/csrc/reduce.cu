@@ -73,12 +73,16 @@ __device__ __forceinline__ T shfl_xor(T v, int mask) {
 struct Out {
     void* v;
     int32_t* i;
+    uint32_t n = 0;  // reduced length (the divisor of a mean)
 };
 
 // Internal op codes beyond the public ones: ArgMax / ArgMin writing both the extreme value and its
-// first index (mtxc_reduce_pair).
+// first index (mtxc_reduce_pair), and the fused statistics of mtxc_reduce_stat.
 constexpr int kPairMax = 5;
 constexpr int kPairMin = 6;
+constexpr int kStatMean = 7;
+constexpr int kStatRms = 8;
+constexpr int kStatNorm = 9;
 
 template <int OP, typename T>
 struct Reducer;
@@ -182,6 +186,103 @@ struct Reducer<kPairMin, T> : PairExtremum<T, false> {
         o.i[gid] = s.i;
     }
 };
+
+// ------------------------------------------------------------------------------------------
+// Fused statistics: mean = sum / (float)n, rms = sqrt(mean(x * x)), norm = sqrt(sum(x * x)), as
+// the reference composes them from its primitives (Matrix.mm:15220-15276), in one pass.
+//   * x * x is the reference's element product in T: fp32 product rounded once to T for the
+//     float-likes, the wrapped product for integers, x itself for Bool.
+//   * the sum is the Sum reducer's (fp32 for float-likes, wrapping integer, logical-or Bool),
+//     rounded to T once: the SumPrimitive's output.
+//   * the division is `sum / (float)n` with the scalar in scalar_operand_type's dtype (matrix.h:
+//     1815-1846): Float and BFloat16 keep their type (the divisor rounded to it), Float16 keeps its
+//     type when n <= 65504, everything else divides in Float after astype.  One rounded division.
+//   * sqrt runs in promote_types(type, Float16) (Matrix.mm:6798-6811): Float16 stays half, Bool
+//     becomes half, BFloat16 and the integers become Float.  One correctly rounded square root.
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ T square_in_type(T v) {
+    if constexpr (std::is_same_v<T, float>) return __fmul_rn(v, v);
+    else if constexpr (Traits<T>::kFloat) return from_float<T>(__fmul_rn(to_float(v), to_float(v)));
+    else if constexpr (Traits<T>::kBool) return v;
+    else {
+        using W = std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>;
+        return (T)(W)((W)v * (W)v);
+    }
+}
+
+// float value of an element (integers round to nearest, Bool is 0 / 1)
+template <typename T>
+__device__ __forceinline__ float as_float(T v) {
+    if constexpr (Traits<T>::kFloat) return to_float(v);
+    else if constexpr (Traits<T>::kBool) return (uint8_t)v ? 1.0f : 0.0f;
+    else return static_cast<float>(v);
+}
+
+template <int OP, typename T>
+struct StatReducer : Reducer<MTXC_REDUCE_SUM, T> {
+    using Sum = Reducer<MTXC_REDUCE_SUM, T>;
+    using State = typename Sum::State;
+    __device__ static void fold(State& s, T v, uint32_t i) { Sum::fold(s, OP == kStatMean ? v : square_in_type(v), i); }
+    // sum / (float)n in the division's dtype; *as_half tells whether that dtype is Float16
+    __device__ static float mean_of(T sum, uint32_t n, bool* as_half) {
+        const float nf = (float)n;
+        *as_half = false;
+        if constexpr (std::is_same_v<T, float>) {
+            return __fdiv_rn(sum, nf);
+        } else if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+            return to_float(from_float<T>(__fdiv_rn(to_float(sum), to_float(from_float<T>(nf)))));
+        } else if constexpr (std::is_same_v<T, __half>) {
+            if (n <= 65504u) {
+                *as_half = true;
+                return to_float(from_float<T>(__fdiv_rn(to_float(sum), to_float(from_float<T>(nf)))));
+            }
+            return __fdiv_rn(to_float(sum), nf);
+        } else {
+            return __fdiv_rn(as_float(sum), nf);
+        }
+    }
+    __device__ static void store(const Out& o, uint64_t gid, const State& s) {
+        T sum;  // the SumPrimitive's output
+        if constexpr (Traits<T>::kFloat) sum = from_float<T>(s);
+        else if constexpr (Traits<T>::kBool) sum = mbool(s != 0);
+        else sum = (T)s;
+        if constexpr (OP == kStatNorm) {
+            if constexpr (std::is_same_v<T, __half> || Traits<T>::kBool)
+                static_cast<__half*>(o.v)[gid] = __float2half_rn(sqrtf(as_float(sum)));
+            else
+                static_cast<float*>(o.v)[gid] = sqrtf(as_float(sum));
+        } else {
+            bool as_half;
+            const float m = mean_of(sum, o.n, &as_half);
+            if constexpr (OP == kStatMean) {
+                if constexpr (std::is_same_v<T, __nv_bfloat16>) static_cast<T*>(o.v)[gid] = __float2bfloat16_rn(m);
+                else if (as_half) static_cast<__half*>(o.v)[gid] = __float2half_rn(m);
+                else static_cast<float*>(o.v)[gid] = m;
+            } else {  // rms: sqrt of the mean, half only when the mean is half
+                if (as_half) static_cast<__half*>(o.v)[gid] = __float2half_rn(sqrtf(m));
+                else static_cast<float*>(o.v)[gid] = sqrtf(m);
+            }
+        }
+    }
+};
+template <typename T>
+struct Reducer<kStatMean, T> : StatReducer<kStatMean, T> {};
+template <typename T>
+struct Reducer<kStatRms, T> : StatReducer<kStatRms, T> {};
+template <typename T>
+struct Reducer<kStatNorm, T> : StatReducer<kStatNorm, T> {};
+
+// Output dtype of a statistic (the dtype the reference's composition ends in).
+int stat_out_dtype(int op, int dtype, uint32_t n) {
+    switch (dtype) {
+        case MTXC_FLOAT: return MTXC_FLOAT;
+        case MTXC_FLOAT16: return op == kStatNorm || n <= 65504u ? MTXC_FLOAT16 : MTXC_FLOAT;
+        case MTXC_BFLOAT16: return op == kStatMean ? MTXC_BFLOAT16 : MTXC_FLOAT;
+        case MTXC_BOOL: return op == kStatNorm ? MTXC_FLOAT16 : MTXC_FLOAT;
+        default: return MTXC_FLOAT;
+    }
+}
 
 template <typename R>
 __device__ __forceinline__ void warp_reduce(typename R::State& s) {
@@ -635,6 +736,9 @@ int launch_reduce_op(int op, const Meta& m, const Out dst, const void* src, uint
         case MTXC_REDUCE_ARGMIN: return launch_reduce<MTXC_REDUCE_ARGMIN, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
         case kPairMax: return launch_reduce<kPairMax, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
         case kPairMin: return launch_reduce<kPairMin, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case kStatMean: return launch_reduce<kStatMean, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case kStatRms: return launch_reduce<kStatRms, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
+        case kStatNorm: return launch_reduce<kStatNorm, T>(m, dst, src, rstride, len, ws, wsb, sms, st);
         default: return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: unknown op");
     }
 }
@@ -649,6 +753,9 @@ size_t partial_bytes_op(int op, const Meta& m, const void* src, uint32_t rstride
         case MTXC_REDUCE_ARGMAX: return plan_reduce<MTXC_REDUCE_ARGMAX, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
         case kPairMax: return plan_reduce<kPairMax, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
         case kPairMin: return plan_reduce<kPairMin, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
+        case kStatMean:
+        case kStatRms:
+        case kStatNorm: return plan_reduce<MTXC_REDUCE_SUM, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
         default: return plan_reduce<MTXC_REDUCE_ARGMIN, T>(m, src, rstride, len, unlimited, sms).partial_bytes;
     }
 }
@@ -698,6 +805,36 @@ extern "C" int mtxc_reduce(int op, int dtype, void* dst, const void* src, uint32
     });
     if (!known)
         return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_reduce: no kernel for dtype ") + dtype_name(dtype));
+    return rc;
+}
+
+extern "C" int mtxc_reduce_stat_dtype(int stat, int dtype, uint32_t reduce_len) {
+    if (stat < MTXC_STAT_MEAN || stat > MTXC_STAT_NORM) return -1;
+    if (!dispatch_dtype(dtype, [](auto*) {})) return -1;
+    return stat_out_dtype(kStatMean + stat, dtype, reduce_len);
+}
+
+extern "C" int mtxc_reduce_stat(int stat, int dtype, void* dst, const void* src, uint32_t reduce_stride,
+                                uint32_t reduce_len, uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides,
+                                const uint32_t* src_strides) {
+    if (int rc = require_init()) return rc;
+    if (stat < MTXC_STAT_MEAN || stat > MTXC_STAT_NORM)
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_stat: unknown statistic");
+    Meta m;
+    if (int rc = make_meta(cdims, shape, dst_strides, src_strides, m)) return rc;
+    if (!dispatch_dtype(dtype, [](auto*) {}))
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_reduce_stat: no kernel for dtype ") + dtype_name(dtype));
+    if (product(m.shape, m.cdims) == 0) return MTXC_OK;
+    if (!dst || (!src && reduce_len)) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce_stat: null buffer");
+    ThreadCtx& c = ctx();
+    int rc = MTXC_OK;
+    Out out{dst, nullptr};
+    out.n = reduce_len;
+    dispatch_dtype(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        rc = launch_reduce_op<T>(kStatMean + stat, m, out, src, reduce_stride, reduce_len, c.workspace,
+                                 c.workspace_bytes, c.sm_count, c.stream());
+    });
     return rc;
 }
 

@@ -34,6 +34,9 @@ DTYPES = {
     np.dtype(np.uint64): 12, np.dtype(np.float16): 1, np.dtype(np.bool_): 7,
 }
 BF16 = 10  # numpy has no bfloat16: its bits travel as uint16 with an explicit dtype code
+# numpy storage of each dtype code (BFloat16 bits in uint16)
+STORAGE = {0: np.float32, 1: np.float16, 2: np.uint8, 3: np.int32, 4: np.int16, 5: np.uint32, 6: np.uint16,
+           7: np.bool_, 8: np.int8, 10: np.uint16, 11: np.int64, 12: np.uint64}
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
 BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5, "equal": 6}
 UNARY_OPS = {"exp": 0, "sqrt": 1}
@@ -324,6 +327,47 @@ class CpuEval:
             if rc != 0:
                 raise RuntimeError(f"{self.prefix}pointwise failed")
         return out[:total].reshape(meta["out_shape"])
+
+
+    # -- mean / rms / norm: the reference's compositions (Matrix.mm:15220-15276) ------------
+    def _scalar_type(self, value: float, code: int) -> int:
+        """scalar_operand_type(float scalar, code) (matrix.h:1815-1822) for a float scalar."""
+        if code in (0, BF16, 9):
+            return code
+        if code == 1:
+            return 1 if -65504 <= value <= 65504 else 0
+        return 0
+
+    def _sqrt(self, v: np.ndarray, code: int):
+        """matrix::sqrt(v): astype to promote_types(code, Float16), then the sqrt loop."""
+        oc = self.promote(code, 1)
+        if oc != code:
+            v = self.astype(v, STORAGE[oc], src_code=code, dst_code=oc)
+        return self.unary("sqrt", np.asarray(v), dtype_code=oc), oc
+
+    def _div_by(self, s: np.ndarray, code: int, value: float):
+        """s / value with the reference's scalar rules (operator/(matrix, T), matrix.h:1868)."""
+        sc = self._scalar_type(value, code)
+        common = self.promote(code, sc)
+        lhs = s if code == common else self.astype(s, STORAGE[common], src_code=code, dst_code=common)
+        rhs = self.astype(np.array(value, dtype=np.float32), STORAGE[sc], dst_code=sc)  # matrix::scalar
+        if sc != common:
+            rhs = self.astype(rhs, STORAGE[common], src_code=sc, dst_code=common)
+        return self.binary("div", np.asarray(lhs), np.asarray(rhs), dtype_code=common), common
+
+    def stat(self, kind: str, x: np.ndarray, axis: int, keepdims=False, dtype_code=None):
+        """x.mean / rms / norm(axis, keepdims).eval_cpu() as the reference composes them from its
+        primitives.  Returns (result, result dtype code)."""
+        code = DTYPES[x.dtype] if dtype_code is None else dtype_code
+        data = self.binary("mul", x, x, dtype_code=code) if kind in ("rms", "norm") else x
+        s = self.reduce("sum", data, axis, keepdims, dtype_code=code)
+        if kind == "norm":
+            return self._sqrt(s, code)
+        n = x.shape[axis]
+        m, mcode = self._div_by(s, code, float(np.float32(n)))
+        if kind == "mean":
+            return m, mcode
+        return self._sqrt(m, mcode)
 
 
 def _base_and_offset(x: np.ndarray):

@@ -188,3 +188,32 @@ def test_pointwise_backends_match_reference(port, ref, code):
             x = port.pointwise(op, ins, dtype_code=code)
             y = ref.pointwise(op, ins, dtype_code=code)
             assert same(x, y), (op, code, [i.shape for i in ins])
+
+
+@pytest.mark.parametrize("code", ALL_CODES)
+def test_stat_compositions_match_reference(port, ref, code):
+    """mean / rms / norm composed from the primitives (mul, sum, astype, scalar division, sqrt) give
+    the same bits through the restatement and through the reference's own loops."""
+    rng = np.random.default_rng(60 + code)
+    for shape, axis in (([4, 300], 1), ([300, 3], 0), ([2, 3, 50], 1), ([5], 0), ([3, 0], 1)):
+        x = values(rng, code, int(np.prod(shape)), special=False).reshape(shape)
+        for kind in ("mean", "rms", "norm"):
+            for keep in (False, True):
+                a, ca = port.stat(kind, x, axis, keep, dtype_code=code)
+                b, cb = ref.stat(kind, x, axis, keep, dtype_code=code)
+                assert ca == cb and same(a, b), (code, kind, shape, axis, keep)
+
+
+def test_stat_output_dtypes(port):
+    """The product's mtxc_reduce_stat_dtype equals the dtype the composition ends in."""
+    from matrix_b200 import _abi
+
+    L = _abi.lib()
+    rng = np.random.default_rng(61)
+    for code in ALL_CODES:
+        for n in (5, 65504, 65505):
+            x = values(rng, code, n).reshape(1, n)
+            for k, kind in enumerate(("mean", "rms", "norm")):
+                _, oc = port.stat(kind, x, 1, dtype_code=code)
+                assert L.mtxc_reduce_stat_dtype(k, code, n) == oc, (code, n, kind)
+    assert L.mtxc_reduce_stat_dtype(0, 9, 4) == -1 and L.mtxc_reduce_stat_dtype(3, 0, 4) == -1
