@@ -6,11 +6,11 @@
 // input (0 on broadcast axes).  Two kernels:
 //
 //  * map_rows_kernel: the innermost axis is contiguous in the output and in every input that is not
-//    broadcast along it (inner stride 1, or 0 = one value per row).  Work units are row segments;
-//    a thread moves chunks of C elements, C = 16 bytes of the smallest operand capped at 64 bytes of
-//    the widest, so every access is a 16-byte vector (u8 -> f32 reads 16 B and writes 64 B per chunk)
-//    or, for a Bool next to 8-byte types, one 8-byte access.  U chunks are loaded before the first is
-//    converted, to keep several loads in flight.
+//    broadcast along it (inner stride 1, or 0 = one value per row).  Work units are row segments cut
+//    into slots of W elements, W * (widest element size) = 16 bytes; lanes take consecutive slots, so
+//    each access of each operand is contiguous across the warp (u8 -> f32: 4-byte loads and 16-byte
+//    stores, both covering 512 contiguous bytes per warp instruction).  U slots are loaded before the
+//    first is converted, about 128 bytes of loads in flight per thread.
 //  * map_generic_kernel: any strides; each thread decodes its element's position from the collapsed
 //    shape, innermost axis fastest (32-bit fast division when every index fits in 32 bits).
 #pragma once
@@ -24,49 +24,60 @@ namespace ew {
 
 constexpr int kBlock = 256;
 constexpr int kMaxIn = 3;
-constexpr uint32_t kSegChunks = 2048;  // chunks per work unit (long rows are cut into segments)
+constexpr uint32_t kSegSlots = 4096;  // slots per work unit (long rows are cut into segments)
 
-template <typename T, int C>
-struct alignas(16) Chunk {
-    T v[C];
+// A slot: W consecutive elements of one operand, moved with one access of W * sizeof(T) bytes
+// (2, 4, 8 or 16).  Lanes of a warp take consecutive slots, so every operand's access is contiguous
+// across the warp whatever its element size.
+template <typename T, int W>
+struct alignas(W * sizeof(T)) Slot {
+    T v[W];
 };
 
-// C elements starting at p: one 8-byte access when the chunk is 8 bytes, else C * sizeof(T) / 16
-// streaming 16-byte vector accesses (p 16-byte aligned).
-template <typename T, int C>
-__device__ __forceinline__ void load_chunk(Chunk<T, C>& out, const T* p) {
-    constexpr int kBytes = C * (int)sizeof(T);
-    static_assert(kBytes == 8 || kBytes % 16 == 0, "chunk must be 8 bytes or whole 16-byte vectors");
-    if constexpr (kBytes == 8) {
+template <typename T, int W>
+__device__ __forceinline__ void load_slot(Slot<T, W>& out, const T* p) {
+    constexpr int kBytes = W * (int)sizeof(T);
+    if constexpr (kBytes == 16) {
+        uint4 r;
+        asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+            : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+            : "l"(p));
+        memcpy(out.v, &r, 16);
+    } else if constexpr (kBytes == 8) {
         uint2 r;
         asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
         memcpy(out.v, &r, 8);
+    } else if constexpr (kBytes == 4) {
+        unsigned r;
+        asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+        memcpy(out.v, &r, 4);
     } else {
-#pragma unroll
-        for (int i = 0; i < kBytes / 16; ++i) {
-            uint4 r;
-            asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                : "l"(reinterpret_cast<const char*>(p) + 16 * i));
-            memcpy(reinterpret_cast<char*>(out.v) + 16 * i, &r, 16);
-        }
+        static_assert(kBytes == 2, "slot of 2, 4, 8 or 16 bytes");
+        unsigned short r;
+        asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
+        memcpy(out.v, &r, 2);
     }
 }
 
-template <typename T, int C>
-__device__ __forceinline__ void store_chunk(T* p, const Chunk<T, C>& in) {
-    constexpr int kBytes = C * (int)sizeof(T);
-    if constexpr (kBytes == 8) {
+template <typename T, int W>
+__device__ __forceinline__ void store_slot(T* p, const Slot<T, W>& in) {
+    constexpr int kBytes = W * (int)sizeof(T);
+    if constexpr (kBytes == 16) {
+        uint4 r;
+        memcpy(&r, in.v, 16);
+        __stcs(reinterpret_cast<uint4*>(p), r);
+    } else if constexpr (kBytes == 8) {
         uint2 r;
         memcpy(&r, in.v, 8);
         __stcs(reinterpret_cast<uint2*>(p), r);
+    } else if constexpr (kBytes == 4) {
+        unsigned r;
+        memcpy(&r, in.v, 4);
+        __stcs(reinterpret_cast<unsigned*>(p), r);
     } else {
-#pragma unroll
-        for (int i = 0; i < kBytes / 16; ++i) {
-            uint4 r;
-            memcpy(&r, reinterpret_cast<const char*>(in.v) + 16 * i, 16);
-            __stcs(reinterpret_cast<uint4*>(reinterpret_cast<char*>(p) + 16 * i), r);
-        }
+        unsigned short r;
+        memcpy(&r, in.v, 2);
+        __stcs(reinterpret_cast<unsigned short*>(p), r);
     }
 }
 
@@ -89,36 +100,31 @@ __device__ __forceinline__ T load_elem(const T* p) {
     return out;
 }
 
-// Chunk width and unroll depth of an op.
+// Slot width and unroll depth of an op: a slot is 16 bytes of the widest operand; U slots per thread
+// per iteration are loaded before the first is converted, about 128 bytes of loads in flight.
 template <class Op>
 struct Shape {
     using Out = typename Op::Out;
     static constexpr int kA = Op::kArity;
-    static constexpr int kMin0 = (int)std::min(sizeof(Out), sizeof(typename Op::In0));
-    static constexpr int kMin1 = kA > 1 ? (int)std::min<size_t>(kMin0, sizeof(typename Op::In1)) : kMin0;
-    static constexpr int kMin = kA > 2 ? (int)std::min<size_t>(kMin1, sizeof(typename Op::In2)) : kMin1;
     static constexpr int kMax0 = (int)std::max(sizeof(Out), sizeof(typename Op::In0));
     static constexpr int kMax1 = kA > 1 ? (int)std::max<size_t>(kMax0, sizeof(typename Op::In1)) : kMax0;
     static constexpr int kMax = kA > 2 ? (int)std::max<size_t>(kMax1, sizeof(typename Op::In2)) : kMax1;
-    // 16 bytes of the smallest operand, but at most 64 bytes of the widest (so 8-byte types next to
-    // Bool move 8 elements per chunk, and the Bool side one 8-byte access)
-    static constexpr int C = std::min(16 / kMin, 64 / kMax);
-    static constexpr int kInBytes = C * ((int)sizeof(typename Op::In0) + (kA > 1 ? (int)sizeof(typename Op::In1) : 0) +
+    static constexpr int W = 16 / kMax;
+    static constexpr int kInBytes = W * ((int)sizeof(typename Op::In0) + (kA > 1 ? (int)sizeof(typename Op::In1) : 0) +
                                          (kA > 2 ? (int)sizeof(typename Op::In2) : 0));
-    static constexpr int kAllBytes = kInBytes + C * (int)sizeof(Out);
-    static constexpr int kU0 = std::min(64 / kInBytes, 512 / kAllBytes);
-    static constexpr int U = kU0 < 1 ? 1 : (kU0 > 4 ? 4 : kU0);
+    static constexpr int kU0 = 128 / kInBytes;
+    static constexpr int U = kU0 < 1 ? 1 : (kU0 > 16 ? 16 : kU0);
 };
 
 struct RowArgs {
     void* dst;
     const void* src[kMaxIn];
-    uint32_t chunks;      // chunks per row
-    uint32_t seg_chunks;  // chunks per work unit
-    uint32_t segs;        // units per row
-    uint32_t units;       // rows * segs (< 2^31)
-    uint32_t tpr;         // threads per unit (power of two <= kBlock)
-    uint32_t bcast;       // bit k: input k has inner stride 0
+    uint32_t slots;      // slots per row
+    uint32_t seg_slots;  // slots per work unit
+    uint32_t segs;       // units per row
+    uint32_t units;      // rows * segs (< 2^31)
+    uint32_t tpr;        // threads per unit (power of two <= kBlock)
+    uint32_t bcast;      // bit k: input k has inner stride 0
     FastDiv seg_div;
     uint32_t n;  // outer axes
     FastDiv fdiv[MTXC_MAX_DIMS];
@@ -126,7 +132,7 @@ struct RowArgs {
     uint32_t ss[kMaxIn][MTXC_MAX_DIMS];
 };
 
-template <class Op, int C, int U>
+template <class Op, int W, int U>
 __global__ void __launch_bounds__(kBlock) map_rows_kernel(const RowArgs a) {
     using Out = typename Op::Out;
     using I0 = typename Op::In0;
@@ -163,41 +169,41 @@ __global__ void __launch_bounds__(kBlock) map_rows_kernel(const RowArgs a) {
         I2 s2{};
         if (A > 1 && b1) s1 = load_elem(p1);
         if (A > 2 && b2) s2 = load_elem(p2);
-        const uint32_t c_end = min(a.chunks, (seg + 1) * a.seg_chunks);
-        uint32_t c = seg * a.seg_chunks + lane;
+        const uint32_t c_end = min(a.slots, (seg + 1) * a.seg_slots);
+        uint32_t c = seg * a.seg_slots + lane;
         for (; c + (U - 1) * a.tpr < c_end; c += U * a.tpr) {
-            Chunk<I0, C> x0[U];
-            Chunk<I1, C> x1[U];
-            Chunk<I2, C> x2[U];
+            Slot<I0, W> x0[U];
+            Slot<I1, W> x1[U];
+            Slot<I2, W> x2[U];
 #pragma unroll
             for (int j = 0; j < U; ++j) {
-                const uint64_t e = (uint64_t)(c + j * a.tpr) * C;
-                if (!b0) load_chunk(x0[j], p0 + e);
-                if (A > 1 && !b1) load_chunk(x1[j], p1 + e);
-                if (A > 2 && !b2) load_chunk(x2[j], p2 + e);
+                const uint64_t e = (uint64_t)(c + j * a.tpr) * W;
+                if (!b0) load_slot(x0[j], p0 + e);
+                if (A > 1 && !b1) load_slot(x1[j], p1 + e);
+                if (A > 2 && !b2) load_slot(x2[j], p2 + e);
             }
 #pragma unroll
             for (int j = 0; j < U; ++j) {
-                Chunk<Out, C> y;
+                Slot<Out, W> y;
 #pragma unroll
-                for (int k = 0; k < C; ++k)
+                for (int k = 0; k < W; ++k)
                     y.v[k] = op(b0 ? s0 : x0[j].v[k], (A > 1 && !b1) ? x1[j].v[k] : s1, (A > 2 && !b2) ? x2[j].v[k] : s2);
-                store_chunk(pd + (uint64_t)(c + j * a.tpr) * C, y);
+                store_slot(pd + (uint64_t)(c + j * a.tpr) * W, y);
             }
         }
         for (; c < c_end; c += a.tpr) {
-            const uint64_t e = (uint64_t)c * C;
-            Chunk<I0, C> x0;
-            Chunk<I1, C> x1;
-            Chunk<I2, C> x2;
-            if (!b0) load_chunk(x0, p0 + e);
-            if (A > 1 && !b1) load_chunk(x1, p1 + e);
-            if (A > 2 && !b2) load_chunk(x2, p2 + e);
-            Chunk<Out, C> y;
+            const uint64_t e = (uint64_t)c * W;
+            Slot<I0, W> x0;
+            Slot<I1, W> x1;
+            Slot<I2, W> x2;
+            if (!b0) load_slot(x0, p0 + e);
+            if (A > 1 && !b1) load_slot(x1, p1 + e);
+            if (A > 2 && !b2) load_slot(x2, p2 + e);
+            Slot<Out, W> y;
 #pragma unroll
-            for (int k = 0; k < C; ++k)
+            for (int k = 0; k < W; ++k)
                 y.v[k] = op(b0 ? s0 : x0.v[k], (A > 1 && !b1) ? x1.v[k] : s1, (A > 2 && !b2) ? x2.v[k] : s2);
-            store_chunk(pd + e, y);
+            store_slot(pd + e, y);
         }
     }
 }
@@ -267,12 +273,12 @@ struct MapDesc {
     const uint32_t* ss[kMaxIn];
 };
 
-// Launches the row kernel when the innermost axis allows 16-byte chunks, else the generic kernel.
+// Launches the row kernel when the innermost axis allows whole slots, else the generic kernel.
 template <class Op>
 int launch_map(const MapDesc& m, int sm_count, cudaStream_t stream) {
     using S = Shape<Op>;
     constexpr int A = Op::kArity;
-    constexpr int C = S::C;
+    constexpr int W = S::W;
     const size_t in_size[kMaxIn] = {sizeof(typename Op::In0), sizeof(typename Op::In1), sizeof(typename Op::In2)};
     uint32_t one = 1, zero = 0;
     uint32_t cdims = m.cdims;
@@ -288,34 +294,34 @@ int launch_map(const MapDesc& m, int sm_count, cudaStream_t stream) {
     const uint64_t total = product(shape, cdims);
     if (total == 0) return MTXC_OK;
     const uint32_t k = cdims - 1;
-    bool rows_ok = sd[k] == 1 && shape[k] % C == 0 && aligned16(m.dst);
+    auto aligned = [](const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; };
+    bool rows_ok = sd[k] == 1 && shape[k] % W == 0 && aligned(m.dst, W * sizeof(typename Op::Out));
     uint32_t bcast = 0;
     for (int i = 0; i < A && rows_ok; ++i) {
         if (ss[i][k] == 0) bcast |= 1u << i;
-        else rows_ok = ss[i][k] == 1 && aligned16(m.src[i]);
+        else rows_ok = ss[i][k] == 1 && aligned(m.src[i], W * in_size[i]);
     }
-    const uint32_t chunks = shape[k] / C;
-    uint32_t seg_chunks = std::min<uint32_t>(std::max<uint32_t>(chunks, 1), kSegChunks);
-    const uint32_t segs = (chunks + seg_chunks - 1) / std::max<uint32_t>(seg_chunks, 1);
+    const uint32_t slots = shape[k] / W;
+    const uint32_t seg_slots = std::min<uint32_t>(std::max<uint32_t>(slots, 1), kSegSlots);
+    const uint32_t segs = (slots + seg_slots - 1) / seg_slots;
     const uint64_t rows = total / shape[k];
-    rows_ok = rows_ok && chunks > 0 && rows * segs < (1ull << 31);
+    rows_ok = rows_ok && slots > 0 && rows * segs < (1ull << 31);
     for (uint32_t j = 0; j < k && rows_ok; ++j) {
         if (shape[j] == 1) continue;
-        rows_ok = shape[j] < (1u << 31) && (uint64_t)sd[j] * sizeof(typename Op::Out) % 16 == 0;
-        for (int i = 0; i < A && rows_ok; ++i)
-            rows_ok = (bcast >> i & 1u) ? true : (uint64_t)ss[i][j] * in_size[i] % 16 == 0;
+        rows_ok = shape[j] < (1u << 31) && sd[j] % W == 0;
+        for (int i = 0; i < A && rows_ok; ++i) rows_ok = (bcast >> i & 1u) || ss[i][j] % W == 0;
     }
     if (rows_ok) {
         RowArgs a{};
         a.dst = m.dst;
         for (int i = 0; i < kMaxIn; ++i) a.src[i] = i < A ? m.src[i] : nullptr;
-        a.chunks = chunks;
-        a.seg_chunks = seg_chunks;
+        a.slots = slots;
+        a.seg_slots = seg_slots;
         a.segs = segs;
         a.seg_div = FastDiv(segs);
         a.units = (uint32_t)(rows * segs);
         uint32_t tpr = 1;
-        while (tpr < seg_chunks && tpr < (uint32_t)kBlock) tpr <<= 1;
+        while (tpr < seg_slots && tpr < (uint32_t)kBlock) tpr <<= 1;
         a.tpr = tpr;
         a.bcast = bcast;
         a.n = k;
@@ -326,7 +332,7 @@ int launch_map(const MapDesc& m, int sm_count, cudaStream_t stream) {
         }
         const uint32_t rpb = kBlock / tpr;
         const uint64_t blocks = std::min<uint64_t>((a.units + rpb - 1) / rpb, (uint64_t)sm_count * 4);
-        map_rows_kernel<Op, C, S::U><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        map_rows_kernel<Op, W, S::U><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         return check_launch("map_rows_kernel");
     }
     GenericArgs g{};

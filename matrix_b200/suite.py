@@ -53,12 +53,13 @@ def _line(name, workload, nbytes, ms, peak, **extra):
 
 
 def run_all(dev, stream, configs=None, scale=1):
-    """configs: names to run (default all: C1 C3 C4 C5a C5b); scale: divide each config's leading
-    extent by this (small cases for profiling)."""
+    """configs: names to run (default all: C1 C3 C4 C5a C5b, and F2 F3 F4 for the statistics, astype
+    and pointwise kernels); scale: divide each config's leading extent by this (small cases for
+    profiling)."""
     peak = _peak()
     g = torch.Generator(device=dev)
     out = []
-    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b"}
+    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4"}
 
     # C1: Sum over the last axis of f32 [1024, 4096] ~ N(0,1)
     if "C1" in want:
@@ -71,6 +72,12 @@ def run_all(dev, stream, configs=None, scale=1):
         _c5a(out, dev, stream, g, peak, scale)
     if "C5b" in want:
         _c5b(out, dev, stream, g, peak, scale)
+    if "F2" in want:
+        _f2(out, dev, stream, g, peak, scale)
+    if "F3" in want:
+        _f3(out, dev, stream, g, peak, scale)
+    if "F4" in want:
+        _f4(out, dev, stream, g, peak, scale)
     torch.cuda.empty_cache()
     return out
 
@@ -178,3 +185,59 @@ def _c5b(out, dev, stream, g, peak, scale):
     ms = _time(c5b, stream, reps=5)
     out.append(_line("C5b", "full Sum f32 2^32 as [8,2^29] (1 GPU)", 8 * cols * 4, ms, peak))
     del x
+
+
+def _f2(out, dev, stream, g, peak, scale):
+    """rms over the last axis of f32 [8192, 32768]: fused (one read) and as the reference's trace."""
+    rows = max(8192 // scale, 1)
+    g.manual_seed(6)
+    x = torch.randn(rows, 32768, generator=g, device=dev)
+    n = x.numel() * 4
+    ms = _time(lambda: backend.stat("rms", x, 1), stream)
+    out.append(_line("F2-rms", "rms(axis=-1) f32 [8192,32768] fused (mtxc_reduce_stat)", n + rows * 4, ms, peak))
+    ms = _time(lambda: backend.stat("mean", x, 1), stream)
+    out.append(_line("F2-mean", "mean(axis=-1) f32 [8192,32768] fused (mtxc_reduce_stat)", n + rows * 4, ms, peak))
+
+    def trace():
+        sq = backend.binary("mul", x, x)
+        s = backend.reduce("sum", sq, 1)
+        nd = torch.full((), 32768.0, device=dev)
+        m = backend.binary("div", s, nd)
+        return backend.unary("sqrt", m)
+
+    ms = _time(trace, stream)
+    out.append(_line("F2-rms-trace", "rms as the reference's trace: mul, sum, div, sqrt (4 kernels)", n + rows * 4, ms,
+                     peak, moved_bytes=3 * n))
+    del x
+
+
+def _f3(out, dev, stream, g, peak, scale):
+    """astype: f32 -> bf16 and u8 -> f32 over [8192, 32768]."""
+    rows = max(8192 // scale, 1)
+    g.manual_seed(7)
+    x = torch.randn(rows, 32768, generator=g, device=dev)
+    ms = _time(lambda: backend.astype(x, torch.bfloat16), stream)
+    out.append(_line("F3-astype-f32-bf16", "astype f32 -> bf16 [8192,32768]", x.numel() * 6, ms, peak))
+    u = torch.randint(0, 256, (rows, 32768), generator=g, device=dev, dtype=torch.int32).to(torch.uint8)
+    del x
+    ms = _time(lambda: backend.astype(u, torch.float32), stream)
+    out.append(_line("F3-astype-u8-f32", "astype u8 -> f32 [8192,32768]", u.numel() * 5, ms, peak))
+    del u
+
+
+def _f4(out, dev, stream, g, peak, scale):
+    """The pointwise family and equal over [8192, 32768] f32 with a broadcast row operand."""
+    rows = max(8192 // scale, 1)
+    g.manual_seed(8)
+    a = torch.randn(rows, 32768, generator=g, device=dev)
+    b = torch.randn(32768, generator=g, device=dev)
+    c = torch.rand(rows, 32768, generator=g, device=dev) < 0.5
+    n = a.numel()
+    ms = _time(lambda: backend.pointwise("where", [c, a, b]), stream)
+    out.append(_line("F4-where", "where(cond bool [8192,32768], a f32 [8192,32768], b f32 [32768])",
+                     n * (1 + 4 + 4) + 32768 * 4, ms, peak))
+    ms = _time(lambda: backend.pointwise("greater", [a, b]), stream)
+    out.append(_line("F4-greater", "greater(a f32 [8192,32768], b f32 [32768]) -> bool", n * 5 + 32768 * 4, ms, peak))
+    ms = _time(lambda: backend.binary("equal", a, b), stream)
+    out.append(_line("F4-equal", "equal(a f32 [8192,32768], b f32 [32768]) -> f32", n * 8 + 32768 * 4, ms, peak))
+    del a, b, c
