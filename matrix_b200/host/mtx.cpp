@@ -53,10 +53,22 @@ int normalize_axis(int axis, uint32_t dims) {
     return axis;
 }
 
+// Elements a layout spans (the reference's effectiveBufferSize): the last element's offset + 1.
+uint64_t span(const std::vector<size_m>& shape, const std::vector<size_m>& strides) {
+    uint64_t last = 0;
+    for (size_t i = 0; i < shape.size(); ++i) {
+        if (shape[i] == 0) return 0;
+        last += (uint64_t)(shape[i] - 1) * strides[i];
+    }
+    return last + 1;
+}
+
 // Allocate-or-adopt the output and fill the tape's cache (primitives.cpp:2866-2882), before the
 // single COMPILE_TRACE return.
 void allocate_output(Primitive& p, matrix& out) {
-    if (!p.out_buffer) p.out_buffer = std::make_shared<Buffer>(out.total_size() * dtype_size(out.type()));
+    if (!p.out_buffer)
+        p.out_buffer = std::make_shared<Buffer>(std::max<uint64_t>(span(out.shape(), out.strides()), 1) *
+                                                dtype_size(out.type()));
     out.ensure_buffer(p.out_buffer);
 }
 
@@ -153,7 +165,7 @@ public:
     }
     std::vector<matrix*> inputs() override { return {&a_, &b_}; }
     const char* name() const override {
-        static const char* n[] = {"Addition", "Subtraction", "Multiplication", "Division", "Max", "Min"};
+        static const char* n[] = {"Addition", "Subtraction", "Multiplication", "Division", "Max", "Min", "Equal"};
         return n[op_];
     }
     int op() const { return op_; }
@@ -167,10 +179,10 @@ private:
     uint32_t shape_[MTXC_MAX_DIMS] = {}, sr_[MTXC_MAX_DIMS] = {}, sa_[MTXC_MAX_DIMS] = {}, sb_[MTXC_MAX_DIMS] = {};
 };
 
-// exp (primitives.cpp:5332-5463)
-class ExpPrimitive : public Primitive {
+// exp / sqrt (ExpPrimitive primitives.cpp:5332-5463, SqrtPrimitive)
+class UnaryPrimitive : public Primitive {
 public:
-    explicit ExpPrimitive(const matrix& in) : input_(in) {
+    UnaryPrimitive(int op, const matrix& in) : op_(op), input_(in) {
         std::vector<size_m> out_strides = row_major(in.shape());
         cdims_ = mtxc_collapse_dims2(in.shape().data(), out_strides.data(), in.strides().data(), in.dims(), 0x7FFFFFFFu,
                                      shape_, s_out_, s_in_);
@@ -181,20 +193,142 @@ public:
         if (t == EvalType::COMPILE_TRACE) return;
         if (evaluated) return;
         evaluated = true;
-        check(mtxc_unary(MTXC_UNARY_EXP, (int)input_.type(), out.data(), input_.data(), cdims_, shape_, s_out_, s_in_),
-              "mtxc_unary");
+        check(mtxc_unary(op_, (int)input_.type(), out.data(), input_.data(), cdims_, shape_, s_out_, s_in_), "mtxc_unary");
     }
     void clear_trace_checks() override {
         evaluated = false;
         if (input_.has_tape()) input_.tape_ptr()->clear_trace_checks();
     }
     std::vector<matrix*> inputs() override { return {&input_}; }
-    const char* name() const override { return "Exp"; }
+    const char* name() const override { return op_ == MTXC_UNARY_EXP ? "Exp" : "Sqrt"; }
+    int op() const { return op_; }
     const matrix& input() const { return input_; }
+
+private:
+    int op_;
+    matrix input_;
+    uint32_t cdims_ = 0;
+    uint32_t shape_[MTXC_MAX_DIMS] = {}, s_out_[MTXC_MAX_DIMS] = {}, s_in_[MTXC_MAX_DIMS] = {};
+};
+
+// astype (AsTypePrimitive, primitives.cpp:3510-3591): collapse_dims(in.shape, out.strides, in.strides)
+class AsTypePrimitive : public Primitive {
+public:
+    AsTypePrimitive(const matrix& in, const std::vector<size_m>& out_strides) : input_(in) {
+        cdims_ = mtxc_collapse_dims2(in.shape().data(), out_strides.data(), in.strides().data(), in.dims(), 0x7FFFFFFFu,
+                                     shape_, s_out_, s_in_);
+    }
+    void eval(matrix& out, EvalType t) override {
+        eval_input(input_, t);
+        allocate_output(*this, out);
+        if (t == EvalType::COMPILE_TRACE) return;
+        if (evaluated) return;
+        evaluated = true;
+        check(mtxc_astype((int)out.type(), (int)input_.type(), out.data(), input_.data(), cdims_, shape_, s_out_, s_in_),
+              "mtxc_astype");
+    }
+    void clear_trace_checks() override {
+        evaluated = false;
+        if (input_.has_tape()) input_.tape_ptr()->clear_trace_checks();
+    }
+    std::vector<matrix*> inputs() override { return {&input_}; }
+    const char* name() const override { return "AsType"; }
 
 private:
     matrix input_;
     uint32_t cdims_ = 0;
+    uint32_t shape_[MTXC_MAX_DIMS] = {}, s_out_[MTXC_MAX_DIMS] = {}, s_in_[MTXC_MAX_DIMS] = {};
+};
+
+// greater / less / logical_and / where / floor / full over make_pointwise's collapse
+// (Matrix.mm:13511-13556); the output is contiguous.
+class PointwisePrimitive : public Primitive {
+public:
+    PointwisePrimitive(int op, std::vector<matrix> ins, const std::vector<size_m>& out_shape)
+        : op_(op), inputs_(std::move(ins)) {
+        const uint32_t rank = (uint32_t)out_shape.size();
+        std::vector<size_m> rows(inputs_.size() * std::max<uint32_t>(rank, 1), 0);
+        for (size_t i = 0; i < inputs_.size(); ++i) {
+            const matrix& in = inputs_[i];
+            for (uint32_t d = 0; d < in.dims(); ++d)
+                rows[i * rank + rank - in.dims() + d] = in.shape()[d] == 1 ? 0 : in.strides()[d];
+        }
+        cdims_ = mtxc_pointwise_collapse(out_shape.data(), rank, rows.data(), (uint32_t)inputs_.size(), shape_, strides_);
+        if (cdims_ == 0xFFFFFFFFu) throw std::invalid_argument("pointwise output exceeds the rank or 32-bit size limit");
+    }
+    void eval(matrix& out, EvalType t) override {
+        for (matrix& in : inputs_) eval_input(in, t);
+        allocate_output(*this, out);
+        if (t == EvalType::COMPILE_TRACE) return;
+        if (evaluated) return;
+        evaluated = true;
+        if (out.total_size() == 0) return;  // the backends return before reading anything
+        const void* ptrs[3] = {};
+        for (size_t i = 0; i < inputs_.size(); ++i) ptrs[i] = inputs_[i].data();
+        const int dt = (int)inputs_[op_ == MTXC_PW_WHERE ? 1 : 0].type();
+        check(mtxc_pointwise(op_, dt, out.data(), ptrs, (uint32_t)inputs_.size(), cdims_, shape_, strides_),
+              "mtxc_pointwise");
+    }
+    void clear_trace_checks() override {
+        evaluated = false;
+        for (matrix& in : inputs_)
+            if (in.has_tape()) in.tape_ptr()->clear_trace_checks();
+    }
+    std::vector<matrix*> inputs() override {
+        std::vector<matrix*> v;
+        for (matrix& in : inputs_) v.push_back(&in);
+        return v;
+    }
+    const char* name() const override {
+        static const char* n[] = {"Greater", "Less", "LogicalAnd", "Where", "Floor", "Full"};
+        return n[op_];
+    }
+
+private:
+    int op_;
+    std::vector<matrix> inputs_;
+    uint32_t cdims_ = 0;
+    uint32_t shape_[MTXC_MAX_DIMS] = {}, strides_[3 * MTXC_MAX_DIMS] = {};
+};
+
+// mean / rms / norm as one node (mtxc_reduce_stat); metadata as ReducePrimitive's
+class StatPrimitive : public Primitive {
+public:
+    StatPrimitive(int stat, const matrix& in, int axis, bool keepdims, const std::vector<size_m>& out_shape)
+        : stat_(stat), input_(in) {
+        const uint32_t dims = in.dims();
+        std::vector<size_m> out_strides = row_major(out_shape);
+        out_strides.resize(dims, 0);
+        cdims_ = mtxc_collapse_dims_reduce2(in.shape().data(), out_strides.data(), in.strides().data(), dims, axis, 0,
+                                            keepdims ? 0 : 1, 0xFFFFFFFFu, shape_, s_out_, s_in_);
+        rstride_ = in.strides()[axis];
+        rlen_ = in.shape()[axis];
+    }
+    void eval(matrix& out, EvalType t) override {
+        eval_input(input_, t);
+        allocate_output(*this, out);
+        if (t == EvalType::COMPILE_TRACE) return;
+        if (evaluated) return;
+        evaluated = true;
+        check(mtxc_reduce_stat(stat_, (int)input_.type(), out.data(), input_.data(), rstride_, rlen_, cdims_, shape_,
+                               s_out_, s_in_),
+              "mtxc_reduce_stat");
+    }
+    void clear_trace_checks() override {
+        evaluated = false;
+        if (input_.has_tape()) input_.tape_ptr()->clear_trace_checks();
+    }
+    std::vector<matrix*> inputs() override { return {&input_}; }
+    const char* name() const override {
+        static const char* n[] = {"Mean", "Rms", "Norm"};
+        return n[stat_];
+    }
+    uint32_t rlen() const { return rlen_; }
+
+private:
+    int stat_;
+    matrix input_;
+    uint32_t cdims_ = 0, rstride_ = 0, rlen_ = 0;
     uint32_t shape_[MTXC_MAX_DIMS] = {}, s_out_[MTXC_MAX_DIMS] = {}, s_in_[MTXC_MAX_DIMS] = {};
 };
 
@@ -230,8 +364,8 @@ std::shared_ptr<Primitive> match_softmax(const matrix& y) {
     if (!div || div->op() != MTXC_BINARY_DIV) return nullptr;
     auto* s = dynamic_cast<const ReducePrimitive*>(div->b().tape());
     if (!s || s->op() != MTXC_REDUCE_SUM || !s->keepdims() || s->input().tape() != div->a().tape()) return nullptr;
-    auto* e = dynamic_cast<const ExpPrimitive*>(div->a().tape());
-    if (!e) return nullptr;
+    auto* e = dynamic_cast<const UnaryPrimitive*>(div->a().tape());
+    if (!e || e->op() != MTXC_UNARY_EXP) return nullptr;
     auto* t = dynamic_cast<const BinaryPrimitive*>(e->input().tape());
     if (!t || t->op() != MTXC_BINARY_SUB) return nullptr;
     auto* m = dynamic_cast<const ReducePrimitive*>(t->b().tape());
@@ -273,16 +407,69 @@ matrix make_reduce(int op, const matrix& x, int axis, bool keepdims) {
 }
 
 matrix make_binary(int op, const matrix& a, const matrix& b) {
-    // promotion inserts astype before + - * / (Matrix.mm:8313-8315); max / min(a, b) use a's dtype
-    if (a.type() != b.type())
-        throw std::runtime_error("mixed dtypes need astype, which this backend does not provide");
+    // + - * / and equal promote both operands with astype first (Matrix.mm:8313-8315, 14452-14454).
+    // max / min(a, b) promote only the result dtype and read b's memory as a's type (Matrix.mm:13364-13366,
+    // 13459), which is meaningful only for equal dtypes; mixed dtypes are refused there.
+    const bool promotes = op != MTXC_BINARY_MAX && op != MTXC_BINARY_MIN;
+    if (!promotes && a.type() != b.type())
+        throw std::runtime_error("max / min(a, b) of mixed dtypes: cast one operand with astype first");
+    const dtype common = promote_types(a.type(), b.type());
+    const matrix lhs = a.type() == common ? a : a.astype(common);
+    const matrix rhs = b.type() == common ? b : b.astype(common);
     std::vector<size_m> out_shape;
-    auto prim = std::make_shared<BinaryPrimitive>(op, a, b, out_shape);
+    auto prim = std::make_shared<BinaryPrimitive>(op, lhs, rhs, out_shape);
     matrix out;
-    out.set_layout(out_shape, row_major(out_shape), a.type());
+    out.set_layout(out_shape, row_major(out_shape), common);
     out.set_tape(prim);
     return out;
 }
+
+// pointwise_cast / pointwise_shape / make_pointwise (Matrix.mm:13487-13556)
+matrix pointwise_cast(const matrix& x, dtype t) { return x.type() == t ? x : x.astype(t); }
+
+std::vector<size_m> pointwise_shape(const std::vector<matrix>& ins) {
+    uint32_t rank = 0;
+    for (const matrix& in : ins) rank = std::max(rank, in.dims());
+    if (rank > MTXC_MAX_DIMS) throw std::invalid_argument("pointwise rank exceeds MAX_TENSOR_DIMS");
+    std::vector<size_m> shape(rank, 1);
+    for (const matrix& in : ins)
+        for (uint32_t d = 0; d < in.dims(); ++d) {
+            size_m& n = shape[rank - in.dims() + d];
+            const size_m m = in.shape()[d];
+            if (n == 1) n = m;
+            else if (m != 1 && n != m) throw std::invalid_argument("incompatible pointwise broadcast shapes");
+        }
+    return shape;
+}
+
+matrix make_pointwise(int op, const std::vector<matrix>& ins, const std::vector<size_m>& shape, dtype t) {
+    for (const matrix& in : ins) {
+        if (in.dims() > shape.size()) throw std::invalid_argument("input rank exceeds pointwise output rank");
+        for (uint32_t d = 0; d < in.dims(); ++d)
+            if (in.shape()[d] != 1 && in.shape()[d] != shape[shape.size() - in.dims() + d])
+                throw std::invalid_argument("input cannot broadcast to pointwise output shape");
+    }
+    auto prim = std::make_shared<PointwisePrimitive>(op, ins, shape);
+    matrix out;
+    out.set_layout(shape, row_major(shape), t);
+    out.set_tape(prim);
+    return out;
+}
+
+matrix make_stat(int stat, const matrix& x, int axis, bool keepdims) {
+    if (x.dims() == 0) throw std::invalid_argument("reduction of a 0-d matrix");
+    axis = normalize_axis(axis, x.dims());
+    std::vector<size_m> out_shape = x.shape();
+    if (keepdims) out_shape[axis] = 1;
+    else out_shape.erase(out_shape.begin() + axis);
+    const int oc = mtxc_reduce_stat_dtype(stat, (int)x.type(), x.shape()[axis]);
+    if (oc < 0) throw std::runtime_error("mean / rms / norm: unsupported dtype");
+    matrix out;
+    out.set_layout(out_shape, row_major(out_shape), (dtype)oc);
+    out.set_tape(std::make_shared<StatPrimitive>(stat, x, axis, keepdims, out_shape));
+    return out;
+}
+
 
 }  // namespace
 
@@ -350,15 +537,7 @@ matrix matrix::min(int axis, bool keepdims) const { return make_reduce(MTXC_REDU
 matrix matrix::argmax(int axis, bool keepdims) const { return make_reduce(MTXC_REDUCE_ARGMAX, *this, axis, keepdims); }
 matrix matrix::argmin(int axis, bool keepdims) const { return make_reduce(MTXC_REDUCE_ARGMIN, *this, axis, keepdims); }
 
-matrix matrix::sum() const {
-    // flatten(0, -1) then sum(0): a contiguous (or lazy, hence contiguous) matrix viewed as 1-D
-    if (!contiguous(shape_, strides_)) throw std::runtime_error("sum(): flatten needs a contiguous matrix");
-    const uint64_t n = total_size();
-    if (n > 0xFFFFFFFFull) throw std::invalid_argument("sum(): more elements than size_m can count");
-    matrix flat = *this;
-    flat.set_layout({(size_m)n}, {1}, type_, offset_);
-    return flat.sum(0);
-}
+matrix matrix::sum() const { return flat("sum()").sum(0); }
 
 matrix operator+(const matrix& a, const matrix& b) { return make_binary(MTXC_BINARY_ADD, a, b); }
 matrix operator-(const matrix& a, const matrix& b) { return make_binary(MTXC_BINARY_SUB, a, b); }
@@ -367,13 +546,86 @@ matrix operator/(const matrix& a, const matrix& b) { return make_binary(MTXC_BIN
 matrix matrix::max(const matrix& a, const matrix& b) { return make_binary(MTXC_BINARY_MAX, a, b); }
 matrix matrix::min(const matrix& a, const matrix& b) { return make_binary(MTXC_BINARY_MIN, a, b); }
 
-matrix matrix::exp(const matrix& x) {
-    if (x.type() != dtype::Float) throw std::runtime_error("exp: float only in this backend");
+namespace {
+// exp / sqrt promote their input to promote_types(type, Float16) (Matrix.mm:6798-6811, 6934-6947)
+matrix make_unary(int op, const matrix& x) {
+    const dtype t = promote_types(x.type(), dtype::Float16);
+    if (t != dtype::Float && t != dtype::Float16) throw std::runtime_error("exp / sqrt: unsupported dtype");
+    const matrix in = x.type() == t ? x : x.astype(t, true);
     matrix out;
-    out.set_layout(x.shape(), row_major(x.shape()), x.type());
-    out.set_tape(std::make_shared<ExpPrimitive>(x));
+    out.set_layout(in.shape(), row_major(in.shape()), t);
+    out.set_tape(std::make_shared<UnaryPrimitive>(op, in));
     return out;
 }
+}  // namespace
+
+matrix matrix::exp(const matrix& x) { return make_unary(MTXC_UNARY_EXP, x); }
+matrix matrix::sqrt(const matrix& x) { return make_unary(MTXC_UNARY_SQRT, x); }
+matrix matrix::equal(const matrix& a, const matrix& b) { return make_binary(MTXC_BINARY_EQUAL, a, b); }
+
+matrix matrix::astype(dtype t, bool make_contig) const {
+    std::vector<size_m> out_strides = make_contig ? row_major(shape_) : strides_;
+    matrix out;
+    out.set_layout(shape_, out_strides, t);
+    out.set_tape(std::make_shared<AsTypePrimitive>(*this, out_strides));
+    return out;
+}
+
+matrix matrix::scalar(float value, dtype t) {
+    // matrix::scalar(value, t) holds dtype_cast<t>(value): converted once, on the device
+    matrix f = from_host(&value, {}, dtype::Float);
+    if (t == dtype::Float) return f;
+    matrix m = f.astype(t, true);
+    m.eval();
+    m.ensure_buffer(m.tape_->out_buffer);
+    m.tape_.reset();
+    return m;
+}
+
+matrix matrix::greater(const matrix& a, const matrix& b) {
+    const dtype t = promote_types(a.type(), b.type());
+    std::vector<matrix> ins{pointwise_cast(a, t), pointwise_cast(b, t)};
+    return make_pointwise(MTXC_PW_GREATER, ins, pointwise_shape(ins), dtype::Bool);
+}
+matrix matrix::less(const matrix& a, const matrix& b) {
+    const dtype t = promote_types(a.type(), b.type());
+    std::vector<matrix> ins{pointwise_cast(a, t), pointwise_cast(b, t)};
+    return make_pointwise(MTXC_PW_LESS, ins, pointwise_shape(ins), dtype::Bool);
+}
+matrix matrix::logical_and(const matrix& a, const matrix& b) {
+    std::vector<matrix> ins{pointwise_cast(a, dtype::Bool), pointwise_cast(b, dtype::Bool)};
+    return make_pointwise(MTXC_PW_LOGICAL_AND, ins, pointwise_shape(ins), dtype::Bool);
+}
+matrix matrix::where(const matrix& cond, const matrix& a, const matrix& b) {
+    const dtype t = promote_types(a.type(), b.type());
+    std::vector<matrix> ins{pointwise_cast(cond, dtype::Bool), pointwise_cast(a, t), pointwise_cast(b, t)};
+    return make_pointwise(MTXC_PW_WHERE, ins, pointwise_shape(ins), t);
+}
+matrix matrix::floor(const matrix& x) { return make_pointwise(MTXC_PW_FLOOR, {x}, x.shape(), x.type()); }
+matrix matrix::full(const std::vector<size_m>& shape, const matrix& value, dtype t) {
+    uint64_t count = 1;
+    for (size_m n : shape) {
+        if (n && count > 0xFFFFFFFFull / n) throw std::overflow_error("pointwise tensor exceeds 32-bit indexing");
+        count *= n;
+    }
+    return make_pointwise(MTXC_PW_FULL, {pointwise_cast(value, t)}, shape, t);
+}
+
+matrix matrix::mean(int axis, bool keepdims) const { return make_stat(MTXC_STAT_MEAN, *this, axis, keepdims); }
+matrix matrix::rms(int axis, bool keepdims) const { return make_stat(MTXC_STAT_RMS, *this, axis, keepdims); }
+matrix matrix::norm(int axis, bool keepdims) const { return make_stat(MTXC_STAT_NORM, *this, axis, keepdims); }
+matrix matrix::flat(const char* what) const {
+    // flatten(0, -1): a contiguous (or lazy, hence contiguous) matrix viewed as 1-D
+    if (!contiguous(shape_, strides_)) throw std::runtime_error(std::string(what) + ": flatten needs a contiguous matrix");
+    const uint64_t n = total_size();
+    if (n > 0xFFFFFFFFull) throw std::invalid_argument(std::string(what) + ": more elements than size_m can count");
+    matrix f = *this;
+    f.set_layout({(size_m)n}, {1}, type_, offset_);
+    return f;
+}
+matrix matrix::mean() const { return flat("mean()").mean(0); }
+matrix matrix::rms() const { return flat("rms()").rms(0); }
+matrix matrix::norm() const { return flat("norm()").norm(0); }
 
 namespace {
 matrix evaluated_view_source(const matrix& m) {

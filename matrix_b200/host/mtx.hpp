@@ -4,14 +4,22 @@
 // The reference is a lazy graph library: an op builds a Primitive node and caches the shape metadata
 // its backend needs (matrix.h:496-1787, primitives.cpp:57-118); eval() / compile() / execute() walk
 // the graph.  This header keeps those names and their meaning for the ops on the hot path:
-//   frontends   operator+ - * /, matrix::max / min(a, b)   (Matrix.mm:8312-8382, 13363-13376, 14668-14682)
+//   frontends   operator+ - * / with promotion (astype in front), matrix::max / min(a, b), matrix::equal
+//               (Matrix.mm:8312-8382, 13363-13376, 14668-14682, 14451-14466)
 //               x.sum / max / min / argmax / argmin(axis, keepdims), x.sum()   (Matrix.mm:14784-16335, 15210-15218)
-//               matrix::exp(x)                               (Matrix.mm:6934-6947)
+//               x.mean / rms / norm(axis, keepdims) and over all elements    (Matrix.mm:15220-15276)
+//               matrix::exp / sqrt(x) with promotion to Float16 or wider      (Matrix.mm:6798-6811, 6934-6947)
+//               x.astype(t, make_contig)                                       (Matrix.mm:8384-8398)
+//               matrix::greater / less / logical_and / where / floor / full    (Matrix.mm:13572-13593)
+//               matrix::scalar(v, t)                                           (a 0-d matrix holding dtype_cast<t>(v))
 //   primitives  allocate-or-adopt the output, return before computing under COMPILE_TRACE, run once
 //               per pass (`evaluated`), then call the backend (primitives.cpp:2836-2902)
 //   evaluation  eval() = compile + execute in one pass; compile() allocates every output and fuses
 //               the softmax trace; execute() runs kernels only -- the first execute is recorded into a
 //               CUDA graph, later ones replay it (Matrix.mm:8415-8475)
+// mean / rms / norm build one fused node (mtxc_reduce_stat: one read of x) whose result and dtype are
+// those of the reference's composition (sum, scalar division, sqrt); the other frontends build the
+// reference's own nodes.
 // Errors keep the reference's exception types: std::invalid_argument for shapes and axes
 // (Matrix.mm:220), std::runtime_error for everything else (Mods/GPUManager.h:62-71).
 //
@@ -83,6 +91,16 @@ public:
     matrix argmax(int axis, bool keepdims = false) const;
     matrix argmin(int axis, bool keepdims = false) const;
     matrix sum() const;  // all elements (flatten then sum(0), Matrix.mm:15215-15218)
+    matrix mean(int axis, bool keepdims = false) const;
+    matrix rms(int axis, bool keepdims = false) const;
+    matrix norm(int axis, bool keepdims = false) const;
+    matrix mean() const;  // all elements (a contiguous matrix viewed as 1-D)
+    matrix rms() const;
+    matrix norm() const;
+    // element type conversion; without make_contig the output keeps this matrix's strides, as the
+    // promotion in front of binary ops does
+    matrix astype(dtype t, bool make_contig = false) const;
+    static matrix scalar(float value, dtype t);
     friend matrix operator+(const matrix& a, const matrix& b);
     friend matrix operator-(const matrix& a, const matrix& b);
     friend matrix operator*(const matrix& a, const matrix& b);
@@ -90,6 +108,14 @@ public:
     static matrix max(const matrix& a, const matrix& b);
     static matrix min(const matrix& a, const matrix& b);
     static matrix exp(const matrix& x);
+    static matrix sqrt(const matrix& x);
+    static matrix equal(const matrix& a, const matrix& b);
+    static matrix greater(const matrix& a, const matrix& b);
+    static matrix less(const matrix& a, const matrix& b);
+    static matrix logical_and(const matrix& a, const matrix& b);
+    static matrix where(const matrix& cond, const matrix& a, const matrix& b);
+    static matrix floor(const matrix& x);
+    static matrix full(const std::vector<size_m>& shape, const matrix& value, dtype t);
 
     // views of an evaluated matrix (no copy: new strides / offset over the same buffer)
     matrix transpose(int a, int b) const;
@@ -132,6 +158,7 @@ public:
     void set_layout(std::vector<size_m> shape, std::vector<size_m> strides, dtype t, uint64_t offset = 0);
 
 private:
+    matrix flat(const char* what) const;  // flatten(0, -1) of a contiguous matrix
     std::shared_ptr<Buffer> buffer_;
     uint64_t offset_ = 0;  // elements
     std::vector<size_m> shape_, strides_;

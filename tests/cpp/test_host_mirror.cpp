@@ -276,12 +276,134 @@ static void test_trace(std::mt19937& rng) {
     EXPECT(ok, "compiled reduction graph");
 }
 
+// operator+ with mixed dtypes inserts astype (promote_types), the pointwise family, equal, sqrt's
+// promotion, and mean / rms / norm with the dtypes of the reference's composition
+static void test_promotion_and_pointwise(std::mt19937& rng) {
+    const std::vector<size_m> ash = {4, 1, 129}, bsh = {1, 37, 129};
+    std::vector<int32_t> ai(total(ash));
+    for (auto& v : ai) v = (int32_t)(rng() % 2001) - 1000;
+    std::vector<float> bf = random_ties(total(bsh), rng);
+    matrix A = matrix::from_host(ai.data(), ash, dtype::Int32);
+    matrix B = matrix::from_host(bf.data(), bsh, dtype::Float);
+    matrix S = A + B;  // Int32 + Float -> Float: astype(Float) of A first
+    S.eval();
+    EXPECT(S.type() == dtype::Float, "Int32 + Float is Float");
+    std::vector<float> got = S.to_host<float>();
+    bool ok = got.size() == 4u * 37 * 129;
+    for (size_t i = 0; ok && i < 4; ++i)
+        for (size_t j = 0; ok && j < 37; ++j)
+            for (size_t k = 0; ok && k < 129; ++k) {
+                volatile float x = (float)ai[i * 129 + k];
+                volatile float r = x + bf[j * 129 + k];
+                ok = got[(i * 37 + j) * 129 + k] == r;
+            }
+    EXPECT(ok, "promoted addition");
+
+    // UInt8 * Int8 -> Int16 (both cast), wrapping in Int16
+    std::vector<uint8_t> u8(64);
+    std::vector<int8_t> i8(64);
+    for (int i = 0; i < 64; ++i) {
+        u8[i] = (uint8_t)(rng() & 0xFF);
+        i8[i] = (int8_t)(rng() & 0xFF);
+    }
+    matrix P = matrix::from_host(u8.data(), {64}, dtype::UInt8) * matrix::from_host(i8.data(), {64}, dtype::Int8);
+    P.eval();
+    EXPECT(P.type() == dtype::Int16, "UInt8 * Int8 is Int16");
+    std::vector<int16_t> p16 = P.to_host<int16_t>();
+    ok = p16.size() == 64;
+    for (int i = 0; ok && i < 64; ++i) ok = p16[i] == (int16_t)((int)u8[i] * (int)i8[i]);
+    EXPECT(ok, "Int16 product");
+
+    // equal, greater, less, where, floor, full, logical_and
+    std::vector<float> x = random_ties(8 * 129, rng), y = random_ties(129, rng);
+    for (int k = 0; k < 40; ++k) x[k] = y[k];  // some equal pairs in the first row
+    matrix X = matrix::from_host(x.data(), {8, 129}, dtype::Float), Y = matrix::from_host(y.data(), {129}, dtype::Float);
+    matrix E = matrix::equal(X, Y), G = matrix::greater(X, Y), L = matrix::less(X, Y), F = matrix::floor(X * Y);
+    matrix W = matrix::where(G, X, Y);
+    matrix Fu = matrix::full({3, 129}, Y, dtype::Int32);
+    matrix LA = matrix::logical_and(G, matrix::less(Y, matrix::scalar(0.5f, dtype::Float)));
+    for (matrix* m : {&E, &G, &L, &F, &W, &Fu, &LA}) m->eval();
+    EXPECT(E.type() == dtype::Float && G.type() == dtype::Bool && W.type() == dtype::Float && Fu.type() == dtype::Int32,
+           "pointwise dtypes");
+    std::vector<float> e = E.to_host<float>(), f = F.to_host<float>(), w = W.to_host<float>();
+    std::vector<uint8_t> g = G.to_host<uint8_t>(), l = L.to_host<uint8_t>(), la = LA.to_host<uint8_t>();
+    std::vector<int32_t> fu = Fu.to_host<int32_t>();
+    ok = true;
+    for (size_t r = 0; r < 8 && ok; ++r)
+        for (size_t c = 0; c < 129 && ok; ++c) {
+            const float a = x[r * 129 + c], b = y[c];
+            volatile float prod = a * b;
+            ok = e[r * 129 + c] == (a == b ? 1.f : 0.f) && g[r * 129 + c] == (a > b) && l[r * 129 + c] == (a < b) &&
+                 w[r * 129 + c] == (a > b ? a : b) && f[r * 129 + c] == std::floor((float)prod) &&
+                 la[r * 129 + c] == ((a > b) && (b < 0.5f));
+        }
+    for (size_t r = 0; r < 3 && ok; ++r)
+        for (size_t c = 0; c < 129 && ok; ++c) ok = fu[r * 129 + c] == (int32_t)y[c];
+    EXPECT(ok, "equal / greater / less / where / floor / full / logical_and");
+
+    // sqrt promotes Int32 to Float and Bool to Float16
+    std::vector<int32_t> sq = {0, 1, 2, 4, 9, 1000000, 7, 65536};
+    matrix R = matrix::sqrt(matrix::from_host(sq.data(), {8}, dtype::Int32));
+    R.eval();
+    std::vector<float> rs = R.to_host<float>();
+    ok = R.type() == dtype::Float && rs.size() == 8;
+    for (int i = 0; ok && i < 8; ++i) ok = rs[i] == std::sqrt((float)sq[i]);
+    EXPECT(ok, "sqrt(Int32) is a correctly rounded Float sqrt");
+    matrix RB = matrix::sqrt(G);
+    EXPECT(RB.type() == dtype::Float16, "sqrt(Bool) is Float16");
+
+    // mean / rms / norm
+    const std::vector<size_m> shape = {64, 4096};
+    std::vector<float> h(total(shape));
+    std::normal_distribution<float> d(0.f, 1.f);
+    for (auto& v : h) v = d(rng);
+    matrix H = matrix::from_host(h.data(), shape, dtype::Float);
+    matrix mean = H.mean(1), rms = H.rms(-1), norm = H.norm(1, true), all = H.mean();
+    for (matrix* m : {&mean, &rms, &norm, &all}) m->eval();
+    EXPECT(std::string(mean.tape()->name()) == "Mean", "mean is one fused node");
+    EXPECT(norm.shape() == std::vector<size_m>({64, 1}), "norm keepdims shape");
+    std::vector<float> mv = mean.to_host<float>(), rv = rms.to_host<float>(), nv = norm.to_host<float>();
+    ok = true;
+    double tot = 0, tabs = 0;
+    for (size_t r = 0; r < 64 && ok; ++r) {
+        double s = 0, a = 0, q = 0;
+        for (size_t c = 0; c < 4096; ++c) {
+            const double v = h[r * 4096 + c];
+            s += v;
+            a += std::fabs(v);
+            q += (double)((float)(h[r * 4096 + c] * h[r * 4096 + c]));
+        }
+        tot += s;
+        tabs += a;
+        ok = std::fabs(mv[r] - s / 4096) <= 1e-5 * a / 4096 + 1e-7 && std::fabs(rv[r] - std::sqrt(q / 4096)) <= 2e-5 * std::sqrt(q / 4096) &&
+             std::fabs(nv[r] - std::sqrt(q)) <= 2e-5 * std::sqrt(q);
+    }
+    EXPECT(ok, "float mean / rms / norm");
+    EXPECT(std::fabs(all.to_host<float>()[0] - tot / h.size()) <= 1e-5 * tabs / h.size() + 1e-7, "mean of all elements");
+    std::vector<int32_t> hi(4096);
+    for (auto& v : hi) v = (int32_t)rng();
+    matrix HI = matrix::from_host(hi.data(), {4096}, dtype::Int32);
+    matrix mi = HI.mean(0), ni = HI.norm(0);
+    mi.eval();
+    ni.eval();
+    uint32_t s32 = 0, q32 = 0;
+    for (auto v : hi) {
+        s32 += (uint32_t)v;
+        q32 += (uint32_t)v * (uint32_t)v;
+    }
+    volatile float fs = (float)(int32_t)s32, fq = (float)(int32_t)q32;
+    EXPECT(mi.type() == dtype::Float && mi.to_host<float>()[0] == fs / 4096.0f, "int32 mean: wrapped sum / (float)n");
+    EXPECT(ni.to_host<float>()[0] == std::sqrt((float)fq) || (std::isnan(ni.to_host<float>()[0]) && fq < 0),
+           "int32 norm: sqrt of the wrapped sum of wrapped squares");
+}
+
 int main() {
     mtx::init(0);
     std::mt19937 rng(1234);
     test_reductions(rng);
     test_binary(rng);
     test_trace(rng);
+    test_promotion_and_pointwise(rng);
     std::printf("host mirror: %d checks, %d failures\n", checks, failures);
     return failures ? 1 : 0;
 }
