@@ -419,9 +419,11 @@ def run_ours(args):
 # sharded reductions (configs 4 and 5b): the reduced axis is the sharded one
 # ------------------------------------------------------------------------------------------
 def run_sharded(args):
-    """C5b: full Sum of f32 2^32 elements (as [8, 2^29], 16 GiB), or C4: Sum over axes (0, 2) of f32
-    [32, 4096, 2048], with axis 0 sharded over the GPUs (strong scaling: the total is fixed).  A step
-    is the local kernels, the NCCL all-gather of the per-rank partials and the ordered merge."""
+    """A BASELINE config sharded over the GPUs on its leading axis (strong scaling: the total is fixed).
+    C5b: full Sum of f32 2^32 elements (as [8, 2^29], 16 GiB); C4: Sum over axes (0, 2) of f32
+    [32, 4096, 2048]; for both the sharded axis is a reduced one, so a step is the local kernels, the NCCL
+    all-gather of the per-rank partials and the ordered merge.  C1 (Sum of the last axis), C3 (Max and
+    ArgMax over axis 1) and C5a (fused softmax) shard an axis they do not reduce: no collective."""
     import datetime
 
     import torch
@@ -441,28 +443,62 @@ def run_sharded(args):
         dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
     backend.init(local)
     stream = torch.cuda.current_stream(dev)
-    if args.workload == "c5b":
+    wl = args.workload
+    collective = wl in ("c4", "c5b")
+    if wl == "c5b":
         rows, cols = 8, 1 << 29
         shape = (rows, cols)
         desc = "C5b: full Sum of f32 2^32 ~ N(0,1) as [8, 2^29] (16 GiB), rows sharded, all-gather + ordered merge"
-    else:
+    elif wl == "c4":
         rows, cols = 32, 4096 * 2048
         shape = (32, 4096, 2048)
         desc = "C4: Sum over axes (0,2) of f32 [32,4096,2048] ~ N(0,1), axis 0 sharded, all-gather + ordered merge"
+    elif wl == "c1":
+        rows, cols = 1024, 4096
+        shape = (rows, cols)
+        desc = "C1: Sum(axis=-1) of f32 [1024,4096] ~ N(0,1), rows sharded, no collective (16 MiB: L2-resident after warm-up)"
+    elif wl == "c3":
+        rows, cols = 64, 8192 * 1024
+        shape = (64, 8192, 1024)
+        desc = "C3: Max and ArgMax(axis=1) of f32 [64,8192,1024] floor(U*256)/256, axis 0 sharded, no collective"
+    else:
+        rows, cols = 8192, 32768
+        shape = (rows, cols)
+        desc = "C5a: softmax over the last axis of f32 [8192,32768] ~ N(0,4), fused kernel, rows sharded, no collective"
     lo, hi = shard_range(rows, world, rank)
     x = torch.empty((hi - lo, *shape[1:]), device=dev)
     g = torch.Generator(device=dev)
     for r in range(lo, hi):  # every global row from its own seed: the tensor does not depend on N
         g.manual_seed(1000 + r)
-        x[r - lo].normal_(generator=g)
-    total_bytes = rows * cols * 4
+        if wl == "c3":
+            x[r - lo].uniform_(generator=g)
+            x[r - lo].mul_(256).floor_().div_(256)
+        else:
+            x[r - lo].normal_(generator=g)
+            if wl == "c5a":
+                x[r - lo].mul_(2.0)
+    # algorithmic bytes per step: every op reads its input once and writes its output
+    if wl == "c3":
+        total_bytes = 2 * (rows * cols * 4 + rows * 1024 * 4)
+    elif wl == "c5a":
+        total_bytes = 2 * rows * cols * 4
+    elif wl == "c1":
+        total_bytes = rows * cols * 4 + rows * 4
+    else:
+        total_bytes = rows * cols * 4
 
     def step():
-        if args.workload == "c5b":
+        if wl == "c5b":
             part = backend.reduce("sum", x, 1)                    # local axis: no collective
             return reduce_sharded("sum", part, 0, rows)           # sharded axis: gather + merge
-        part = backend.reduce("sum", x, 2)                        # [rows_local, 4096]
-        return reduce_sharded("sum", part, 0, rows)               # [4096]
+        if wl == "c4":
+            part = backend.reduce("sum", x, 2)                    # [rows_local, 4096]
+            return reduce_sharded("sum", part, 0, rows)           # [4096]
+        if wl == "c1":
+            return backend.reduce("sum", x, 1)
+        if wl == "c3":
+            return backend.reduce("max", x, 1), backend.reduce("argmax", x, 1)
+        return backend.softmax_lastdim(x)
 
     result = step()
     torch.cuda.synchronize()
@@ -471,6 +507,11 @@ def run_sharded(args):
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # a bounded sleep kernel (~0.1 ms per step, outside the timed region) keeps the GPU busy while the
+    # host queues the K steps, so the events time the device work rather than the host's launch rate
+    # (C1's 16 MiB step is shorter than one Python launch)
+    if wl in ("c1", "c3", "c5a"):
+        torch.cuda._sleep(200_000 * args.steps)
     e0.record(stream)
     for _ in range(args.steps):
         result = step()
@@ -482,16 +523,30 @@ def run_sharded(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t[0])
-    # correctness: the fp64 sum of the same tensor (torch, as a reference value only)
-    dims = tuple(range(1, x.dim())) if args.workload == "c5b" else (0, 2)
-    ref = x.sum(dim=dims, dtype=torch.float64)
-    absum = x.abs().sum(dim=dims, dtype=torch.float64)
+    # correctness against torch on the same tensor (a reference value only, never the measured path)
+    if collective:
+        dims = tuple(range(1, x.dim())) if wl == "c5b" else (0, 2)
+        ref = x.sum(dim=dims, dtype=torch.float64)
+        absum = x.abs().sum(dim=dims, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ref)
+            dist.all_reduce(absum)
+        ref = ref.sum() if wl == "c5b" else ref
+        absum = absum.sum() if wl == "c5b" else absum
+        ok = bool(((result.double() - ref).abs() <= 1e-5 * absum + 1e-30).all())
+    elif wl == "c1":
+        ok = bool(((result.double() - x.sum(1, dtype=torch.float64)).abs()
+                   <= 1e-5 * x.abs().sum(1, dtype=torch.float64)).all())
+    elif wl == "c3":
+        vals, idx = result
+        ok = bool(torch.equal(vals, x.amax(1)) and torch.equal(idx.long(), x.argmax(1)))
+    else:
+        want = torch.softmax(x.double(), dim=-1)
+        ok = bool(((result.double() - want).abs() <= 1e-5 * want + 1e-30).all())
     if world > 1:
-        dist.all_reduce(ref)
-        dist.all_reduce(absum)
-    ref = ref.sum() if args.workload == "c5b" else ref
-    absum = absum.sum() if args.workload == "c5b" else absum
-    ok = bool(((result.double() - ref).abs() <= 1e-5 * absum + 1e-30).all())
+        flag = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = bool(flag.item())
     if rank == 0:
         peak, _ = measured_peak()
         value = total_bytes * args.steps / (ms / 1e3) / 1e9
@@ -499,7 +554,7 @@ def run_sharded(args):
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) per row)",
                 "config": {"workload": desc, "parallelism": f"axis 0 sharded over {world} GPU(s)",
-                           "l2": "input larger than L2"},
+                           "l2": "input L2-resident (16 MiB)" if wl == "c1" else "input larger than L2"},
                 "frac_of_hbm_peak": round(value / world / peak, 4), "within_tolerance_of_fp64": ok}
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -520,8 +575,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--rows", type=int, default=256, help="leading rows of a per rank (256 = C2; smaller for ncu)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
-    ap.add_argument("--workload", choices=["c2", "c4", "c5b"], default="c2",
-                    help="c2 (default headline) or a sharded reduction over the GPUs (c4, c5b)")
+    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5a", "c5b"], default="c2",
+                    help="c2 (default headline) or another config sharded over the GPUs: c1, c3, c5a (no "
+                         "collective), c4, c5b (all-gather + ordered merge of the reduced-axis partials)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
