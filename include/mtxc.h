@@ -337,8 +337,9 @@ int mtxc_pointwise(int op, int dtype, void* dst, const void* const* inputs, uint
 /* Fused evaluation of the reference's softmax trace over the last axis of contiguous float rows
  *     m = x.max(-1, true); e = matrix::exp(x - m); y = e / e.sum(-1, true)
  * (MaxReduction, Subtraction, Exp, Sum and Division primitives; BASELINE config 5a): x is read once
- * and y written once.  Element-wise identical to the trace (same max, x - m, expf, one division)
- * except for the order of the fp32 additions in the row sum.  Rows start row_stride elements apart;
+ * and y written once.  Element-wise the trace's arithmetic (same max, x - m, expf) except for the order
+ * of the fp32 additions in the row sum and y = e * (1 / s), one correctly rounded reciprocal per row,
+ * within 1 ulp of the trace's e / s.  Rows start row_stride elements apart;
  * row_len must be a multiple of 4, rows 16-byte aligned and row_len <= MTXC_SOFTMAX_MAX_ROW, else
  * MTXC_ERR_INVALID_ARGUMENT (evaluate the unfused trace instead).  A compiled trace substitutes it
  * for those five primitives when their shapes match (no counterpart kernel in the reference, which
