@@ -330,8 +330,11 @@ int launch_map(const MapDesc& m, int sm_count, cudaStream_t stream) {
             a.sd[j] = sd[j];
             for (int i = 0; i < A; ++i) a.ss[i][j] = ss[i][j];
         }
+        // one block per rpb work units: measured on B200 against grids of 2-64 blocks per SM looping over
+        // the units, the hardware block scheduler balances best (u8 -> f32 astype 0.83 -> 0.98 of the
+        // measured copy bandwidth, where 0.82 -> 0.98)
         const uint32_t rpb = kBlock / tpr;
-        const uint64_t blocks = std::min<uint64_t>((a.units + rpb - 1) / rpb, (uint64_t)sm_count * 4);
+        const uint64_t blocks = (a.units + rpb - 1) / rpb;
         map_rows_kernel<Op, W, S::U><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         return check_launch("map_rows_kernel");
     }
