@@ -372,6 +372,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+    sustained = sustained_copy_gbs(dev, stream, elapsed_ms) if rank == 0 and args.rows == 256 else None
 
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -393,7 +394,12 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "broadcast_rows_kernel", "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-                         if peak_kind == "measured" else "fallback 6.65 TB/s"},
+                         if peak_kind == "measured" else "fallback 6.65 TB/s",
+                         "sustained_copy_gbs": sustained,
+                         "frac_of_sustained_copy": round(achieved / sustained, 4) if sustained else None,
+                         "sustained_note": "a device copy of random f32 (2 GiB read + 2 GiB written per copy) back to "
+                                           "back for as long as the timed region, on the same GPU right after it: the "
+                                           "bandwidth a long stream keeps under the 1 kW power cap"},
             "clocks": clocks,
             "e2e": {"value": round(e2e_value, 3) if e2e_value else None, "unit": UNIT,
                     "h2d_bytes_per_step": (a.numel() + b.numel()) * 4, "d2h_bytes_per_step": nbytes_out * len(OPS),
@@ -413,6 +419,32 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def sustained_copy_gbs(dev, stream, ms_target: float) -> float:
+    """Bandwidth of a plain device copy of random f32 data (torch's copy kernel, used only as a
+    reference denominator), run back to back for about `ms_target` ms: what a memory stream sustains
+    once the power cap is reached, next to the burst copy figure in MEASURED_PEAKS.json."""
+    import torch
+
+    n = 1 << 29  # 2 GiB
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    src = torch.rand(n, generator=g, device=dev)
+    dst = torch.empty_like(src)
+    for _ in range(3):
+        dst.copy_(src)
+    copies = max(3, int(ms_target / 0.66))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(copies):
+        dst.copy_(src)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    gbs = copies * 2 * n * 4 / (e0.elapsed_time(e1) / 1e3) / 1e9
+    del src, dst
+    return round(gbs, 1)
 
 
 # ------------------------------------------------------------------------------------------

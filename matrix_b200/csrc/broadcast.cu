@@ -30,6 +30,12 @@ namespace {
 
 constexpr int kBlock = 256;
 constexpr uint32_t kSegVecs = 4096;
+// Rows per work unit of the grouped kernel.  Measured on B200 (C2, random data, 200 back-to-back
+// launch pairs, one CTA per work unit): the row kernel 0.88 of the measured copy bandwidth, R = 2 0.89,
+// R = 4 0.94, R = 8 0.96.
+// Division is long per element (and 8 rows of its code use up to 255 registers): 2 rows for it.
+template <int OP>
+constexpr int kGroupRows = OP == MTXC_BINARY_DIV ? 2 : 8;
 
 template <int OP, typename T>
 __device__ __forceinline__ T apply(T x, T y) {
@@ -163,6 +169,107 @@ __global__ void __launch_bounds__(kBlock) broadcast_rows_kernel(const RowArgs ar
 }
 
 // ------------------------------------------------------------------------------------------
+// grouped rows: both operands contiguous along the row, and one of them broadcast (stride 0) along
+// the next axis out.  Consecutive rows of that axis then share that operand's row (C2: every
+// a[i, 0, :] serves the 512 rows b[0, j, :]).  A work unit covers R such rows: the shared operand's
+// vector is loaded once for R outputs, the other operand's R vectors once each, so the reads from L2
+// per 16-byte output vector drop from 2 to (1 + R) / R.  The operands live in L2 (C2: 12 MiB); what
+// the row kernel spends there is the SM <-> L2 traffic of two reads next to every write.
+// ------------------------------------------------------------------------------------------
+struct GroupArgs {
+    void* r;
+    const void* a;
+    const void* b;
+    uint32_t vec_per_row;
+    uint32_t seg_vecs;
+    uint32_t segs;
+    uint32_t extent;      // rows along the grouped axis (shape[k-1])
+    uint32_t groups;      // ceil(extent / R)
+    uint32_t units;       // (rows / extent) * groups * segs
+    uint32_t tpr;
+    uint32_t other_stride;  // the non-shared operand's stride along the grouped axis
+    FastDiv seg_div;
+    FastDiv group_div;    // divides by groups
+    Dims d;               // axes 0 .. k-1 (the grouped axis included): shape, a strides (s0), b strides (s1)
+};
+
+template <int OP, typename T, bool SHARE_A, int R>
+__global__ void __launch_bounds__(kBlock) broadcast_group_kernel(const GroupArgs g) {
+    constexpr int V = Vec16<T>::N;
+    constexpr uint32_t U = 2;  // vector positions in flight per thread (each with 1 + R loads)
+    const uint32_t rows_per_block = kBlock / g.tpr;
+    const uint32_t sub = threadIdx.x / g.tpr;
+    const uint32_t lane = threadIdx.x % g.tpr;
+    const T* __restrict__ pa = static_cast<const T*>(g.a);
+    const T* __restrict__ pb = static_cast<const T*>(g.b);
+    T* __restrict__ pr = static_cast<T*>(g.r);
+    const uint64_t row_len = (uint64_t)g.vec_per_row * V;
+    for (uint32_t u = blockIdx.x * rows_per_block + sub; u < g.units; u += gridDim.x * rows_per_block) {
+        uint32_t gu = u, seg = 0;
+        if (g.segs > 1) g.seg_div.divmod(u, gu, seg);
+        uint32_t outer, gi;
+        g.group_div.divmod(gu, outer, gi);
+        const uint32_t j0 = gi * R;
+        const uint32_t nr = min((uint32_t)R, g.extent - j0);
+        const uint32_t row0 = outer * g.extent + j0;
+        uint64_t oa = 0, ob = 0;
+        uint32_t rem = row0;
+#pragma unroll 1
+        for (int i = (int)g.d.n - 1; i >= 0; --i) {
+            uint32_t q, idx;
+            g.d.fdiv[i].divmod(rem, q, idx);
+            oa += (uint64_t)idx * g.d.s0[i];
+            ob += (uint64_t)idx * g.d.s1[i];
+            rem = q;
+        }
+        const T* ps = SHARE_A ? pa + oa : pb + ob;  // shared along the group
+        const T* po = SHARE_A ? pb + ob : pa + oa;  // one row per grouped index
+        T* rr = pr + (uint64_t)row0 * row_len;
+        const uint32_t c_end = min(g.vec_per_row, (seg + 1) * g.seg_vecs);
+        uint32_t c = seg * g.seg_vecs + lane;
+        if (nr == (uint32_t)R) {
+            for (; c + (U - 1) * g.tpr < c_end; c += U * g.tpr) {
+                Vec16<T> xs[U], xo[U][R];
+#pragma unroll
+                for (uint32_t k = 0; k < U; ++k) {
+                    const uint64_t e = (uint64_t)(c + k * g.tpr) * V;
+                    xs[k] = load_cached(ps + e);
+#pragma unroll
+                    for (int t = 0; t < R; ++t) xo[k][t] = load_cached(po + (uint64_t)t * g.other_stride + e);
+                }
+#pragma unroll
+                for (uint32_t k = 0; k < U; ++k) {
+                    const uint64_t e = (uint64_t)(c + k * g.tpr) * V;
+#pragma unroll
+                    for (int t = 0; t < R; ++t) {
+                        Vec16<T> out;
+#pragma unroll
+                        for (int j = 0; j < V; ++j)
+                            out.v[j] = SHARE_A ? apply<OP, T>(xs[k].v[j], xo[k][t].v[j])
+                                               : apply<OP, T>(xo[k][t].v[j], xs[k].v[j]);
+                        store_stream(rr + (uint64_t)t * row_len + e, out);
+                    }
+                }
+            }
+        }
+        // the tail of a segment, and every vector of a partial last group (extent not a multiple of R)
+        for (; c < c_end; c += g.tpr) {
+            const uint64_t e = (uint64_t)c * V;
+            const Vec16<T> xs = load_cached(ps + e);
+#pragma unroll 1
+            for (uint32_t t = 0; t < nr; ++t) {
+                const Vec16<T> xo = load_cached(po + (uint64_t)t * g.other_stride + e);
+                Vec16<T> out;
+#pragma unroll
+                for (int j = 0; j < V; ++j)
+                    out.v[j] = SHARE_A ? apply<OP, T>(xs.v[j], xo.v[j]) : apply<OP, T>(xo.v[j], xs.v[j]);
+                store_stream(rr + (uint64_t)t * row_len + e, out);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // generic: the reference's per-element decode (Matrix.mm:7486-7494)
 // ------------------------------------------------------------------------------------------
 struct GenericArgs {
@@ -230,6 +337,43 @@ int launch_broadcast(void* r, const void* a, const void* b, uint32_t cdims, cons
                    (sb[k] == 0 || aligned16(b)) && total / shape[k] < (1ull << 32);
     for (uint32_t i = 0; i < k && rows_ok; ++i)
         rows_ok = shape[i] == 1 || ((sa[k] == 0 || sa[i] % V == 0) && (sb[k] == 0 || sb[i] % V == 0));
+    // grouped rows: both operands contiguous along the row, exactly one broadcast along axis k - 1
+    if (rows_ok && k >= 1 && sa[k] == 1 && sb[k] == 1 && (sa[k - 1] == 0) != (sb[k - 1] == 0) &&
+        shape[k - 1] >= (uint32_t)kGroupRows<OP>) {
+        const bool share_a = sa[k - 1] == 0;
+        GroupArgs g{};
+        g.r = r;
+        g.a = a;
+        g.b = b;
+        g.vec_per_row = shape[k] / V;
+        g.seg_vecs = std::min<uint32_t>(g.vec_per_row, kSegVecs);
+        g.segs = (g.vec_per_row + g.seg_vecs - 1) / g.seg_vecs;
+        g.extent = shape[k - 1];
+        g.groups = (g.extent + kGroupRows<OP> - 1) / kGroupRows<OP>;
+        g.other_stride = share_a ? sb[k - 1] : sa[k - 1];
+        const uint64_t units = (total / shape[k] / g.extent) * g.groups * g.segs;
+        uint32_t tpr = 1;
+        while (tpr < g.seg_vecs && tpr < (uint32_t)kBlock) tpr <<= 1;
+        g.tpr = tpr;
+        g.seg_div = FastDiv(g.segs);
+        g.group_div = FastDiv(g.groups);
+        g.d.n = k;
+        for (uint32_t i = 0; i < k; ++i) {
+            g.d.shape[i] = shape[i];
+            g.d.s0[i] = sa[i];
+            g.d.s1[i] = sb[i];
+            g.d.fdiv[i] = FastDiv(shape[i]);
+        }
+        if (units < (1ull << 31)) {
+            g.units = (uint32_t)units;
+            // one CTA per work unit (against 3 and 8 CTAs per SM looping over the units: 0.91 -> 0.94 at R = 4)
+            const uint32_t rows_per_block = kBlock / tpr;
+            const uint64_t blocks = (units + rows_per_block - 1) / rows_per_block;
+            if (share_a) broadcast_group_kernel<OP, T, true, kGroupRows<OP>><<<(unsigned)blocks, kBlock, 0, stream>>>(g);
+            else broadcast_group_kernel<OP, T, false, kGroupRows<OP>><<<(unsigned)blocks, kBlock, 0, stream>>>(g);
+            return check_launch("broadcast_group_kernel");
+        }
+    }
     if (rows_ok) {
         RowArgs args{};
         args.r = r;
