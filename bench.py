@@ -67,7 +67,7 @@ def measured_peak():
 
 def profile_traffic():
     """DRAM bytes (read + write) per launch of the dominant kernel, from the committed ncu summary."""
-    p = REPO / "profiles" / "broadcast_rows_c2_traffic.txt"
+    p = REPO / "profiles" / "broadcast_group_c2_traffic.txt"
     try:
         for line in p.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch:"):
@@ -393,7 +393,7 @@ def run_ours(args):
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "broadcast_rows_kernel", "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                         "kernel": "broadcast_group_kernel", "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6.65 TB/s",
                          "sustained_copy_gbs": sustained,
                          "frac_of_sustained_copy": round(achieved / sustained, 4) if sustained else None,
