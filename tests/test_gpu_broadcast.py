@@ -200,3 +200,33 @@ def test_long_rows_are_segmented(gpu, port):
         check_binary(gpu, port, op, col, [95, 1], [1, 1], 1, big, [95, 70000], [70000, 1], 0, "column first")
     check_exp(gpu, port, a, [n], [1], 0, "one long row")
     check_exp(gpu, port, big, [96, 70000], [70000, 1], 0, "rows")
+
+
+GROUPED = [
+    # (a shape, b shape): both contiguous along the row, exactly one broadcast along the next axis out
+    ([4, 1, 64], [1, 13, 64]),      # a shared; 13 rows = one full group of 8 and a partial one
+    ([1, 21, 32], [6, 1, 32]),      # b shared along the 21-axis (partial last group)
+    ([2, 1, 20480], [1, 9, 20480]),  # rows of 5120 vectors: segmented, and a partial group
+    ([3, 2, 1, 8], [1, 1, 16, 8]),  # several outer axes
+    ([1, 8, 256], [5, 8, 256]),     # neither operand shared along the next axis out: the row kernel
+]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.int32, np.uint8, np.float16], ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("op", OPS)
+def test_grouped_rows(gpu, port, dtype, op):
+    """Layouts the grouped row kernel takes (rows sharing a broadcast operand, 8 per work unit; 2 for
+    division), with partial last groups, the shared operand on either side and segmented rows."""
+    rng = np.random.default_rng(91)
+    for sa, sb in GROUPED:
+        if np.dtype(dtype) == np.float16:
+            a = (rng.standard_normal(int(np.prod(sa))) * 4).astype(np.float16)
+            b = (rng.standard_normal(int(np.prod(sb))) * 4).astype(np.float16)
+        else:
+            a, b = operands(rng, dtype, int(np.prod(sa)), int(np.prod(sb)), op)
+        if op == "div" and np.dtype(dtype).kind in "iu":  # a is the divisor of the swapped check
+            a[a == 0] = 1
+            if np.dtype(dtype).kind == "i":
+                a[a == -1] = 3
+        check_binary(gpu, port, op, a, sa, contiguous_strides(sa), 0, b, sb, contiguous_strides(sb), 0, "grouped")
+        check_binary(gpu, port, op, b, sb, contiguous_strides(sb), 0, a, sa, contiguous_strides(sa), 0, "grouped swapped")
