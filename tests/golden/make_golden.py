@@ -104,6 +104,66 @@ def main() -> int:
             for n in (1, 2, 3)]
         cases.append(rec)
 
+    # the widened rows: Float16 / BFloat16 / Bool reductions and broadcasts, astype over every dtype
+    # pair, exp / sqrt, equal, the make_pointwise family and its collapse, mean / rms / norm
+    from tests.test_oracle_pin_pointwise import ALL_CODES, STORAGE, values
+
+    for code in (1, 10, 7):
+        for shape, strides, off in views[:8]:
+            need = off + sum((e - 1) * s for e, s in zip(shape, strides)) + 1
+            base = values(rng, code, need, special=code != 7)
+            x = strided_view(base, shape, strides, off)
+            bkey = put(base)
+            for axis in range(len(shape)):
+                for op in ("sum", "max", "min", "argmax", "argmin"):
+                    out = ref.reduce(op, x, axis, False, dtype_code=code)
+                    cases.append(dict(kind="reduce_code", op=op, code=code, input=bkey, shape=shape, strides=strides,
+                                      offset=off, axis=axis, output=put(out)))
+        for sa, sb in pairs[:6]:
+            a = values(rng, code, int(np.prod(sa)), special=code != 7).reshape(sa)
+            b = values(rng, code, int(np.prod(sb)), special=code != 7).reshape(sb)
+            for op in ("add", "sub", "mul", "div", "max", "min", "equal"):
+                bb = np.ones_like(b) if (code == 7 and op == "div") else b
+                out = ref.binary(op, a, bb, dtype_code=code)
+                cases.append(dict(kind="binary_code", op=op, code=code, a=put(a), b=put(bb), output=put(out)))
+    for src in ALL_CODES:
+        for dst in ALL_CODES:
+            x = values(rng, src, 24, dst_code=dst, special=dst not in (2, 3, 4, 5, 6, 8, 11, 12)).reshape(4, 6)
+            for view, mc in ((x, True), (x.T, False), (x[:, ::2], True)):
+                out = ref.astype(view, STORAGE[dst], make_contig=mc, src_code=src, dst_code=dst)
+                cases.append(dict(kind="astype", src=src, dst=dst, input=put(x), view=["plain", "T", "step2"][
+                    0 if view is x else (1 if mc is False else 2)], make_contig=mc, output=put(np.ascontiguousarray(out))))
+    for op in ("exp", "sqrt"):
+        for dt in (np.float32, np.float16):
+            x = np.abs(rng.standard_normal(60) * 5).astype(dt).reshape(5, 12) if op == "sqrt" else \
+                (rng.standard_normal(60) * 5).astype(dt).reshape(5, 12)
+            cases.append(dict(kind="unary", op=op, input=put(x), output=put(ref.unary(op, x.T))))
+    for code in ALL_CODES:
+        for s0, s1, s2 in (([3, 1, 5], [4, 5], [3, 4, 1]), ([6], [1], [6]), ([2, 3, 4], [3, 1], [4])):
+            a = values(rng, code, int(np.prod(s0)), special=True).reshape(s0)
+            b = values(rng, code, int(np.prod(s1)), special=True).reshape(s1)
+            c = rng.integers(0, 2, int(np.prod(s2))).astype(np.bool_).reshape(s2)
+            for op, ins in (("greater", [a, b]), ("less", [a, b]), ("where", [c, a, b]), ("floor", [a]), ("full", [b])) + \
+                    ((("logical_and", [a, b]),) if code == 7 else ()):
+                out = ref.pointwise(op, ins, dtype_code=code)
+                cases.append(dict(kind="pointwise", op=op, code=code, inputs=[put(i) for i in ins], output=put(out)))
+    from tests.test_oracle_pin_pointwise import _collapse_case
+
+    for trial in range(200):
+        shape, rows = _collapse_case(rng)
+        try:
+            want = ref.pointwise_collapse(shape, rows)
+        except ValueError:
+            want = None
+        cases.append(dict(kind="pointwise_collapse", shape=shape, rows=rows, collapse=want))
+    for code in ALL_CODES:
+        x = values(rng, code, 4 * 70, special=False).reshape(4, 70)
+        for kind in ("mean", "rms", "norm"):
+            for axis in (0, 1):
+                out, oc = ref.stat(kind, x, axis, False, dtype_code=code)
+                cases.append(dict(kind="stat", stat=kind, code=code, input=put(x), axis=axis, out_code=oc,
+                                  output=put(out)))
+
     (HERE / "cases.json").write_text(json.dumps(cases, separators=(",", ":")))
     np.savez_compressed(HERE / "golden.npz", **arrays)
     print(f"{len(cases)} cases, {len(arrays)} arrays")
