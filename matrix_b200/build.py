@@ -82,8 +82,10 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
     # the C++ host mirror of the reference API (mtx.hpp), a plain C++ library over the C ABI
     host_srcs = sorted(HOST.glob("*.cpp"))
     if host_srcs and (not HOST_LIB.exists() or _stale(HOST_LIB, [*host_srcs, *HOST.glob("*.hpp"), LIB, *headers])):
+        cuda_include = Path(nvcc()).resolve().parent.parent / "include"  # NVTX v3 (header-only)
         run(["g++", "-O2", "-std=c++17", "-fPIC", "-Wall", "-shared", "-I", str(INCLUDE), "-I", str(HOST),
-             "-o", str(HOST_LIB), *map(str, host_srcs), "-L", str(LIBDIR), "-lmtxc", "-Wl,-rpath,$ORIGIN"])
+             "-I", str(cuda_include), "-o", str(HOST_LIB), *map(str, host_srcs), "-L", str(LIBDIR), "-lmtxc",
+             "-ldl", "-Wl,-rpath,$ORIGIN"])
     return LIB
 
 

@@ -7,10 +7,17 @@
 #include <set>
 
 #include "mtxc.h"
+#include "nvtx3/nvToolsExt.h"  // header-only NVTX v3: ranges cost nothing unless a profiler is attached
 
 namespace mtx {
 
 namespace {
+
+// An NVTX range over a scope (eval / compile / execute show up as named ranges in Nsight tools).
+struct Range {
+    explicit Range(const char* name) { nvtxRangePushA(name); }
+    ~Range() { nvtxRangePop(); }
+};
 
 [[noreturn]] void raise(int rc, const std::string& where) {
     std::string msg = where + ": " + mtxc_last_error();
@@ -671,6 +678,7 @@ matrix matrix::reshape(const std::vector<size_m>& shape) const {
 }
 
 void matrix::eval() {
+    Range range("mtx::eval");
     if (!tape_) return;
     if (tape_->evaluated) {
         ensure_buffer(tape_->out_buffer);
@@ -682,6 +690,7 @@ void matrix::eval() {
 }
 
 void matrix::compile() {
+    Range range("mtx::compile");
     if (!tape_) return;
     fuse_graph(*this);
     tape_->eval(*this, EvalType::COMPILE_TRACE);
@@ -690,6 +699,7 @@ void matrix::compile() {
 }
 
 void matrix::execute() {
+    Range range("mtx::execute");
     if (!tape_) return;
     if (!tape_->out_buffer) compile();
     if (!graph_) {

@@ -143,3 +143,56 @@ def test_shard_ranges_cover_the_axis():
             assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
             assert max(h - l for l, h in spans) - min(h - l for l, h in spans) <= 1
             assert shard_offsets(n, world) == [s[0] for s in spans]
+
+
+def _absent_rank_worker(rank, port, mode, results):
+    """Rank 1 joins the group but never reaches the collective: it idles past rank 0's timeout
+    ("idle") or leaves at once ("exit").  Rank 0 runs reduce_sharded and must get an error."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    from matrix_b200.shard import reduce_sharded, shard_range
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        if mode == "idle":
+            time.sleep(12)
+        results[rank] = "left"
+        return  # no destroy: the rank is gone as far as the group knows
+    t0 = time.monotonic()
+    try:
+        lo, hi = shard_range(11, 2, 0)
+        x = torch.from_numpy(make_global(np.int32)[lo:hi].copy())
+        reduce_sharded("sum", x, 0, 11, ops=cpu_ops())
+        results[rank] = "no error"
+    except Exception as e:  # the failure the caller must see
+        results[rank] = f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}: {str(e)[:200]}"
+
+
+@pytest.mark.parametrize("mode", ["idle", "exit"])
+def test_absent_rank_is_an_error_not_a_hang(mode):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_absent_rank_worker, args=(r, port, mode, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p.is_alive() for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert not any(alive), f"a rank hung: {dict(results)}"
+    r0 = results.get(0, "")
+    assert r0.startswith("error after"), dict(results)
+    elapsed = float(r0.split()[2])
+    assert elapsed < 30, r0
+    if mode == "idle":  # the collective itself gave up: after the group's 3 s timeout, not before
+        assert elapsed >= 2.5, r0
