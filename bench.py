@@ -519,13 +519,37 @@ def run_sharded(args):
     else:
         total_bytes = rows * cols * 4
 
+    # C4 / C5b: the local reduction of step k + 1 overlaps the exchange of step k.  The local partials
+    # go to one of two buffers on the main stream; the all-gather and the ordered merge of that buffer
+    # run on a side stream, which waits for the partials, and the main stream does not overwrite a
+    # buffer before the side stream is done with it.
+    side = torch.cuda.Stream(dev)
+    parts = [backend.reduce("sum", x, 1 if wl == "c5b" else 2) for _ in range(2)]
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    for ev in done:
+        ev.record(stream)
+    counter = [0]
+
+    def exchange_step():
+        k = counter[0] % 2
+        counter[0] += 1
+        stream.wait_event(done[k])                                # buffer k free again
+        backend.reduce("sum", x, 1 if wl == "c5b" else 2, out=parts[k])   # local axis: no collective
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        side.wait_event(ready)
+        with torch.cuda.stream(side):
+            backend.set_stream(side)
+            try:
+                r = reduce_sharded("sum", parts[k], 0, rows)      # sharded axis: gather + merge
+            finally:
+                backend.set_stream(stream)
+            done[k].record(side)
+        return r
+
     def step():
-        if wl == "c5b":
-            part = backend.reduce("sum", x, 1)                    # local axis: no collective
-            return reduce_sharded("sum", part, 0, rows)           # sharded axis: gather + merge
-        if wl == "c4":
-            part = backend.reduce("sum", x, 2)                    # [rows_local, 4096]
-            return reduce_sharded("sum", part, 0, rows)           # [4096]
+        if collective:
+            return exchange_step()
         if wl == "c1":
             return backend.reduce("sum", x, 1)
         if wl == "c3":
@@ -541,12 +565,14 @@ def run_sharded(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # a bounded sleep kernel (~0.1 ms per step, outside the timed region) keeps the GPU busy while the
     # host queues the K steps, so the events time the device work rather than the host's launch rate
-    # (C1's 16 MiB step is shorter than one Python launch)
-    if wl in ("c1", "c3", "c5a"):
-        torch.cuda._sleep(200_000 * args.steps)
+    # (C1's 16 MiB step is shorter than one Python launch; C4's sharded step is shorter than the
+    # Python that enqueues its reduction, NCCL all-gather and merge)
+    torch.cuda._sleep(200_000 * args.steps)
     e0.record(stream)
     for _ in range(args.steps):
         result = step()
+    if collective:
+        stream.wait_stream(side)  # the last exchange is inside the timed region
     e1.record(stream)
     torch.cuda.synchronize()
     dist.barrier()
