@@ -299,6 +299,19 @@ int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, const void*
                           const uint32_t* shape, const uint32_t* r_strides, const uint32_t* a_strides,
                           const uint32_t* b_strides);
 
+/* a op b for operands of different dtypes with the promotion fused in: the result equals
+ * mtxc_broadcast_binary(op, dtype, ...) applied to the operands after mtxc_astype to dtype =
+ * promote_types(a_dtype, b_dtype), which is what the reference evaluates (astype of the operand whose dtype
+ * differs, then the op: Matrix.mm:8312-8382), bit for bit -- but in one pass, without writing and
+ * re-reading a converted copy.  Same metadata as mtxc_broadcast_binary (the strides of the operands as
+ * given; the reference's astype keeps them).  Supported: op ADD, SUB, MUL, DIV or EQUAL; dtype Float with
+ * one Float operand and the other of any dtype but Complex64.  Anything else: MTXC_ERR_UNSUPPORTED_DTYPE
+ * (evaluate astype + mtxc_broadcast_binary instead); dtype other than promote_types(a_dtype, b_dtype):
+ * MTXC_ERR_INVALID_ARGUMENT. */
+int mtxc_broadcast_binary_mixed(int op, int dtype, int a_dtype, int b_dtype, void* r, const void* a, const void* b,
+                                uint32_t cdims, const uint32_t* shape, const uint32_t* r_strides,
+                                const uint32_t* a_strides, const uint32_t* b_strides);
+
 /* Elementwise unary op over collapse_dims(shape, out strides, in strides) metadata
  * (Matrix.mm:6798-6925, 6934-7065), on Float or Float16 (the frontends promote other dtypes first).
  * EXP: CUDA expf, within 2 ulp of the CPU's std::exp (Float16: that result rounded once).  SQRT: the

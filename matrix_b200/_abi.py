@@ -80,6 +80,7 @@ def lib() -> C.CDLL:
             "mtxc_reduce_pair": (i32, [i32, i32, vp, vp, vp, u32, u32, u32, U32P, U32P, U32P]),
             "mtxc_merge_partials": (i32, [i32, i32, vp, vp, vp, vp, vp, u32, u64]),
             "mtxc_broadcast_binary": (i32, [i32, i32, vp, vp, vp, u32, U32P, U32P, U32P, U32P]),
+            "mtxc_broadcast_binary_mixed": (i32, [i32, i32, i32, i32, vp, vp, vp, u32, U32P, U32P, U32P, U32P]),
             "mtxc_unary": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),
             "mtxc_softmax_lastdim": (i32, [i32, vp, vp, u64, u32, u64, u64]),
             "mtxc_astype": (i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P]),

@@ -196,12 +196,33 @@ def binary_launch(op: str, a_ptr: int, b_ptr: int, dtype: int, out_ptr: int, met
                                       sb))
 
 
+MIXED_OPS = ("add", "sub", "mul", "div", "equal")
+
+
 def binary(op: str, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
            meta: BinaryMeta | None = None) -> torch.Tensor:
-    """a <op> b with broadcasting, evaluated through mtxc_broadcast_binary.  Both operands must
-    already share a dtype (the reference inserts astype before the op)."""
+    """a <op> b with broadcasting, evaluated through mtxc_broadcast_binary.  Operands of different
+    dtypes are promoted as the reference does (promote_types, astype first): in one pass through
+    mtxc_broadcast_binary_mixed where it covers the pair (a Float result with a Float operand), else with
+    an explicit astype of the operand(s) whose dtype differs."""
     if a.dtype != b.dtype:
-        raise _abi.MtxcError(_abi.ERR_UNSUPPORTED_DTYPE, "operands must share a dtype (astype first)")
+        if op not in MIXED_OPS:
+            raise _abi.MtxcError(_abi.ERR_UNSUPPORTED_DTYPE, "max / min of mixed dtypes: cast one operand first")
+        ca, cb = dtype_code(a.dtype), dtype_code(b.dtype)
+        common = lib().mtxc_promote_types(ca, cb)
+        if common == 0 and 0 in (ca, cb):
+            if meta is None:
+                meta = binary_meta(list(a.shape), _check_strides(a), list(b.shape), _check_strides(b))
+            if out is None:
+                out = torch.empty(meta.out_shape, dtype=torch.float32, device=a.device)
+            shape, sr, sa, sb = meta.arrays
+            check(lib().mtxc_broadcast_binary_mixed(_abi.BINARY_OPS[op], 0, ca, cb, out.data_ptr(), a.data_ptr(),
+                                                     b.data_ptr(), meta.cdims, shape, sr, sa, sb))
+            return out
+        t = CODE_TO_TORCH[common]
+        a = a if a.dtype == t else astype(a, t, make_contig=False)
+        b = b if b.dtype == t else astype(b, t, make_contig=False)
+        meta = None
     code = dtype_code(a.dtype)
     if meta is None:
         meta = binary_meta(list(a.shape), _check_strides(a), list(b.shape), _check_strides(b))

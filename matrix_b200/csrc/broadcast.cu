@@ -23,7 +23,7 @@
 //            stride decode.
 #include <algorithm>
 
-#include "mtxc_internal.cuh"
+#include "ops.cuh"
 
 namespace mtxc {
 namespace {
@@ -36,47 +36,6 @@ constexpr uint32_t kSegVecs = 4096;
 // Division is long per element (and 8 rows of its code use up to 255 registers): 2 rows for it.
 template <int OP>
 constexpr int kGroupRows = OP == MTXC_BINARY_DIV ? 2 : 8;
-
-template <int OP, typename T>
-__device__ __forceinline__ T apply(T x, T y) {
-    if constexpr (OP == MTXC_BINARY_EQUAL) {  // matrix::equal: T(1) or T(0) (Matrix.mm:14536)
-        if constexpr (Traits<T>::kFloat) return from_float<T>(equal(x, y) ? 1.0f : 0.0f);
-        else if constexpr (Traits<T>::kBool) return mbool(x == y);
-        else return equal(x, y) ? T(1) : T(0);
-    } else if constexpr (OP == MTXC_BINARY_MAX) return less(x, y) ? y : x;  // std::max: x unless x < y
-    else if constexpr (OP == MTXC_BINARY_MIN) return less(y, x) ? y : x;  // std::min: x unless y < x
-    else if constexpr (Traits<T>::kFloat) {
-        // one round-to-nearest operation in fp32; for the half types the fp32 result rounded once to
-        // T is the correctly rounded half-precision result (fp32 carries more than 2p + 2 bits)
-        const float a = to_float(x), b = to_float(y);
-        float r;
-        if constexpr (OP == MTXC_BINARY_ADD) r = __fadd_rn(a, b);
-        else if constexpr (OP == MTXC_BINARY_SUB) r = __fsub_rn(a, b);
-        else if constexpr (OP == MTXC_BINARY_MUL) r = __fmul_rn(a, b);
-        else r = __fdiv_rn(a, b);
-        return from_float<T>(r);
-    } else if constexpr (Traits<T>::kBool) {
-        // C++ bool arithmetic: promote to int, convert the result back to bool
-        const int a = (uint8_t)x, b = (uint8_t)y;
-        int r;
-        if constexpr (OP == MTXC_BINARY_ADD) r = a + b;
-        else if constexpr (OP == MTXC_BINARY_SUB) r = a - b;
-        else if constexpr (OP == MTXC_BINARY_MUL) r = a * b;
-        else r = b ? a / b : 0;
-        return mbool(r != 0);
-    } else {
-        // integers: C++ promotion then truncation back to T, with the + - * done in unsigned
-        // arithmetic so that overflow wraps as it does on the reference's CPU
-        using W = std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>;
-        if constexpr (OP == MTXC_BINARY_ADD) return (T)(W)((W)x + (W)y);
-        else if constexpr (OP == MTXC_BINARY_SUB) return (T)(W)((W)x - (W)y);
-        else if constexpr (OP == MTXC_BINARY_MUL) return (T)(W)((W)x * (W)y);
-        else {
-            using P = decltype(x / y);  // the promoted type the reference divides in
-            return (T)((P)x / (P)y);
-        }
-    }
-}
 
 // ------------------------------------------------------------------------------------------
 // rows: contiguous result, innermost operand strides in {0, 1}

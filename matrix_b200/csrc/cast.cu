@@ -15,53 +15,10 @@
 //   the destination; outside that range the reference's result depends on its compiler, and this
 //   kernel gives the low bits of the 64-bit truncation (saturated at the int64 range, NaN -> 0).
 #include "elementwise.cuh"
+#include "ops.cuh"
 
 namespace mtxc {
 namespace {
-
-template <typename T>
-constexpr bool kFloatLike = Traits<T>::kFloat;
-template <typename T>
-constexpr bool kBoolT = std::is_same_v<T, mbool>;
-
-template <typename D, typename S>
-__device__ __forceinline__ D convert(S x) {
-    if constexpr (std::is_same_v<D, S>) {
-        return x;
-    } else if constexpr (kBoolT<D>) {
-        if constexpr (kFloatLike<S>) return mbool(to_float(x) != 0.0f);
-        else return mbool(x != S(0));
-    } else if constexpr (kBoolT<S>) {
-        const uint32_t v = static_cast<uint8_t>(x) != 0;
-        if constexpr (kFloatLike<D>) return from_float<D>((float)v);
-        else return D(v);
-    } else if constexpr (kFloatLike<D> && kFloatLike<S>) {
-        return from_float<D>(to_float(x));  // exact widening, then one rounding
-    } else if constexpr (kFloatLike<D>) {  // integer -> float-like
-        if constexpr (std::is_same_v<D, float>) {
-            return static_cast<float>(x);  // cvt.rn
-        } else if constexpr (sizeof(S) <= 2 || std::is_same_v<D, __half>) {
-            // exact in float below 2^24; every larger integer rounds to +-inf in half precision
-            return from_float<D>(static_cast<float>(x));
-        } else if constexpr (std::is_same_v<S, int32_t>) {
-            return __int2bfloat16_rn(x);
-        } else if constexpr (std::is_same_v<S, uint32_t>) {
-            return __uint2bfloat16_rn(x);
-        } else if constexpr (std::is_same_v<S, int64_t>) {
-            return __ll2bfloat16_rn((long long)x);
-        } else {
-            return __ull2bfloat16_rn((unsigned long long)x);
-        }
-    } else if constexpr (kFloatLike<S>) {  // float-like -> integer
-        const float f = to_float(x);
-        if constexpr (std::is_same_v<D, uint64_t>) {
-            if (f >= 9223372036854775808.0f) return (uint64_t)__float2ull_rz(f);
-        }
-        return static_cast<D>((uint64_t)__float2ll_rz(f));
-    } else {
-        return static_cast<D>(x);  // integer -> integer: modulo 2^bits
-    }
-}
 
 template <typename D, typename S>
 struct CastOp {

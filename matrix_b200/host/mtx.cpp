@@ -161,9 +161,14 @@ public:
         if (t == EvalType::COMPILE_TRACE) return;
         if (evaluated) return;
         evaluated = true;
-        check(mtxc_broadcast_binary(op_, (int)a_.type(), out.data(), a_.data(), b_.data(), cdims_, shape_, sr_, sa_,
-                                    sb_),
-              "mtxc_broadcast_binary");
+        if (a_.type() != b_.type())  // promotion fused into the op (Float result, one Float operand)
+            check(mtxc_broadcast_binary_mixed(op_, (int)out.type(), (int)a_.type(), (int)b_.type(), out.data(),
+                                              a_.data(), b_.data(), cdims_, shape_, sr_, sa_, sb_),
+                  "mtxc_broadcast_binary_mixed");
+        else
+            check(mtxc_broadcast_binary(op_, (int)a_.type(), out.data(), a_.data(), b_.data(), cdims_, shape_, sr_,
+                                        sa_, sb_),
+                  "mtxc_broadcast_binary");
     }
     void clear_trace_checks() override {
         evaluated = false;
@@ -421,8 +426,13 @@ matrix make_binary(int op, const matrix& a, const matrix& b) {
     if (!promotes && a.type() != b.type())
         throw std::runtime_error("max / min(a, b) of mixed dtypes: cast one operand with astype first");
     const dtype common = promote_types(a.type(), b.type());
-    const matrix lhs = a.type() == common ? a : a.astype(common);
-    const matrix rhs = b.type() == common ? b : b.astype(common);
+    // a Float result with one Float operand: the conversion happens inside the op's kernel
+    // (mtxc_broadcast_binary_mixed), same bits as astype + op without the promoted copy
+    const bool fused = promotes && a.type() != b.type() && common == dtype::Float &&
+                       (a.type() == dtype::Float || b.type() == dtype::Float) && a.type() != dtype::Complex64 &&
+                       b.type() != dtype::Complex64;
+    const matrix lhs = (a.type() == common || fused) ? a : a.astype(common);
+    const matrix rhs = (b.type() == common || fused) ? b : b.astype(common);
     std::vector<size_m> out_shape;
     auto prim = std::make_shared<BinaryPrimitive>(op, lhs, rhs, out_shape);
     matrix out;

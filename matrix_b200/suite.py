@@ -68,7 +68,7 @@ def run_all(dev, stream, configs=None, scale=1):
     peak = _peak()
     g = torch.Generator(device=dev)
     out = []
-    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4"}
+    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4", "F5"}
 
     # C1: Sum over the last axis of f32 [1024, 4096] ~ N(0,1)
     if "C1" in want:
@@ -87,6 +87,8 @@ def run_all(dev, stream, configs=None, scale=1):
         _f3(out, dev, stream, g, peak, scale)
     if "F4" in want:
         _f4(out, dev, stream, g, peak, scale)
+    if "F5" in want:
+        _f5(out, dev, stream, g, peak, scale)
     torch.cuda.empty_cache()
     return out
 
@@ -254,3 +256,25 @@ def _f4(out, dev, stream, g, peak, scale):
     ms = _time(lambda: backend.binary("equal", a, b), stream)
     out.append(_line("F4-equal", "equal(a f32 [8192,32768], b f32 [32768]) -> f32", n * 8 + 32768 * 4, ms, peak))
     del a, b, c
+
+
+def _f5(out, dev, stream, g, peak, scale):
+    """int32 [8192, 32768] + f32 [32768] -> f32: promotion fused into the op, and as the reference's
+    astype + add."""
+    rows = max(8192 // scale, 1)
+    g.manual_seed(9)
+    a = torch.randint(-1000, 1001, (rows, 32768), generator=g, device=dev, dtype=torch.int32)
+    b = torch.randn(32768, generator=g, device=dev)
+    n = a.numel()
+    ms = _time(lambda: backend.binary("add", a, b), stream)
+    out.append(_line("F5-mixed-fused", "int32 [8192,32768] + f32 [32768] -> f32, promotion fused (mtxc_broadcast_binary_mixed)",
+                     n * 8 + 32768 * 4, ms, peak))
+
+    def unfused():
+        af = backend.astype(a, torch.float32, make_contig=False)
+        return backend.binary("add", af, b)
+
+    ms = _time(unfused, stream)
+    out.append(_line("F5-mixed-astype-then-add", "the same as the reference runs it: astype to f32, then add (2 kernels)",
+                     n * 8 + 32768 * 4, ms, peak, moved_bytes=n * 16 + 32768 * 4))
+    del a, b
