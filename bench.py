@@ -408,6 +408,9 @@ def run_ours(args):
         }
         if world == 1 and not args.no_cpu and args.rows == 256:
             line["cpu_baseline"] = cpu_baseline_line(os.cpu_count() or 1, target_s=args.cpu_seconds)
+            # the reference's loop is single-threaded: its own one-core speed, beside the row-sliced figure
+            one = cpu_baseline_line(1, target_s=max(2.0, args.cpu_seconds / 3))
+            line["cpu_baseline"]["single_thread"] = {"value": one["value"], "cores": 1, "sample": one["sample"]}
         print(json.dumps(line), flush=True)
         if args.suite:
             from matrix_b200 import suite
