@@ -114,13 +114,25 @@ struct Reducer<MTXC_REDUCE_SUM, T> {
     }
 };
 
-// Extremum with index (float-likes for Max / Min; every type for ArgMax / ArgMin).
+// Extremum with index (float-likes for Max / Min; every type for ArgMax / ArgMin).  The half types keep
+// the running value in float: the widening is exact, so comparisons, NaN and ties are unchanged, and each
+// element is converted once instead of at every comparison.
 template <typename T, bool kMax>
 struct PairExtremum {
-    using State = Pair<T>;
-    __device__ static State init() { return State{kMax ? lowest_value<T>() : highest_value<T>(), 0}; }
-    __device__ static bool beats(T a, T b) { return kMax ? less(b, a) : less(a, b); }
-    __device__ static void fold(State& s, T v, uint32_t i) {
+    using V = std::conditional_t<Traits<T>::kFloat, float, T>;
+    using State = Pair<V>;
+    __device__ static V widen(T v) {
+        if constexpr (Traits<T>::kFloat) return to_float(v);
+        else return v;
+    }
+    __device__ static T narrow(V v) {
+        if constexpr (Traits<T>::kFloat) return from_float<T>(v);  // exact: v came from a T
+        else return v;
+    }
+    __device__ static State init() { return State{widen(kMax ? lowest_value<T>() : highest_value<T>()), 0}; }
+    __device__ static bool beats(V a, V b) { return kMax ? less(b, a) : less(a, b); }
+    __device__ static void fold(State& s, T x, uint32_t i) {
+        const V v = widen(x);
         if (beats(v, s.v)) {
             s.v = v;
             s.i = (int32_t)i;
@@ -152,7 +164,7 @@ template <typename T>
 struct Reducer<MTXC_REDUCE_MAX, T> : ExtremumOf<T, true> {
     using Base = ExtremumOf<T, true>;
     __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
-        if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = s.v;
+        if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = Base::narrow(s.v);
         else static_cast<T*>(o.v)[gid] = s;
     }
 };
@@ -160,31 +172,39 @@ template <typename T>
 struct Reducer<MTXC_REDUCE_MIN, T> : ExtremumOf<T, false> {
     using Base = ExtremumOf<T, false>;
     __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
-        if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = s.v;
+        if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = Base::narrow(s.v);
         else static_cast<T*>(o.v)[gid] = s;
     }
 };
 template <typename T>
 struct Reducer<MTXC_REDUCE_ARGMAX, T> : PairExtremum<T, true> {
-    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(o.v)[gid] = s.i; }
+    using Base = PairExtremum<T, true>;
+    __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
+        static_cast<int32_t*>(o.v)[gid] = s.i;
+    }
 };
 template <typename T>
 struct Reducer<MTXC_REDUCE_ARGMIN, T> : PairExtremum<T, false> {
-    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) { static_cast<int32_t*>(o.v)[gid] = s.i; }
+    using Base = PairExtremum<T, false>;
+    __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
+        static_cast<int32_t*>(o.v)[gid] = s.i;
+    }
 };
 // Max / Min value and its first index in one pass: exactly the Max and ArgMax (Min and ArgMin)
 // results, since a (value, index) state that was never updated holds (initial value, 0).
 template <typename T>
 struct Reducer<kPairMax, T> : PairExtremum<T, true> {
-    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) {
-        static_cast<T*>(o.v)[gid] = s.v;
+    using Base = PairExtremum<T, true>;
+    __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
+        static_cast<T*>(o.v)[gid] = Base::narrow(s.v);
         o.i[gid] = s.i;
     }
 };
 template <typename T>
 struct Reducer<kPairMin, T> : PairExtremum<T, false> {
-    __device__ static void store(const Out& o, uint64_t gid, const Pair<T>& s) {
-        static_cast<T*>(o.v)[gid] = s.v;
+    using Base = PairExtremum<T, false>;
+    __device__ static void store(const Out& o, uint64_t gid, const typename Base::State& s) {
+        static_cast<T*>(o.v)[gid] = Base::narrow(s.v);
         o.i[gid] = s.i;
     }
 };

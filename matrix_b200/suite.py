@@ -68,7 +68,7 @@ def run_all(dev, stream, configs=None, scale=1):
     peak = _peak()
     g = torch.Generator(device=dev)
     out = []
-    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4", "F5"}
+    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4", "F5", "F6"}
 
     # C1: Sum over the last axis of f32 [1024, 4096] ~ N(0,1)
     if "C1" in want:
@@ -89,6 +89,8 @@ def run_all(dev, stream, configs=None, scale=1):
         _f4(out, dev, stream, g, peak, scale)
     if "F5" in want:
         _f5(out, dev, stream, g, peak, scale)
+    if "F6" in want:
+        _f6(out, dev, stream, g, peak, scale)
     torch.cuda.empty_cache()
     return out
 
@@ -278,3 +280,29 @@ def _f5(out, dev, stream, g, peak, scale):
     out.append(_line("F5-mixed-astype-then-add", "the same as the reference runs it: astype to f32, then add (2 kernels)",
                      n * 8 + 32768 * 4, ms, peak, moved_bytes=n * 16 + 32768 * 4))
     del a, b
+
+
+def _f6(out, dev, stream, g, peak, scale):
+    """The half-precision kernels at the configs' shapes: bf16 broadcast Add (C2), f16 Max and ArgMax over
+    axis 1 (C3), bf16 full Sum of 2^31 elements."""
+    g.manual_seed(10)
+    b0 = max(256 // scale, 1)
+    a = (torch.rand(b0, 1, 4096, generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+    b = (torch.rand(1, 512, 4096, generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+    outb = torch.empty(b0, 512, 4096, dtype=torch.bfloat16, device=dev)
+    meta = backend.binary_meta(list(a.shape), list(a.stride()), list(b.shape), list(b.stride()))
+    ms = _time(lambda: backend.binary("add", a, b, out=outb, meta=meta), stream)
+    out.append(_line("F6-bf16-add-C2", "broadcast Add bf16 a[256,1,4096] + b[1,512,4096]", outb.numel() * 2 +
+                     (a.numel() + b.numel()) * 2, ms, peak))
+    del a, b, outb
+    c0 = max(64 // scale, 1)
+    x = (torch.floor(torch.rand(c0, 8192, 1024, generator=g, device=dev) * 256) / 256).to(torch.float16)
+    ms = _time(lambda: backend.reduce("max", x, 1), stream)
+    out.append(_line("F6-f16-max-C3", "Max(axis=1) f16 [64,8192,1024]", x.numel() * 2 + c0 * 1024 * 2, ms, peak))
+    ms = _time(lambda: backend.reduce("argmax", x, 1), stream)
+    out.append(_line("F6-f16-argmax-C3", "ArgMax(axis=1) f16 [64,8192,1024]", x.numel() * 2 + c0 * 1024 * 4, ms, peak))
+    del x
+    y = torch.randn(8, (1 << 28) // scale, generator=g, device=dev).to(torch.bfloat16)
+    ms = _time(lambda: backend.reduce("sum", y, 1), stream)
+    out.append(_line("F6-bf16-sum", "Sum(axis=1) bf16 [8, 2^28] (4 GiB)", y.numel() * 2, ms, peak))
+    del y
