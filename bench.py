@@ -224,6 +224,56 @@ def cpu_baseline_line(threads: int, target_s: float = 10.0):
                       f"{threads} thread(s) over row slices, {dt:.2f} s"}
 
 
+def suite_cpu_hook():
+    """CPU leg of the --suite lines: the reference's own loop (oracle/_ref, else the restatement) on a
+    leading-axis slice of the config's input, timed on one host core, and the GPU's result for the same
+    slice compared with it (bit-exact, or the float-sum rule: within 1e-5 * sum|x| of the CPU or of the
+    exact fp64 sum)."""
+    import numpy as np
+
+    from oracle import oracle
+
+    ev = oracle.reference()
+    kind = "reference"
+    if ev is None:
+        ev, kind = oracle.port(), "port"
+
+    def hook(line, spec):
+        import torch
+
+        xs = spec["sample"].contiguous()
+        a = xs.cpu().numpy()
+        g = spec["gpu"](xs)
+        torch.cuda.synchronize()
+        g = g.cpu().numpy()
+        t0 = time.perf_counter()
+        c = spec["cpu"](ev, a)
+        dt = time.perf_counter() - t0
+        line["cpu_reference"] = {"GB/s": round(a.nbytes / dt / 1e9, 4), "cores": 1, "kind": kind,
+                                 "sample": spec["desc"], "ms": round(dt * 1e3, 2)}
+        with np.errstate(invalid="ignore"):
+            if spec["kind"] == "exact":
+                ok = g.shape == c.shape and bool(np.array_equal(g, c, equal_nan=True))
+                verdict = "bit-exact" if ok else "MISMATCH"
+            elif spec["kind"] == "softmax":
+                x64 = a.astype(np.float64)
+                e = np.exp(x64 - x64.max(-1, keepdims=True))
+                e /= e.sum(-1, keepdims=True)
+                ok = bool((np.abs(g - c) <= 1e-5 * np.abs(c) + 1e-30).all() or
+                          (np.abs(g - e) <= 1e-5 * e + 1e-30).all())
+                verdict = "within rel 1e-5" if ok else "MISMATCH"
+            else:
+                x64 = a.astype(np.float64)
+                ax = spec["axis"]
+                exact = x64.sum(axis=ax)
+                tol = 1e-5 * np.abs(x64).sum(axis=ax) + 1e-30
+                ok = bool(((np.abs(g - c) <= tol) | (np.abs(g - exact) <= tol)).all())
+                verdict = "within 1e-5 * sum|x|" if ok else "MISMATCH"
+        line["parity_on_sample"] = verdict
+
+    return hook
+
+
 # ------------------------------------------------------------------------------------------
 # reference arm
 # ------------------------------------------------------------------------------------------
@@ -416,7 +466,8 @@ def run_ours(args):
             from matrix_b200 import suite
 
             cfgs = args.suite_configs.split(",") if args.suite_configs else None
-            for extra in suite.run_all(dev, stream, cfgs, args.suite_scale):
+            hook = None if args.no_cpu else suite_cpu_hook()
+            for extra in suite.run_all(dev, stream, cfgs, args.suite_scale, cpu_hook=hook):
                 print(json.dumps(extra), flush=True)
     if world > 1:
         dist.barrier()

@@ -61,10 +61,22 @@ def _line(name, workload, nbytes, ms, peak, **extra):
     return d
 
 
-def run_all(dev, stream, configs=None, scale=1):
+_CPU_HOOK = None
+
+
+def _cpu(line, **spec):
+    """Hands a config's sample to the caller's CPU-reference hook (bench.py: the reference's own loop
+    timed on a leading-axis slice of the same input, and that slice's GPU result compared with it)."""
+    if _CPU_HOOK is not None:
+        _CPU_HOOK(line, spec)
+
+
+def run_all(dev, stream, configs=None, scale=1, cpu_hook=None):
     """configs: names to run (default all: C1 C3 C4 C5a C5b, and F2 F3 F4 for the statistics, astype
     and pointwise kernels); scale: divide each config's leading extent by this (small cases for
     profiling)."""
+    global _CPU_HOOK
+    _CPU_HOOK = cpu_hook
     peak = _peak()
     g = torch.Generator(device=dev)
     out = []
@@ -107,6 +119,8 @@ def _c1(out, dev, stream, g, peak):
                flush=lambda: torch.sum(scratch, dim=0, out=sink))
     out.append(_line("C1", "Sum(axis=-1) f32 [1024,4096] (L2 flushed before each rep)", 1024 * 4096 * 4 + 4096, ms,
                      peak))
+    _cpu(out[-1], sample=x, gpu=lambda t: backend.reduce("sum", t, -1), cpu=lambda ev, a: ev.reduce("sum", a, -1),
+         kind="sum", axis=-1, desc="the whole input")
     # the same launch with the 16 MiB input resident in L2 (126 MB), as it is in a loop over one tensor
     ms = _time(lambda: backend.reduce("sum", x, -1, out=y, meta=m), stream)
     out.append(_line("C1-warm", "Sum(axis=-1) f32 [1024,4096], input L2-resident (not an HBM figure)",
@@ -125,8 +139,12 @@ def _c3(out, dev, stream, g, peak, scale):
     nbytes = b0 * 8192 * 1024 * 4 + b0 * 1024 * 4
     ms = _time(lambda: backend.reduce("max", x, 1, out=vmax, meta=m), stream)
     out.append(_line("C3-max", "Max(axis=1) f32 [64,8192,1024]", nbytes, ms, peak))
+    _cpu(out[-1], sample=x[:1], gpu=lambda t: backend.reduce("max", t, 1), cpu=lambda ev, a: ev.reduce("max", a, 1),
+         kind="exact", desc="x[:1] (32 MiB)")
     ms = _time(lambda: backend.reduce("argmax", x, 1, out=imax, meta=m), stream)
     out.append(_line("C3-argmax", "ArgMax(axis=1) f32 [64,8192,1024]", nbytes, ms, peak))
+    _cpu(out[-1], sample=x[:1], gpu=lambda t: backend.reduce("argmax", t, 1),
+         cpu=lambda ev, a: ev.reduce("argmax", a, 1), kind="exact", desc="x[:1] (32 MiB)")
     ms = _time(lambda: backend.reduce_pair("max", x, 1, meta=m), stream)
     out.append(_line("C3-max+argmax", "Max and ArgMax(axis=1) from one read (mtxc_reduce_pair)", nbytes + b0 * 1024 * 4,
                      ms, peak, ops_served=2))
@@ -152,6 +170,9 @@ def _c4(out, dev, stream, g, peak, scale):
         ms = _time(c4, stream)
         out.append(_line(name, "x.sum(2).sum(0) [32,4096,2048]", b0 * 4096 * 2048 * 4 + 4096 * 4, ms, peak,
                          moved_bytes=b0 * 4096 * 2048 * 4 + 2 * b0 * 4096 * 4 + 4096 * 4))
+        _cpu(out[-1], sample=x[:2], gpu=lambda t: backend.reduce("sum", backend.reduce("sum", t, 2), 0),
+             cpu=lambda ev, a: ev.reduce("sum", ev.reduce("sum", a, 2), 0),
+             kind="sum" if name == "C4-f32" else "exact", axis=(0, 2), desc="x[:2] (64 MiB)")
         del x, mid
 
 
@@ -182,6 +203,13 @@ def _c5a(out, dev, stream, g, peak, scale):
     ms = _time(lambda: backend.softmax_lastdim(x, out=t), stream)
     out.append(_line("C5a-fused", "softmax trace fused (mtxc_softmax_lastdim) f32 [8192,32768]", 2 * n, ms, peak,
                      moved_bytes=2 * n))
+
+    def cpu_trace(ev, a):
+        e = ev.unary("exp", ev.binary("sub", a, ev.reduce("max", a, -1, True)))
+        return ev.binary("div", e, ev.reduce("sum", e, -1, True))
+
+    _cpu(out[-1], sample=x[:16], gpu=lambda v: backend.softmax_lastdim(v), cpu=cpu_trace, kind="softmax",
+         desc="x[:16] (2 MiB), the reference's five-primitive trace on the CPU")
     del x, t
 
 
@@ -201,6 +229,8 @@ def _c5b(out, dev, stream, g, peak, scale):
 
     ms = _time(c5b, stream, reps=5)
     out.append(_line("C5b", "full Sum f32 2^32 as [8,2^29] (1 GPU)", 8 * cols * 4, ms, peak))
+    _cpu(out[-1], sample=x[:1, : 1 << 24], gpu=lambda t: backend.reduce("sum", t, 1),
+         cpu=lambda ev, a: ev.reduce("sum", a, 1), kind="sum", axis=1, desc="x[:1, :2^24] (64 MiB)")
     del x
 
 
