@@ -45,6 +45,13 @@ def test_calls_before_init_fail_cleanly():
     assert lib.mtxc_broadcast_binary(0, 0, None, None, None, 1, arr([4]), arr([1]), arr([1]), arr([1])) == \
         _abi.ERR_NOT_INITIALIZED
     assert lib.mtxc_unary(0, 0, None, None, 1, arr([4]), arr([1]), arr([1])) == _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_astype(0, 3, None, None, 1, arr([4]), arr([1]), arr([1])) == _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_reduce_stat(0, 0, None, None, 1, 4, 1, arr([4]), arr([1]), arr([4])) == _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_broadcast_binary_mixed(0, 0, 0, 3, None, None, None, 1, arr([4]), arr([1]), arr([1]),
+                                           arr([1])) == _abi.ERR_NOT_INITIALIZED
+    ptrs = (C.c_void_p * 3)()
+    assert lib.mtxc_pointwise(0, 0, None, ptrs, 2, 1, arr([4]), arr([], 24)) == _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_softmax_lastdim(0, None, None, 1, 4, 4, 4) == _abi.ERR_NOT_INITIALIZED
     assert lib.mtxc_sync() == _abi.ERR_NOT_INITIALIZED
     size = C.c_size_t(123)
     assert lib.mtxc_workspace_size(C.byref(size)) == 0 and size.value == 0
