@@ -20,8 +20,8 @@
 //           256-thread CTA (G = 256) owns a (row, split) unit and streams it with 128-bit
 //           loads (scalar head / tail around the 16-byte aligned body).
 //   cols    reduce_stride != 1 and the innermost output axis is contiguous in the input: a
-//           warp spans 32 x (16 / sizeof(T)) consecutive outputs with one 128-bit load per
-//           lane per reduced row, the CTA's 8 warps interleave the reduced rows, and CTAs
+//           warp spans 32 x V consecutive outputs with one vector load per lane per reduced row
+//           (V x sizeof(T) = 16 bytes, fewer for the narrow types), the CTA's 8 warps interleave the reduced rows, and CTAs
 //           split the reduced axis when there are too few outputs to fill 148 SMs.
 //   generic anything else (non-row-major output strides, short rows, odd layouts): one
 //           thread per output walking its run, exactly like the reference CPU loop.
@@ -32,7 +32,7 @@
 #include <map>
 #include <mutex>
 
-#include "mtxc_internal.cuh"
+#include "elementwise.cuh"
 
 namespace mtxc {
 namespace {
@@ -85,6 +85,17 @@ constexpr int kPairMin = 6;
 constexpr int kStatMean = 7;
 constexpr int kStatRms = 8;
 constexpr int kStatNorm = 9;
+
+// Columns per lane of the column kernel: 16 bytes' worth, except for the (value, index) reductions of
+// the 1- and 2-byte integer types and Bool, where 16 or 8 states per lane cost occupancy: 4 columns
+// per lane, read with 4- or 8-byte loads (B200, int8 ArgMax over a strided axis 0.10 -> 0.21 of the
+// measured copy bandwidth, int16 0.31 -> 0.40; the other cases measured no better with fewer columns).
+template <int OP, typename T>
+constexpr int col_vec() {
+    constexpr bool index_pair = OP == MTXC_REDUCE_ARGMAX || OP == MTXC_REDUCE_ARGMIN || OP == kPairMax || OP == kPairMin;
+    if constexpr (index_pair && sizeof(T) <= 2 && !Traits<T>::kFloat) return 4;
+    else return 16 / (int)sizeof(T);
+}
 
 template <int OP, typename T>
 struct Reducer;
@@ -463,16 +474,17 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
         const uint32_t step = ty_count;
         if constexpr (V > 1) {
             for (; r + (kUnroll - 1) * step < end; r += kUnroll * step) {
-                Vec16<T> x[kUnroll];
+                ew::Slot<T, V> x[kUnroll];
 #pragma unroll
-                for (int k = 0; k < kUnroll; ++k) x[k] = load_stream(p + (size_t)(r + k * step) * a.rstride);
+                for (int k = 0; k < kUnroll; ++k) ew::load_slot(x[k], p + (size_t)(r + k * step) * a.rstride);
 #pragma unroll
                 for (int k = 0; k < kUnroll; ++k)
 #pragma unroll
                     for (int j = 0; j < V; ++j) R::fold(st[j], x[k].v[j], r + k * step);
             }
             for (; r < end; r += step) {
-                Vec16<T> x = load_stream(p + (size_t)r * a.rstride);
+                ew::Slot<T, V> x;
+                ew::load_slot(x, p + (size_t)r * a.rstride);
 #pragma unroll
                 for (int j = 0; j < V; ++j) R::fold(st[j], x.v[j], r);
             }
@@ -664,10 +676,11 @@ ReducePlan plan_reduce(const Meta& m, const void* src, uint32_t rstride, uint32_
     }
     if (rstride != 1 && m.s_in[k] == 1 && m.shape[k] >= 2) {
         p.kind = Plan::kCols;
+        constexpr uint32_t VC = col_vec<OP, T>();
         const uint32_t inner = m.shape[k];
-        bool vec_ok = aligned16(src) && inner % V == 0 && rstride % V == 0;
-        for (uint32_t i = 0; i < k; ++i) vec_ok = vec_ok && (m.shape[i] == 1 || m.s_in[i] % V == 0);
-        p.vec = vec_ok ? (int)V : 1;
+        bool vec_ok = reinterpret_cast<uintptr_t>(src) % (VC * sizeof(T)) == 0 && inner % VC == 0 && rstride % VC == 0;
+        for (uint32_t i = 0; i < k; ++i) vec_ok = vec_ok && (m.shape[i] == 1 || m.s_in[i] % VC == 0);
+        p.vec = vec_ok ? (int)VC : 1;
         const uint32_t threads_across = (inner + p.vec - 1) / p.vec;
         uint32_t tx = 1;
         while (tx < threads_across && tx < 32) tx <<= 1;
@@ -676,7 +689,7 @@ ReducePlan plan_reduce(const Meta& m, const void* src, uint32_t rstride, uint32_
         const uint64_t base = col_tiles * (p.outputs / inner);
         // the split is planned with the vector kernel's occupancy whatever the alignment, so
         // the workspace a call needs does not depend on its pointers
-        const void* fn = (const void*)reduce_cols_kernel<OP, T, V>;
+        const void* fn = (const void*)reduce_cols_kernel<OP, T, VC>;
         const uint64_t block_slots = (uint64_t)sm_count * blocks_per_sm(fn);
         const uint32_t ty_count = kBlock / tx;
         const uint32_t max_split = std::max<uint32_t>(1, len / (ty_count * 8));
@@ -743,7 +756,7 @@ int launch_reduce(const Meta& m, const Out dst, const void* src, uint32_t rstrid
         }
         const uint64_t blocks = (uint64_t)a.col_tiles * a.outer * p.split;
         if (blocks >= (1ull << 31)) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: too many column tiles");
-        if (p.vec > 1) reduce_cols_kernel<OP, T, V><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        if (p.vec > 1) reduce_cols_kernel<OP, T, col_vec<OP, T>()><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         else reduce_cols_kernel<OP, T, 1><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         if (int rc = check_launch("reduce_cols_kernel")) return rc;
     } else {
