@@ -75,3 +75,29 @@ def test_workspace_query_is_host_only():
     assert lib.mtxc_reduce_workspace_bytes(0, 1, 1, 2048, 1, arr([16]), arr([1]), arr([2048]), C.byref(b)) == 0
     assert lib.mtxc_reduce_workspace_bytes(0, 9, 1, 2048, 1, arr([16]), arr([1]), arr([2048]), C.byref(b)) == \
         _abi.ERR_UNSUPPORTED_DTYPE
+
+
+def test_noalloc_scratch_covers_the_planned_reductions():
+    """The split plans stay far inside mtxc_reduce_noalloc's static scratch: no reduction of these large
+    shapes (rows, columns, every op, 1- to 8-byte types, pair states included) asks for more partial bytes
+    than MTXC_NOALLOC_SCRATCH_BYTES, so the allocation-free entry point's refusal is a guard, not a
+    limit callers meet.  (Host-only: the workspace query plans without a device.)"""
+    from matrix_b200 import _abi
+
+    lib, arr = _abi.lib(), _abi.u32_array
+    scratch = 4 << 20
+    worst = 0
+    b = C.c_size_t()
+    for dtype in (0, 1, 2, 3, 7, 8, 10, 11):
+        for op in range(5):
+            # rows: few long rows, many short rows
+            for rows, length in ((1, 1 << 31), (8, 1 << 29), (1000, 1 << 20), (9000, 4096), (1 << 20, 256)):
+                assert lib.mtxc_reduce_workspace_bytes(op, dtype, 1, length, 1, arr([rows]), arr([1]),
+                                                       arr([length]), C.byref(b)) == 0
+                worst = max(worst, b.value)
+            # columns: a strided reduced axis over [outer, length, inner]
+            for outer, length, inner in ((1, 1 << 22, 512), (32, 65536, 512), (1, 1 << 19, 4096), (64, 8192, 1024)):
+                assert lib.mtxc_reduce_workspace_bytes(op, dtype, inner, length, 2, arr([outer, inner]),
+                                                       arr([inner, 1]), arr([length * inner, 1]), C.byref(b)) == 0
+                worst = max(worst, b.value)
+    assert 0 < worst <= scratch, worst
