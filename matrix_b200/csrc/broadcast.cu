@@ -110,19 +110,13 @@ __global__ void __launch_bounds__(kBlock) broadcast_rows_kernel(const RowArgs ar
             }
 #pragma unroll
             for (uint32_t k = 0; k < U; ++k) {
-                Vec16<T> out;
-#pragma unroll
-                for (int j = 0; j < V; ++j) out.v[j] = apply<OP, T>(xa[k].v[j], xb[k].v[j]);
-                store_stream(rr + (uint64_t)(c + k * args.tpr) * V, out);
+                store_stream(rr + (uint64_t)(c + k * args.tpr) * V, apply_vec<OP, T>(xa[k], xb[k]));
             }
         }
         for (; c < c_end; c += args.tpr) {
             const Vec16<T> xa = A_VEC ? load_cached(ra + (uint64_t)c * V) : sa;
             const Vec16<T> xb = B_VEC ? load_cached(rb + (uint64_t)c * V) : sb;
-            Vec16<T> out;
-#pragma unroll
-            for (int j = 0; j < V; ++j) out.v[j] = apply<OP, T>(xa.v[j], xb.v[j]);
-            store_stream(rr + (uint64_t)c * V, out);
+            store_stream(rr + (uint64_t)c * V, apply_vec<OP, T>(xa, xb));
         }
     }
 }
@@ -200,14 +194,9 @@ __global__ void __launch_bounds__(kBlock) broadcast_group_kernel(const GroupArgs
                 for (uint32_t k = 0; k < U; ++k) {
                     const uint64_t e = (uint64_t)(c + k * g.tpr) * V;
 #pragma unroll
-                    for (int t = 0; t < R; ++t) {
-                        Vec16<T> out;
-#pragma unroll
-                        for (int j = 0; j < V; ++j)
-                            out.v[j] = SHARE_A ? apply<OP, T>(xs[k].v[j], xo[k][t].v[j])
-                                               : apply<OP, T>(xo[k][t].v[j], xs[k].v[j]);
-                        store_stream(rr + (uint64_t)t * row_len + e, out);
-                    }
+                    for (int t = 0; t < R; ++t)
+                        store_stream(rr + (uint64_t)t * row_len + e,
+                                     SHARE_A ? apply_vec<OP, T>(xs[k], xo[k][t]) : apply_vec<OP, T>(xo[k][t], xs[k]));
                 }
             }
         }
@@ -218,11 +207,8 @@ __global__ void __launch_bounds__(kBlock) broadcast_group_kernel(const GroupArgs
 #pragma unroll 1
             for (uint32_t t = 0; t < nr; ++t) {
                 const Vec16<T> xo = load_cached(po + (uint64_t)t * g.other_stride + e);
-                Vec16<T> out;
-#pragma unroll
-                for (int j = 0; j < V; ++j)
-                    out.v[j] = SHARE_A ? apply<OP, T>(xs.v[j], xo.v[j]) : apply<OP, T>(xo.v[j], xs.v[j]);
-                store_stream(rr + (uint64_t)t * row_len + e, out);
+                store_stream(rr + (uint64_t)t * row_len + e,
+                             SHARE_A ? apply_vec<OP, T>(xs, xo) : apply_vec<OP, T>(xo, xs));
             }
         }
     }

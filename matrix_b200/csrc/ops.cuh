@@ -50,6 +50,41 @@ __device__ __forceinline__ T apply(T x, T y) {
     }
 }
 
+// apply() over a 16-byte vector of elements.  For the 1-byte types the element-wise ops that need no
+// per-byte carries out of a word run on whole 32-bit words: wrapping Add / Sub of int8 / uint8 with the
+// per-byte SIMD intrinsics, Bool Add / Sub / Mul as "a or b", "a differs from b", "a and b" per byte
+// (C++ bool arithmetic: bool(int(a) + int(b)) ...), each result byte normalised to 0 or 1.  Same results
+// as the element loop, a quarter of the instructions.
+__device__ __forceinline__ uint32_t nonzero_bytes(uint32_t x) {  // 1 in every byte of x that is not 0
+    return ((((x & 0x7f7f7f7fu) + 0x7f7f7f7fu) | x) & 0x80808080u) >> 7;
+}
+
+template <int OP, typename T>
+__device__ __forceinline__ Vec16<T> apply_vec(const Vec16<T>& x, const Vec16<T>& y) {
+    constexpr bool int8_wrap = (std::is_same_v<T, int8_t> || std::is_same_v<T, uint8_t>) &&
+                               (OP == MTXC_BINARY_ADD || OP == MTXC_BINARY_SUB);
+    constexpr bool bool_logic = std::is_same_v<T, mbool> &&
+                                (OP == MTXC_BINARY_ADD || OP == MTXC_BINARY_SUB || OP == MTXC_BINARY_MUL);
+    Vec16<T> out;
+    if constexpr (int8_wrap || bool_logic) {
+        uint32_t a[4], b[4], r[4];
+        memcpy(a, &x, 16);
+        memcpy(b, &y, 16);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            if constexpr (int8_wrap) r[w] = OP == MTXC_BINARY_ADD ? __vadd4(a[w], b[w]) : __vsub4(a[w], b[w]);
+            else if constexpr (OP == MTXC_BINARY_ADD) r[w] = nonzero_bytes(a[w] | b[w]);
+            else if constexpr (OP == MTXC_BINARY_SUB) r[w] = nonzero_bytes(a[w] ^ b[w]);
+            else r[w] = nonzero_bytes(a[w]) & nonzero_bytes(b[w]);
+        }
+        memcpy(&out, r, 16);
+    } else {
+#pragma unroll
+        for (int j = 0; j < Vec16<T>::N; ++j) out.v[j] = apply<OP, T>(x.v[j], y.v[j]);
+    }
+    return out;
+}
+
 // dtype_cast (matrix.h:260-267) on the device: static_cast, through float between the half types.
 //   integer -> integer: the value modulo 2^bits;            integer -> float-like: round to nearest even;
 //   float-like -> float-like: round to nearest even;         anything -> bool: x != 0 (NaN is true);

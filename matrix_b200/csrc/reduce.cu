@@ -118,6 +118,26 @@ struct Reducer<MTXC_REDUCE_SUM, T> {
         else s = (State)(s + o);
     }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
+    // a whole 16-byte vector at once for the 1-byte types: dp4a sums four bytes per instruction (the
+    // wrap-around sum is the same modulo 2^bits), a Bool sum is an or
+    static constexpr bool kVecFold = sizeof(T) == 1;
+    __device__ static void fold_vec(State& s, const Vec16<T>& x) {
+        uint32_t w[4];
+        memcpy(w, &x, 16);
+        if constexpr (Traits<T>::kBool) {
+            s |= (w[0] | w[1] | w[2] | w[3]) != 0u;
+        } else if constexpr (std::is_signed_v<T>) {
+            int acc = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc = __dp4a((int)w[i], 0x01010101, acc);
+            s = (State)(s + (State)acc);
+        } else {
+            unsigned acc = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc = __dp4a(w[i], 0x01010101u, acc);
+            s = (State)(s + (State)acc);
+        }
+    }
     __device__ static void store(const Out& o, uint64_t gid, const State& s) {
         if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = from_float<T>(s);
         else if constexpr (Traits<T>::kBool) static_cast<T*>(o.v)[gid] = mbool(s != 0);
@@ -256,6 +276,7 @@ template <int OP, typename T>
 struct StatReducer : Reducer<MTXC_REDUCE_SUM, T> {
     using Sum = Reducer<MTXC_REDUCE_SUM, T>;
     using State = typename Sum::State;
+    static constexpr bool kVecFold = OP == kStatMean && Sum::kVecFold;  // rms / norm square each element
     __device__ static void fold(State& s, T v, uint32_t i) { Sum::fold(s, OP == kStatMean ? v : square_in_type(v), i); }
     // sum / (float)n in the division's dtype; *as_half tells whether that dtype is Float16
     __device__ static float mean_of(T sum, uint32_t n, bool* as_half) {
@@ -316,6 +337,12 @@ int stat_out_dtype(int op, int dtype, uint32_t n) {
         default: return MTXC_FLOAT;
     }
 }
+
+// Reducers that fold a whole vector at once (kVecFold); the others fold element by element.
+template <class R, class = void>
+struct VecFold : std::false_type {};
+template <class R>
+struct VecFold<R, std::void_t<decltype(R::kVecFold)>> : std::bool_constant<R::kVecFold> {};
 
 template <typename R>
 __device__ __forceinline__ void warp_reduce(typename R::State& s) {
@@ -393,14 +420,23 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
 #pragma unroll
             for (int k = 0; k < kUnroll; ++k) x[k] = load_stream(pv + (size_t)(c + k * G) * V);
 #pragma unroll
-            for (int k = 0; k < kUnroll; ++k)
+            for (int k = 0; k < kUnroll; ++k) {
+                if constexpr (VecFold<R>::value) {
+                    R::fold_vec(st[k % V], x[k]);
+                } else {
 #pragma unroll
-                for (int j = 0; j < V; ++j) R::fold(st[j], x[k].v[j], vbeg + (c + k * G) * V + j);
+                    for (int j = 0; j < V; ++j) R::fold(st[j], x[k].v[j], vbeg + (c + k * G) * V + j);
+                }
+            }
         }
         for (; c < nvec; c += G) {
             Vec16<T> x = load_stream(pv + (size_t)c * V);
+            if constexpr (VecFold<R>::value) {
+                R::fold_vec(st[0], x);
+            } else {
 #pragma unroll
-            for (int j = 0; j < V; ++j) R::fold(st[j], x.v[j], vbeg + c * V + j);
+                for (int j = 0; j < V; ++j) R::fold(st[j], x.v[j], vbeg + c * V + j);
+            }
         }
         for (uint32_t i = vbeg + nvec * V + lane; i < end; i += G) R::fold(st[0], p[i], i);
 
