@@ -746,7 +746,6 @@ int launch_reduce(const Meta& m, const Out dst, const void* src, uint32_t rstrid
     if (p.outputs == 0) return MTXC_OK;
     if (p.partial_bytes > workspace_bytes)
         return fail(MTXC_ERR_WORKSPACE, "mtxc_reduce: workspace too small for the split partials");
-    constexpr int V = Vec16<T>::N;
     const uint32_t k = m.cdims - 1;
     if (p.kind == Plan::kRows) {
         RowArgs a{};
