@@ -7,7 +7,7 @@ import pytest
 
 from tests.helpers import assert_bits_equal
 from tests.test_gpu_pointwise import dev
-from tests.test_oracle_pin_pointwise import STORAGE, values
+from tests.test_oracle_pin_pointwise import values
 
 pytestmark = pytest.mark.gpu
 

@@ -10,7 +10,7 @@ import zlib
 import numpy as np
 import pytest
 
-from tests.helpers import (ALL_DTYPES, INT_DTYPES, assert_bits_equal, assert_sum_close, device_view, make_values,
+from tests.helpers import (INT_DTYPES, assert_bits_equal, assert_sum_close, device_view, make_values,
                            strided_view, to_device)
 
 pytestmark = pytest.mark.gpu

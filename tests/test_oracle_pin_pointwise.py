@@ -9,7 +9,6 @@ import ctypes as C
 import numpy as np
 import pytest
 
-from tests.helpers import strided_view
 
 NUMPY_TYPES = [np.float32, np.float16, np.uint8, np.int32, np.int16, np.uint32, np.uint16, np.bool_, np.int8,
                np.int64, np.uint64]
