@@ -2,14 +2,14 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--suite]
 
-Metric (BASELINE.json): reduce/broadcast GB/s (algorithmic HBM bytes per second, whole job)
+Metric: reduce/broadcast GB/s (algorithmic HBM bytes per second, whole job)
 and its fraction of the B200 HBM roofline, against the reference's CPU path.
 
-Workload (one "step"): BASELINE config 2, the broadcasted Add and Mul of float32
+Workload (one "step"): benchmark config 2, the broadcasted Add and Mul of float32
 a[256,1,4096] ~ U(-1,1) with b[1,512,4096] ~ U(-1,1) into [256,512,4096] (2 GiB each),
 evaluated through the C ABI (mtxc_broadcast_binary) with the metadata the reference's
 operator+ / operator* build.  Algorithmic bytes per op: out 2^31 + a 2^22 + b 2^23 =
-2,160,066,560.  Inputs are synthetic (seeded), as BASELINE names no dataset.
+2,160,066,560.  Inputs are synthetic (seeded), as no dataset is named for this benchmark.
 
 Multi-GPU (torchrun, one rank per GPU): weak scaling.  The global a is [256*N, 1, 4096],
 sharded along its leading axis; each rank evaluates its shard against a replicated b.  The
@@ -20,7 +20,7 @@ maximum over ranks is reported.
 lambdas of Matrix.mm:7475-7567, compiled from the reference tree into
 oracle/_ref/libmtx_ref.so), one slice of output rows per host thread, on a bounded sample.
 
-`--suite` additionally prints one line per other BASELINE config (C1, C3, C4, C5a, C5b);
+`--suite` additionally prints one line per other benchmark config (C1, C3, C4, C5a, C5b);
 those lines are diagnostics, not the headline.
 """
 from __future__ import annotations
@@ -505,7 +505,7 @@ def sustained_copy_gbs(dev, stream, ms_target: float) -> float:
 # sharded reductions (configs 4 and 5b): the reduced axis is the sharded one
 # ------------------------------------------------------------------------------------------
 def run_sharded(args):
-    """A BASELINE config sharded over the GPUs on its leading axis (strong scaling: the total is fixed).
+    """A benchmark config sharded over the GPUs on its leading axis (strong scaling: the total is fixed).
     C5b: full Sum of f32 2^32 elements (as [8, 2^29], 16 GiB); C4: Sum over axes (0, 2) of f32
     [32, 4096, 2048]; for both the sharded axis is a reduced one, so a step is the local kernels, the NCCL
     all-gather of the per-rank partials and the ordered merge.  C1 (Sum of the last axis), C3 (Max and
@@ -680,7 +680,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--suite", action="store_true", help="also time the other BASELINE configs")
+    ap.add_argument("--suite", action="store_true", help="also time the other benchmark configs")
     ap.add_argument("--suite-configs", default="", help="comma-separated subset of C1,C3,C4,C5a,C5b,F2,F3,F4,F5,F6")
     ap.add_argument("--suite-scale", type=int, default=1, help="divide the configs' leading extent (small cases)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")

@@ -349,7 +349,7 @@ int mtxc_pointwise(int op, int dtype, void* dst, const void* const* inputs, uint
 
 /* Fused evaluation of the reference's softmax trace over the last axis of contiguous float rows
  *     m = x.max(-1, true); e = matrix::exp(x - m); y = e / e.sum(-1, true)
- * (MaxReduction, Subtraction, Exp, Sum and Division primitives; BASELINE config 5a): x is read once
+ * (MaxReduction, Subtraction, Exp, Sum and Division primitives; benchmark config 5a): x is read once
  * and y written once.  Element-wise the trace's arithmetic (same max, x - m, expf) except for the order
  * of the fp32 additions in the row sum and y = e * (1 / s), one correctly rounded reciprocal per row,
  * within 1 ulp of the trace's e / s.  Rows start row_stride elements apart;

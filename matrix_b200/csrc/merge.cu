@@ -1,5 +1,5 @@
 // Ordered merge of per-shard partial reductions: the cross-GPU step of a reduction whose reduced
-// axis is sharded across GPUs (BASELINE configs 4 and 5b).
+// axis is sharded across GPUs (benchmark configs 4 and 5b).
 //
 // Each of `parts` shards reduced its contiguous slice of the axis; their partial results arrive
 // part-major (part p's `outputs` results at p * outputs, in shard order, e.g. from an NCCL

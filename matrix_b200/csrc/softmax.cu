@@ -1,7 +1,7 @@
 // Fused row softmax for sm_100a: the reference's compiled trace
 //     m = x.max(-1, true); e = matrix::exp(x - m); y = e / e.sum(-1, true)
 // (MaxReductionPrimitive, SubtractionPrimitive, ExpPrimitive, SumPrimitive, DivisionPrimitive;
-// BASELINE config 5a) evaluated in one kernel that reads x once and writes y once, instead of the
+// benchmark config 5a) evaluated in one kernel that reads x once and writes y once, instead of the
 // five kernels and ~4 passes over the data the trace takes one primitive at a time.
 //
 // Each row is held by one thread-block cluster: C CTAs of 256 threads, each thread keeping 4 * VPT

@@ -1,4 +1,4 @@
-"""Device-time measurements of the other BASELINE configs (bench.py --suite).
+"""Device-time measurements of the other benchmark configurations (bench.py --suite).
 
 Each config is run through the same C-ABI calls a user makes (matrix_b200.backend), with
 seeded synthetic inputs generated on the device, 3 warm-up repetitions and the median of 20
@@ -29,7 +29,7 @@ def _peak() -> float:
         return 6650.0
 
 
-SPEC_GBS = 8000.0  # B200 HBM3e nominal peak (BASELINE north_star: ~8 TB/s)
+SPEC_GBS = 8000.0  # B200 HBM3e nominal peak (~8 TB/s)
 
 
 def _time(fn, stream, reps=20, warmup=3, flush=None):

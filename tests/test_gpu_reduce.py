@@ -196,7 +196,7 @@ def test_unsupported_dtype_is_an_error(gpu):
 
 
 # ------------------------------------------------------------------------------------------
-# BASELINE configs at full size (C1, C3, C4) and C5b at reduced size
+# The benchmark configs at full size (C1, C3, C4) and C5b at reduced size
 # ------------------------------------------------------------------------------------------
 @pytest.mark.slow
 def test_config1_sum_last_axis(gpu, port):
