@@ -183,6 +183,25 @@ struct ValueExtremum {
     __device__ static void fold(State& s, T v, uint32_t) {
         if (kMax ? less(s, v) : less(v, s)) s = v;
     }
+    // 1- and 2-byte integers and Bool (its bytes compare unsigned) fold a 16-byte vector word-wise:
+    // the per-byte / per-half SIMD max / min of the four words, then of the lanes within the word
+    static constexpr bool kVecFold = sizeof(T) <= 2;
+    __device__ static uint32_t ext2(uint32_t a, uint32_t b) {
+        if constexpr (sizeof(T) == 1 && std::is_signed_v<T>) return kMax ? __vmaxs4(a, b) : __vmins4(a, b);
+        else if constexpr (sizeof(T) == 1) return kMax ? __vmaxu4(a, b) : __vminu4(a, b);
+        else if constexpr (std::is_signed_v<T>) return kMax ? __vmaxs2(a, b) : __vmins2(a, b);
+        else return kMax ? __vmaxu2(a, b) : __vminu2(a, b);
+    }
+    __device__ static void fold_vec(State& s, const Vec16<T>& x) {
+        uint32_t w[4];
+        memcpy(w, &x, 16);
+        uint32_t m = ext2(ext2(w[0], w[1]), ext2(w[2], w[3]));
+        m = ext2(m, m >> 16);                               // low lane: the extreme of lanes (0, 2) and (1, 3)
+        if constexpr (sizeof(T) == 1) m = ext2(m, m >> 8);  // low byte: the extreme of all four
+        T v;
+        memcpy(&v, &m, sizeof(T));
+        fold(s, v, 0);
+    }
     __device__ static void merge(State& s, const State& o) { fold(s, o, 0); }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
     __device__ static void store(const Out& o, uint64_t gid, const State& s) { static_cast<T*>(o.v)[gid] = s; }
