@@ -100,6 +100,11 @@ constexpr int col_vec() {
 template <int OP, typename T>
 struct Reducer;
 
+// packed lanes of a vector-folding reducer: one 16-byte vector's worth of partial results
+struct Lanes {
+    uint32_t w[4];
+};
+
 // Sum: float-likes accumulate in fp32 (rounded to T once, at the end); integers in the unsigned
 // type of the accumulator width (wrap-around, as the reference's T accumulator); Bool as C++ bool
 // does, where `acc += x` is a logical or.
@@ -118,25 +123,24 @@ struct Reducer<MTXC_REDUCE_SUM, T> {
         else s = (State)(s + o);
     }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
-    // a whole 16-byte vector at once for the 1-byte types: dp4a sums four bytes per instruction (the
-    // wrap-around sum is the same modulo 2^bits), a Bool sum is an or
+    // The 1-byte types fold whole 16-byte vectors into a packed state of four words, reduced into a
+    // State once per segment: dp4a adds four bytes per instruction into each word (the wrap-around
+    // sum is the same modulo 2^bits), a Bool sum is an or of the words.
     static constexpr bool kVecFold = sizeof(T) == 1;
-    __device__ static void fold_vec(State& s, const Vec16<T>& x) {
+    __device__ static Lanes vec_init() { return Lanes{}; }
+    __device__ static void vec_fold(Lanes& p, const Vec16<T>& x) {
         uint32_t w[4];
         memcpy(w, &x, 16);
-        if constexpr (Traits<T>::kBool) {
-            s |= (w[0] | w[1] | w[2] | w[3]) != 0u;
-        } else if constexpr (std::is_signed_v<T>) {
-            int acc = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc = __dp4a((int)w[i], 0x01010101, acc);
-            s = (State)(s + (State)acc);
-        } else {
-            unsigned acc = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc = __dp4a(w[i], 0x01010101u, acc);
-            s = (State)(s + (State)acc);
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (Traits<T>::kBool) p.w[i] |= w[i];
+            else if constexpr (std::is_signed_v<T>) p.w[i] = (uint32_t)__dp4a((int)w[i], 0x01010101, (int)p.w[i]);
+            else p.w[i] = __dp4a(w[i], 0x01010101u, p.w[i]);
         }
+    }
+    __device__ static void vec_finish(State& s, const Lanes& p) {
+        if constexpr (Traits<T>::kBool) s |= (p.w[0] | p.w[1] | p.w[2] | p.w[3]) != 0u;
+        else s = (State)(s + (State)(p.w[0] + p.w[1] + p.w[2] + p.w[3]));
     }
     __device__ static void store(const Out& o, uint64_t gid, const State& s) {
         if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = from_float<T>(s);
@@ -183,8 +187,9 @@ struct ValueExtremum {
     __device__ static void fold(State& s, T v, uint32_t) {
         if (kMax ? less(s, v) : less(v, s)) s = v;
     }
-    // 1- and 2-byte integers and Bool (its bytes compare unsigned) fold a 16-byte vector word-wise:
-    // the per-byte / per-half SIMD max / min of the four words, then of the lanes within the word
+    // 1- and 2-byte integers and Bool (its bytes compare unsigned) fold 16-byte vectors into a packed
+    // state of four words with the per-byte / per-half SIMD max / min, whose lanes are reduced into a
+    // State once per segment
     static constexpr bool kVecFold = sizeof(T) <= 2;
     __device__ static uint32_t ext2(uint32_t a, uint32_t b) {
         if constexpr (sizeof(T) == 1 && std::is_signed_v<T>) return kMax ? __vmaxs4(a, b) : __vmins4(a, b);
@@ -192,15 +197,26 @@ struct ValueExtremum {
         else if constexpr (std::is_signed_v<T>) return kMax ? __vmaxs2(a, b) : __vmins2(a, b);
         else return kMax ? __vmaxu2(a, b) : __vminu2(a, b);
     }
-    __device__ static void fold_vec(State& s, const Vec16<T>& x) {
+    __device__ static Lanes vec_init() {
+        Vec16<T> x;
+#pragma unroll
+        for (int j = 0; j < Vec16<T>::N; ++j) x.v[j] = init();
+        Lanes p;
+        memcpy(&p, &x, 16);
+        return p;
+    }
+    __device__ static void vec_fold(Lanes& p, const Vec16<T>& x) {
         uint32_t w[4];
         memcpy(w, &x, 16);
-        uint32_t m = ext2(ext2(w[0], w[1]), ext2(w[2], w[3]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p.w[i] = ext2(p.w[i], w[i]);
+    }
+    __device__ static void vec_finish(State& s, const Lanes& p) {
+        uint32_t m = ext2(ext2(p.w[0], p.w[1]), ext2(p.w[2], p.w[3]));
         m = ext2(m, m >> 16);                               // low lane: the extreme of lanes (0, 2) and (1, 3)
         if constexpr (sizeof(T) == 1) m = ext2(m, m >> 8);  // low byte: the extreme of all four
-        T v;
-        memcpy(&v, &m, sizeof(T));
-        fold(s, v, 0);
+        if constexpr (sizeof(T) == 1) fold(s, (T)(uint8_t)m, 0);
+        else fold(s, (T)(uint16_t)m, 0);
     }
     __device__ static void merge(State& s, const State& o) { fold(s, o, 0); }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
@@ -434,6 +450,8 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
         const uint32_t nvec = (end - vbeg) / V;
         const T* pv = p + vbeg;
         uint32_t c = lane;
+        [[maybe_unused]] Lanes pk;
+        if constexpr (VecFold<R>::value) pk = R::vec_init();
         for (; c + (kUnroll - 1) * G < nvec; c += kUnroll * G) {
             Vec16<T> x[kUnroll];
 #pragma unroll
@@ -441,7 +459,7 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
 #pragma unroll
             for (int k = 0; k < kUnroll; ++k) {
                 if constexpr (VecFold<R>::value) {
-                    R::fold_vec(st[k % V], x[k]);
+                    R::vec_fold(pk, x[k]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < V; ++j) R::fold(st[j], x[k].v[j], vbeg + (c + k * G) * V + j);
@@ -451,12 +469,13 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
         for (; c < nvec; c += G) {
             Vec16<T> x = load_stream(pv + (size_t)c * V);
             if constexpr (VecFold<R>::value) {
-                R::fold_vec(st[0], x);
+                R::vec_fold(pk, x);
             } else {
 #pragma unroll
                 for (int j = 0; j < V; ++j) R::fold(st[j], x.v[j], vbeg + c * V + j);
             }
         }
+        if constexpr (VecFold<R>::value) R::vec_finish(st[0], pk);
         for (uint32_t i = vbeg + nvec * V + lane; i < end; i += G) R::fold(st[0], p[i], i);
 
 #pragma unroll
