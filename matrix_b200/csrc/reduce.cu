@@ -32,6 +32,8 @@
 #include <map>
 #include <mutex>
 
+#include <atomic>
+
 #include "elementwise.cuh"
 
 namespace mtxc {
@@ -86,15 +88,15 @@ constexpr int kStatMean = 7;
 constexpr int kStatRms = 8;
 constexpr int kStatNorm = 9;
 
-// Columns per lane of the column kernel: 16 bytes' worth, except for the (value, index) reductions of
-// the 1- and 2-byte integer types and Bool, where 16 or 8 states per lane cost occupancy: 4 columns
-// per lane, read with 4- or 8-byte loads (B200, int8 ArgMax over a strided axis 0.10 -> 0.21 of the
-// measured copy bandwidth, int16 0.31 -> 0.40; the other cases measured no better with fewer columns).
+// Columns per lane of the column kernel: 16 bytes' worth, read with one 16-byte load per reduced row;
+// when the operand is not 16-byte aligned, the 1- and 2-byte types fall back to 4-byte lanes.
 template <int OP, typename T>
 constexpr int col_vec() {
-    constexpr bool index_pair = OP == MTXC_REDUCE_ARGMAX || OP == MTXC_REDUCE_ARGMIN || OP == kPairMax || OP == kPairMin;
-    if constexpr (index_pair && sizeof(T) <= 2 && !Traits<T>::kFloat) return 4;
-    else return 16 / (int)sizeof(T);
+    return 16 / (int)sizeof(T);
+}
+template <typename T>
+constexpr int col_vec_narrow() {
+    return sizeof(T) <= 2 ? 4 / (int)sizeof(T) : 1;
 }
 
 template <int OP, typename T>
@@ -177,6 +179,98 @@ struct PairExtremum {
         if (beats(o.v, s.v) || (equal(o.v, s.v) && o.i < s.i)) s = o;
     }
     __device__ static State shfl(const State& s, int m) { return State{shfl_xor(s.v, m), shfl_xor(s.i, m)}; }
+
+    // Column kernel, 1- and 2-byte integers and Bool (bytes compare unsigned): the lane's 16 bytes of
+    // columns keep their best values packed in four words; per reduced row, one SIMD compare per word
+    // gives the lanes the row beats (strictly, so the first row of a tie is kept), one SIMD max / min
+    // updates the values, and the row's number within the current chunk of rows (1-based, 16 bits) is
+    // merged into the packed 16-bit "row of the best" lanes where the row won (a row that wins no lane
+    // skips both).  A chunk ends after 65,535 rows or at the end of the lane's rows: lanes that won in
+    // it turn their chunk number back into a row index.  No branch per element; every index stays
+    // exact whatever the length.
+    static constexpr bool kColSimd = !Traits<T>::kFloat && sizeof(T) <= 2;
+    static constexpr int kLanes = 16 / (int)sizeof(T);
+    struct ColState {
+        Lanes best;
+        uint32_t won[kLanes / 2];  // 16-bit lanes: chunk row number of the lane's best, 0 = none yet
+        int32_t idx[kLanes];       // row index of the best as of the last finished chunk
+        uint32_t n;                // rows of the current chunk so far
+        uint32_t row;              // last row folded
+        uint32_t step;             // distance between the lane's consecutive rows
+        uint32_t limit;            // rows per chunk (at most 65,535)
+    };
+    __device__ static uint32_t simd_beats(uint32_t x, uint32_t b) {  // all ones in the lanes where x beats b
+        if constexpr (sizeof(T) == 1 && std::is_signed_v<T>) return kMax ? __vcmpgts4(x, b) : __vcmplts4(x, b);
+        else if constexpr (sizeof(T) == 1) return kMax ? __vcmpgtu4(x, b) : __vcmpltu4(x, b);
+        else if constexpr (std::is_signed_v<T>) return kMax ? __vcmpgts2(x, b) : __vcmplts2(x, b);
+        else return kMax ? __vcmpgtu2(x, b) : __vcmpltu2(x, b);
+    }
+    __device__ static uint32_t simd_ext(uint32_t x, uint32_t b) {
+        if constexpr (sizeof(T) == 1 && std::is_signed_v<T>) return kMax ? __vmaxs4(x, b) : __vmins4(x, b);
+        else if constexpr (sizeof(T) == 1) return kMax ? __vmaxu4(x, b) : __vminu4(x, b);
+        else if constexpr (std::is_signed_v<T>) return kMax ? __vmaxs2(x, b) : __vmins2(x, b);
+        else return kMax ? __vmaxu2(x, b) : __vminu2(x, b);
+    }
+    __device__ static ColState col_init(uint32_t step, uint32_t limit) {
+        ColState c;
+        Vec16<T> v;
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) {
+            v.v[j] = kMax ? lowest_value<T>() : highest_value<T>();
+            c.idx[j] = 0;
+        }
+        memcpy(&c.best, &v, 16);
+#pragma unroll
+        for (int i = 0; i < kLanes / 2; ++i) c.won[i] = 0;
+        c.n = 0;
+        c.row = 0;
+        c.step = step;
+        c.limit = limit;
+        return c;
+    }
+    // lanes that won in the current chunk take the row index of their last win; the chunk restarts
+    __device__ static void col_flush(ColState& c) {
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) {
+            const uint32_t t = (c.won[j / 2] >> (16 * (j % 2))) & 0xffffu;
+            if (t != 0) c.idx[j] = (int32_t)(c.row - (c.n - t) * c.step);
+        }
+#pragma unroll
+        for (int i = 0; i < kLanes / 2; ++i) c.won[i] = 0;
+        c.n = 0;
+    }
+    __device__ static void col_fold(ColState& c, const uint32_t (&w)[4], uint32_t row) {
+        c.n += 1;
+        c.row = row;
+        const uint32_t t2 = c.n * 0x00010001u;  // the chunk row number in both 16-bit halves
+        uint32_t m[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m[i] = simd_beats(w[i], c.best.w[i]);
+        // a row that beats no lane changes nothing (the common case once the columns' extremes are
+        // found, e.g. Bool after its first true)
+        if ((m[0] | m[1] | m[2] | m[3]) != 0u) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                c.best.w[i] = simd_ext(w[i], c.best.w[i]);
+                if constexpr (sizeof(T) == 1) {
+                    // byte lanes (4i .. 4i+3) -> the 16-bit lanes of won[2i] and won[2i + 1]
+                    const uint32_t lo = __byte_perm(m[i], 0, 0x1100), hi = __byte_perm(m[i], 0, 0x3322);
+                    c.won[2 * i] = (c.won[2 * i] & ~lo) | (t2 & lo);
+                    c.won[2 * i + 1] = (c.won[2 * i + 1] & ~hi) | (t2 & hi);
+                } else {
+                    c.won[i] = (c.won[i] & ~m[i]) | (t2 & m[i]);
+                }
+            }
+        }
+        if (c.n == c.limit) col_flush(c);
+    }
+    __device__ static void col_finish(ColState& c, State (&st)[kLanes]) {
+        col_flush(c);
+        Vec16<T> v;
+        memcpy(&v, &c.best, 16);
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) st[j] = State{v.v[j], c.idx[j]};
+    }
 };
 
 // Integer and Bool Max / Min: equal values are indistinguishable, so no index is needed.
@@ -217,6 +311,20 @@ struct ValueExtremum {
         if constexpr (sizeof(T) == 1) m = ext2(m, m >> 8);  // low byte: the extreme of all four
         if constexpr (sizeof(T) == 1) fold(s, (T)(uint8_t)m, 0);
         else fold(s, (T)(uint16_t)m, 0);
+    }
+    // column kernel: the 16 columns of a lane fold as one packed vector
+    static constexpr bool kColSimd = kVecFold;
+    using ColState = Lanes;
+    __device__ static Lanes col_init(uint32_t, uint32_t) { return vec_init(); }
+    __device__ static void col_fold(Lanes& p, const uint32_t (&w)[4], uint32_t) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p.w[i] = ext2(p.w[i], w[i]);
+    }
+    __device__ static void col_finish(Lanes& p, State (&st)[Vec16<T>::N]) {
+        Vec16<T> v;
+        memcpy(&v, &p, 16);
+#pragma unroll
+        for (int j = 0; j < Vec16<T>::N; ++j) st[j] = v.v[j];
     }
     __device__ static void merge(State& s, const State& o) { fold(s, o, 0); }
     __device__ static State shfl(const State& s, int m) { return shfl_xor(s, m); }
@@ -378,6 +486,11 @@ template <class R, class = void>
 struct VecFold : std::false_type {};
 template <class R>
 struct VecFold<R, std::void_t<decltype(R::kVecFold)>> : std::bool_constant<R::kVecFold> {};
+// Reducers whose column kernel folds a lane's 16 bytes of columns as packed words (kColSimd).
+template <class R, class = void>
+struct ColSimd : std::false_type {};
+template <class R>
+struct ColSimd<R, std::void_t<decltype(R::kColSimd)>> : std::bool_constant<R::kColSimd> {};
 
 template <typename R>
 __device__ __forceinline__ void warp_reduce(typename R::State& s) {
@@ -516,8 +629,14 @@ struct ColArgs {
     uint32_t col_tiles;   // CTAs across `inner`
     uint32_t tx;          // threads across columns (power of two, <= 32)
     uint64_t outputs;     // M = outer * inner
+    uint32_t chunk;       // rows per chunk of the packed (value, index) column fold
     Dims d;               // outer axes: shape (fast divisors) and input strides in s1
 };
+
+// Rows per chunk of the packed column fold: 65,535 (the 16-bit row numbers' range).  A lower value
+// changes no result, only how often the chunk numbers turn into row indices; it is settable so tests can
+// reach that step at small sizes (mtxc_debug_set_col_chunk, not part of the public header).
+std::atomic<uint32_t> g_col_chunk{65535};
 
 template <int OP, typename T, int V>
 __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
@@ -546,7 +665,28 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
         const uint32_t end = min(a.len, begin + a.seg);
         uint32_t r = begin + ty;
         const uint32_t step = ty_count;
-        if constexpr (V > 1) {
+        if constexpr (ColSimd<R>::value && V * sizeof(T) == 16) {
+            typename R::ColState cs = R::col_init(step, a.chunk);
+            for (; r + (kUnroll - 1) * step < end; r += kUnroll * step) {
+                ew::Slot<T, V> x[kUnroll];
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) ew::load_slot(x[k], p + (size_t)(r + k * step) * a.rstride);
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) {
+                    uint32_t w[4];
+                    memcpy(w, &x[k], 16);
+                    R::col_fold(cs, w, r + k * step);
+                }
+            }
+            for (; r < end; r += step) {
+                ew::Slot<T, V> x;
+                ew::load_slot(x, p + (size_t)r * a.rstride);
+                uint32_t w[4];
+                memcpy(w, &x, 16);
+                R::col_fold(cs, w, r);
+            }
+            R::col_finish(cs, st);
+        } else if constexpr (V > 1) {
             for (; r + (kUnroll - 1) * step < end; r += kUnroll * step) {
                 ew::Slot<T, V> x[kUnroll];
 #pragma unroll
@@ -751,10 +891,14 @@ ReducePlan plan_reduce(const Meta& m, const void* src, uint32_t rstride, uint32_
     if (rstride != 1 && m.s_in[k] == 1 && m.shape[k] >= 2) {
         p.kind = Plan::kCols;
         constexpr uint32_t VC = col_vec<OP, T>();
+        constexpr uint32_t VN = col_vec_narrow<T>();
         const uint32_t inner = m.shape[k];
-        bool vec_ok = reinterpret_cast<uintptr_t>(src) % (VC * sizeof(T)) == 0 && inner % VC == 0 && rstride % VC == 0;
-        for (uint32_t i = 0; i < k; ++i) vec_ok = vec_ok && (m.shape[i] == 1 || m.s_in[i] % VC == 0);
-        p.vec = vec_ok ? (int)VC : 1;
+        auto vec_ok = [&](uint32_t vc) {
+            bool ok = reinterpret_cast<uintptr_t>(src) % (vc * sizeof(T)) == 0 && inner % vc == 0 && rstride % vc == 0;
+            for (uint32_t i = 0; i < k; ++i) ok = ok && (m.shape[i] == 1 || m.s_in[i] % vc == 0);
+            return ok;
+        };
+        p.vec = vec_ok(VC) ? (int)VC : VN > 1 && vec_ok(VN) ? (int)VN : 1;
         const uint32_t threads_across = (inner + p.vec - 1) / p.vec;
         uint32_t tx = 1;
         while (tx < threads_across && tx < 32) tx <<= 1;
@@ -821,6 +965,7 @@ int launch_reduce(const Meta& m, const Out dst, const void* src, uint32_t rstrid
         a.tx = p.tx;
         a.col_tiles = (((a.inner + p.vec - 1) / p.vec) + p.tx - 1) / p.tx;
         a.outputs = p.outputs;
+        a.chunk = g_col_chunk.load(std::memory_order_relaxed);
         a.d.n = k;
         for (uint32_t i = 0; i < k; ++i) {
             a.d.shape[i] = m.shape[i];
@@ -829,7 +974,9 @@ int launch_reduce(const Meta& m, const Out dst, const void* src, uint32_t rstrid
         }
         const uint64_t blocks = (uint64_t)a.col_tiles * a.outer * p.split;
         if (blocks >= (1ull << 31)) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_reduce: too many column tiles");
-        if (p.vec > 1) reduce_cols_kernel<OP, T, col_vec<OP, T>()><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        constexpr int VN = col_vec_narrow<T>();
+        if (p.vec == col_vec<OP, T>()) reduce_cols_kernel<OP, T, col_vec<OP, T>()><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
+        else if (VN > 1 && p.vec == VN) reduce_cols_kernel<OP, T, VN><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         else reduce_cols_kernel<OP, T, 1><<<(unsigned)blocks, kBlock, 0, stream>>>(a);
         if (int rc = check_launch("reduce_cols_kernel")) return rc;
     } else {
@@ -1095,4 +1242,10 @@ extern "C" int mtxc_reduce_pair(int op, int dtype, void* dst_values, int32_t* ds
     if (!known)
         return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_reduce_pair: no kernel for dtype ") + dtype_name(dtype));
     return rc;
+}
+
+// Test hook: rows per chunk of the packed column fold (clamped to 1 .. 65,535); returns the previous value.
+extern "C" uint32_t mtxc_debug_set_col_chunk(uint32_t rows) {
+    const uint32_t v = rows < 1 ? 1 : rows > 65535 ? 65535 : rows;
+    return mtxc::g_col_chunk.exchange(v);
 }

@@ -101,3 +101,16 @@ def test_noalloc_scratch_covers_the_planned_reductions():
                                                        arr([inner, 1]), arr([length * inner, 1]), C.byref(b)) == 0
                 worst = max(worst, b.value)
     assert 0 < worst <= scratch, worst
+
+
+def test_column_chunk_hook_clamps():
+    """mtxc_debug_set_col_chunk (a test hook outside the public header) sets the rows per chunk of the
+    packed column (value, index) fold within 1 .. 65,535 and returns the previous value."""
+    from matrix_b200 import _abi
+
+    fn = _abi.lib().mtxc_debug_set_col_chunk
+    fn.argtypes, fn.restype = [C.c_uint32], C.c_uint32
+    assert fn(7) == 65535
+    assert fn(0) == 7
+    assert fn(1 << 20) == 1
+    assert fn(65535) == 65535

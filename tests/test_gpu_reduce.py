@@ -69,6 +69,75 @@ def test_reduce_int_dtypes(gpu, port, dtype, op):
             check_reduce(gpu, port, op, base, shape, strides, 0, axis, False)
 
 
+NARROW = [np.int8, np.uint8, np.int16, np.uint16, np.bool_]
+
+
+def narrow_pattern(rng, kind, shape, axis, dtype):
+    """Values along `axis` of `shape` that steer the packed column extremum through each branch:
+    random over the full range, heavy ties (four distinct values), rising or falling along the
+    reduced axis (a new best every row), constant, and all at the type's lowest or highest value
+    (no row ever beats the initial state)."""
+    dt = np.dtype(dtype)
+    lo, hi = (0, 1) if dt == np.bool_ else (np.iinfo(dt).min, np.iinfo(dt).max)
+    n = int(np.prod(shape))
+    if kind == "random":
+        v = rng.integers(lo, hi + 1, n, dtype=np.int64)
+    elif kind == "ties":
+        v = rng.integers(lo, lo + 4 if dt != np.bool_ else 2, n, dtype=np.int64)
+    elif kind in ("rising", "falling"):
+        pos = np.indices(shape)[axis].reshape(-1).astype(np.int64)
+        span = hi - lo
+        step = pos * span // max(shape[axis] - 1, 1)
+        v = lo + step if kind == "rising" else hi - step
+    elif kind == "constant":
+        v = np.full(n, lo + (hi - lo) // 3, dtype=np.int64)
+    else:  # "low" / "high"
+        v = np.full(n, lo if kind == "low" else hi, dtype=np.int64)
+    return v.astype(dt)
+
+
+@pytest.mark.parametrize("dtype", NARROW, ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("op", ["max", "min", "argmax", "argmin"])
+def test_reduce_narrow_columns(gpu, port, dtype, op):
+    """Max / Min / ArgMax / ArgMin over a strided axis of the 1- and 2-byte types: the 16-byte packed
+    lanes (inner extent a multiple of 16 bytes), the 4-byte fallback lanes (a multiple of 4 bytes, or an
+    operand offset that breaks 16-byte alignment), and the split path (long reduced axis), each with the
+    value patterns that take the packed compare's rare update on every row or on none.  Bit-exact,
+    first index of a tie."""
+    rng = np.random.default_rng(zlib.crc32(f"narrow{op}{np.dtype(dtype).name}".encode()))
+    code = 7 if dtype == np.bool_ else None
+    cases = [([300, 64], 0, 0), ([3, 257, 48], 1, 0), ([1000, 20], 0, 0), ([700, 96], 0, 4), ([20000, 32], 0, 0)]
+    set_chunk = _col_chunk_setter()
+    # the default chunk (65,535 rows: one chunk per lane at these sizes), then chunks of 1, 3 and 7 rows,
+    # which turn the 16-bit chunk row numbers into indices at every row or in the middle of the lane's rows
+    for chunk in (65535, 1, 3, 7):
+        set_chunk(chunk)
+        try:
+            for shape, axis, off in (cases if chunk == 65535 else cases[:2]):
+                strides = [int(np.prod(shape[i + 1:])) for i in range(len(shape))]
+                for kind in ("random", "ties", "rising", "falling", "constant", "low", "high"):
+                    v = narrow_pattern(rng, kind, shape, axis, dtype)
+                    base = np.concatenate([np.zeros(off, dtype=v.dtype), v])
+                    x = strided_view(base, shape, strides, off)
+                    cpu = port.reduce(op, x, axis, False, dtype_code=code) if code else port.reduce(op, x, axis, False)
+                    out = gpu.reduce(op, device_view(to_device(base), shape, strides, off), axis)
+                    gpu.sync()
+                    assert_bits_equal(out.cpu().numpy(), cpu,
+                                      f"{np.dtype(dtype).name} {op} {shape} axis {axis} +{off} {kind} chunk {chunk}")
+        finally:
+            set_chunk(65535)
+
+
+def _col_chunk_setter():
+    import ctypes
+
+    from matrix_b200 import _abi
+
+    fn = _abi.lib().mtxc_debug_set_col_chunk
+    fn.argtypes, fn.restype = [ctypes.c_uint32], ctypes.c_uint32
+    return fn
+
+
 @pytest.mark.parametrize("op", OPS)
 def test_reduce_float_specials(gpu, port, op):
     """NaN never wins, the first of equal extremes (incl. -0.0 / +0.0) is kept, rows of only
