@@ -180,15 +180,16 @@ struct PairExtremum {
     }
     __device__ static State shfl(const State& s, int m) { return State{shfl_xor(s.v, m), shfl_xor(s.i, m)}; }
 
-    // Column kernel, 1- and 2-byte integers and Bool (bytes compare unsigned): the lane's 16 bytes of
-    // columns keep their best values packed in four words; per reduced row, one SIMD compare per word
-    // gives the lanes the row beats (strictly, so the first row of a tie is kept), one SIMD max / min
-    // updates the values, and the row's number within the current chunk of rows (1-based, 16 bits) is
-    // merged into the packed 16-bit "row of the best" lanes where the row won (a row that wins no lane
+    // Column kernel, 1- and 2-byte types (integers, Bool whose bytes compare unsigned, and the half
+    // types, compared as the floats they widen to): the lane's 16 bytes of columns keep their best
+    // values packed in four words; per reduced row, one SIMD compare per word gives the lanes the row
+    // beats (strictly, so the first row of a tie is kept; NaN never beats), the row's bits replace the
+    // best in exactly those lanes, and the row's number within the current chunk of rows (1-based, 16
+    // bits) is merged into the packed 16-bit "row of the best" lanes there (a row that beats no lane
     // skips both).  A chunk ends after 65,535 rows or at the end of the lane's rows: lanes that won in
     // it turn their chunk number back into a row index.  No branch per element; every index stays
     // exact whatever the length.
-    static constexpr bool kColSimd = !Traits<T>::kFloat && sizeof(T) <= 2;
+    static constexpr bool kColSimd = sizeof(T) <= 2;
     static constexpr int kLanes = 16 / (int)sizeof(T);
     struct ColState {
         Lanes best;
@@ -198,20 +199,30 @@ struct PairExtremum {
         uint32_t row;              // last row folded
         uint32_t step;             // distance between the lane's consecutive rows
         uint32_t limit;            // rows per chunk (at most 65,535)
+        uint32_t lane_stride;      // index distance between neighbouring lanes (rows: 1, columns: 0)
     };
     __device__ static uint32_t simd_beats(uint32_t x, uint32_t b) {  // all ones in the lanes where x beats b
-        if constexpr (sizeof(T) == 1 && std::is_signed_v<T>) return kMax ? __vcmpgts4(x, b) : __vcmplts4(x, b);
-        else if constexpr (sizeof(T) == 1) return kMax ? __vcmpgtu4(x, b) : __vcmpltu4(x, b);
-        else if constexpr (std::is_signed_v<T>) return kMax ? __vcmpgts2(x, b) : __vcmplts2(x, b);
-        else return kMax ? __vcmpgtu2(x, b) : __vcmpltu2(x, b);
+        if constexpr (std::is_same_v<T, __half>) {
+            __half2 hx, hb;
+            memcpy(&hx, &x, 4);
+            memcpy(&hb, &b, 4);
+            return kMax ? __hgt2_mask(hx, hb) : __hlt2_mask(hx, hb);
+        } else if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+            __nv_bfloat162 hx, hb;
+            memcpy(&hx, &x, 4);
+            memcpy(&hb, &b, 4);
+            return kMax ? __hgt2_mask(hx, hb) : __hlt2_mask(hx, hb);
+        } else if constexpr (sizeof(T) == 1 && std::is_signed_v<T>) {
+            return kMax ? __vcmpgts4(x, b) : __vcmplts4(x, b);
+        } else if constexpr (sizeof(T) == 1) {
+            return kMax ? __vcmpgtu4(x, b) : __vcmpltu4(x, b);
+        } else if constexpr (std::is_signed_v<T>) {
+            return kMax ? __vcmpgts2(x, b) : __vcmplts2(x, b);
+        } else {
+            return kMax ? __vcmpgtu2(x, b) : __vcmpltu2(x, b);
+        }
     }
-    __device__ static uint32_t simd_ext(uint32_t x, uint32_t b) {
-        if constexpr (sizeof(T) == 1 && std::is_signed_v<T>) return kMax ? __vmaxs4(x, b) : __vmins4(x, b);
-        else if constexpr (sizeof(T) == 1) return kMax ? __vmaxu4(x, b) : __vminu4(x, b);
-        else if constexpr (std::is_signed_v<T>) return kMax ? __vmaxs2(x, b) : __vmins2(x, b);
-        else return kMax ? __vmaxu2(x, b) : __vminu2(x, b);
-    }
-    __device__ static ColState col_init(uint32_t step, uint32_t limit) {
+    __device__ static ColState col_init(uint32_t step, uint32_t limit, uint32_t lane_stride = 0) {
         ColState c;
         Vec16<T> v;
 #pragma unroll
@@ -226,6 +237,7 @@ struct PairExtremum {
         c.row = 0;
         c.step = step;
         c.limit = limit;
+        c.lane_stride = lane_stride;
         return c;
     }
     // lanes that won in the current chunk take the row index of their last win; the chunk restarts
@@ -233,7 +245,7 @@ struct PairExtremum {
 #pragma unroll
         for (int j = 0; j < kLanes; ++j) {
             const uint32_t t = (c.won[j / 2] >> (16 * (j % 2))) & 0xffffu;
-            if (t != 0) c.idx[j] = (int32_t)(c.row - (c.n - t) * c.step);
+            if (t != 0) c.idx[j] = (int32_t)(c.row - (c.n - t) * c.step + (uint32_t)j * c.lane_stride);
         }
 #pragma unroll
         for (int i = 0; i < kLanes / 2; ++i) c.won[i] = 0;
@@ -251,7 +263,7 @@ struct PairExtremum {
         if ((m[0] | m[1] | m[2] | m[3]) != 0u) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                c.best.w[i] = simd_ext(w[i], c.best.w[i]);
+                c.best.w[i] = (c.best.w[i] & ~m[i]) | (w[i] & m[i]);
                 if constexpr (sizeof(T) == 1) {
                     // byte lanes (4i .. 4i+3) -> the 16-bit lanes of won[2i] and won[2i + 1]
                     const uint32_t lo = __byte_perm(m[i], 0, 0x1100), hi = __byte_perm(m[i], 0, 0x3322);
@@ -269,7 +281,7 @@ struct PairExtremum {
         Vec16<T> v;
         memcpy(&v, &c.best, 16);
 #pragma unroll
-        for (int j = 0; j < kLanes; ++j) st[j] = State{v.v[j], c.idx[j]};
+        for (int j = 0; j < kLanes; ++j) st[j] = State{widen(v.v[j]), c.idx[j]};
     }
 };
 
@@ -315,7 +327,7 @@ struct ValueExtremum {
     // column kernel: the 16 columns of a lane fold as one packed vector
     static constexpr bool kColSimd = kVecFold;
     using ColState = Lanes;
-    __device__ static Lanes col_init(uint32_t, uint32_t) { return vec_init(); }
+    __device__ static Lanes col_init(uint32_t, uint32_t, uint32_t = 0) { return vec_init(); }
     __device__ static void col_fold(Lanes& p, const uint32_t (&w)[4], uint32_t) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) p.w[i] = ext2(p.w[i], w[i]);
@@ -525,6 +537,7 @@ struct RowArgs {
     uint32_t seg;       // elements per split (multiple of 16 / sizeof(T) unless split == 1)
     uint32_t split;     // S
     uint32_t rows;      // M
+    uint32_t chunk;     // vectors per chunk of the packed (value, index) fold
     Dims d;             // shape (with fast divisors) and input strides in s1
 };
 
@@ -563,8 +576,39 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
         const uint32_t nvec = (end - vbeg) / V;
         const T* pv = p + vbeg;
         uint32_t c = lane;
+        // (value, index) of the 1- and 2-byte types but Float16: the packed fold of the column kernel,
+        // its lanes being the V positions of the thread's vectors (consecutive vectors G * V elements
+        // apart).  Float16 keeps the element fold, whose widening is one conversion (B200, ArgMax over
+        // rows of 32,768: Float16 1.01 element-wise / 0.94 packed; BFloat16 0.86 / 0.94, int16 0.74 /
+        // 0.86, int8 0.37 / 0.74 of the measured copy bandwidth)
+        constexpr bool kPackedPair = !VecFold<R>::value && ColSimd<R>::value && !std::is_same_v<T, __half>;
+        if constexpr (kPackedPair) {
+            typename R::ColState cs = R::col_init(G * V, a.chunk, 1);
+            for (; c + (kUnroll - 1) * G < nvec; c += kUnroll * G) {
+                Vec16<T> x[kUnroll];
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) x[k] = load_stream(pv + (size_t)(c + k * G) * V);
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) {
+                    uint32_t w[4];
+                    memcpy(w, &x[k], 16);
+                    R::col_fold(cs, w, vbeg + (c + k * G) * V);
+                }
+            }
+            for (; c < nvec; c += G) {
+                Vec16<T> x = load_stream(pv + (size_t)c * V);
+                uint32_t w[4];
+                memcpy(w, &x, 16);
+                R::col_fold(cs, w, vbeg + c * V);
+            }
+            S lanes[V];
+            R::col_finish(cs, lanes);
+#pragma unroll
+            for (int j = 0; j < V; ++j) R::merge(st[j], lanes[j]);
+        }
         [[maybe_unused]] Lanes pk;
         if constexpr (VecFold<R>::value) pk = R::vec_init();
+        if constexpr (!kPackedPair)
         for (; c + (kUnroll - 1) * G < nvec; c += kUnroll * G) {
             Vec16<T> x[kUnroll];
 #pragma unroll
@@ -579,6 +623,7 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
                 }
             }
         }
+        if constexpr (!kPackedPair)
         for (; c < nvec; c += G) {
             Vec16<T> x = load_stream(pv + (size_t)c * V);
             if constexpr (VecFold<R>::value) {
@@ -633,7 +678,7 @@ struct ColArgs {
     Dims d;               // outer axes: shape (fast divisors) and input strides in s1
 };
 
-// Rows per chunk of the packed column fold: 65,535 (the 16-bit row numbers' range).  A lower value
+// Rows (or row vectors) per chunk of the packed (value, index) fold: 65,535 (the 16-bit chunk numbers' range).  A lower value
 // changes no result, only how often the chunk numbers turn into row indices; it is settable so tests can
 // reach that step at small sizes (mtxc_debug_set_col_chunk, not part of the public header).
 std::atomic<uint32_t> g_col_chunk{65535};
@@ -938,6 +983,7 @@ int launch_reduce(const Meta& m, const Out dst, const void* src, uint32_t rstrid
         a.seg = p.seg;
         a.split = p.split;
         a.rows = (uint32_t)p.outputs;
+        a.chunk = g_col_chunk.load(std::memory_order_relaxed);
         a.d.n = m.cdims;
         for (uint32_t i = 0; i < m.cdims; ++i) {
             a.d.shape[i] = m.shape[i];

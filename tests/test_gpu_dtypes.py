@@ -145,3 +145,39 @@ def test_reduce_pair_half(gpu, port, kind):
         gv, want_v = bf16_to_f32(gv), bf16_to_f32(want_v)
     assert_bits_equal(gv, want_v, "pair value")
     assert_bits_equal(i.cpu().numpy(), port.reduce("argmax", x, 1, dtype_code=code(kind)), "pair index")
+
+
+@pytest.mark.parametrize("kind", ["f16", "bf16"])
+@pytest.mark.parametrize("op", ["max", "min", "argmax", "argmin"])
+def test_reduce_half_packed(gpu, port, kind, op):
+    """The packed (value, index) fold of the half types (16-byte lanes of 8 elements compared as the
+    floats they widen to), over columns and over rows: NaN, infinities, +-0 and ties; values rising or
+    falling along the reduced axis (a new best every row); the 4-byte fallback lanes and misaligned
+    operands; chunks of 1 and 3 rows as well as the default, so the 16-bit chunk numbers turn into
+    indices mid-run.  Bit-exact."""
+    import ctypes
+
+    from matrix_b200 import _abi
+
+    set_chunk = _abi.lib().mtxc_debug_set_col_chunk
+    set_chunk.argtypes, set_chunk.restype = [ctypes.c_uint32], ctypes.c_uint32
+    rng = np.random.default_rng(31)
+    cases = [([300, 64], 0, 0), ([3, 257, 48], 1, 0), ([1000, 20], 0, 0), ([700, 96], 0, 4),
+             ([64, 3000], 1, 0), ([8, 70001], 1, 0), ([5, 4099], 1, 3)]  # the last three: over rows
+    for chunk in (65535, 1, 3):
+        set_chunk(chunk)
+        try:
+            for shape, axis, off in cases:
+                strides = [int(np.prod(shape[i + 1:])) for i in range(len(shape))]
+                n = int(np.prod(shape))
+                for pattern in ("special", "rising", "falling"):
+                    if pattern == "special":
+                        v = make(kind, rng, n, special=True)
+                    else:
+                        ramp = (np.indices(shape)[axis].reshape(-1) / 32.0 - 4.0).astype(np.float32)
+                        ramp = ramp if pattern == "rising" else -ramp
+                        v = ramp.astype(np.float16) if kind == "f16" else to_bf16_bits(ramp)
+                    base = np.concatenate([np.zeros(off, dtype=v.dtype), v])
+                    check_reduce(gpu, port, kind, op, base, shape, strides, off, axis)
+        finally:
+            set_chunk(65535)

@@ -98,22 +98,26 @@ def narrow_pattern(rng, kind, shape, axis, dtype):
 
 @pytest.mark.parametrize("dtype", NARROW, ids=lambda d: np.dtype(d).name)
 @pytest.mark.parametrize("op", ["max", "min", "argmax", "argmin"])
-def test_reduce_narrow_columns(gpu, port, dtype, op):
-    """Max / Min / ArgMax / ArgMin over a strided axis of the 1- and 2-byte types: the 16-byte packed
-    lanes (inner extent a multiple of 16 bytes), the 4-byte fallback lanes (a multiple of 4 bytes, or an
-    operand offset that breaks 16-byte alignment), and the split path (long reduced axis), each with the
-    value patterns that take the packed compare's rare update on every row or on none.  Bit-exact,
-    first index of a tie."""
+def test_reduce_narrow_packed(gpu, port, dtype, op):
+    """Max / Min / ArgMax / ArgMin of the 1- and 2-byte types through the packed folds: over a strided
+    axis, the 16-byte lanes (inner extent a multiple of 16 bytes), the 4-byte fallback lanes (a multiple
+    of 4 bytes, or an operand offset that breaks 16-byte alignment) and the split path (long reduced
+    axis); over rows, lanes along the row.  Each with value patterns that make every row (or vector) win
+    some lane or none, and with chunks of 1, 3 and 7 rows besides the default, so the 16-bit chunk
+    numbers turn into indices mid-run.  Bit-exact, first index of a tie."""
     rng = np.random.default_rng(zlib.crc32(f"narrow{op}{np.dtype(dtype).name}".encode()))
     code = 7 if dtype == np.bool_ else None
-    cases = [([300, 64], 0, 0), ([3, 257, 48], 1, 0), ([1000, 20], 0, 0), ([700, 96], 0, 4), ([20000, 32], 0, 0)]
+    cases = [([300, 64], 0, 0), ([3, 257, 48], 1, 0), ([1000, 20], 0, 0), ([700, 96], 0, 4), ([20000, 32], 0, 0),
+             # rows: the same packed fold with the lanes along the row (warp and CTA per row, a split row,
+             # an odd length, a start off the 16-byte boundary)
+             ([64, 3000], 1, 0), ([8, 70001], 1, 0), ([5, 4099], 1, 3)]
     set_chunk = _col_chunk_setter()
     # the default chunk (65,535 rows: one chunk per lane at these sizes), then chunks of 1, 3 and 7 rows,
     # which turn the 16-bit chunk row numbers into indices at every row or in the middle of the lane's rows
     for chunk in (65535, 1, 3, 7):
         set_chunk(chunk)
         try:
-            for shape, axis, off in (cases if chunk == 65535 else cases[:2]):
+            for shape, axis, off in (cases if chunk == 65535 else cases[:2] + cases[5:]):
                 strides = [int(np.prod(shape[i + 1:])) for i in range(len(shape))]
                 for kind in ("random", "ties", "rising", "falling", "constant", "low", "high"):
                     v = narrow_pattern(rng, kind, shape, axis, dtype)
