@@ -45,6 +45,16 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Cluster-wide barrier in which only the warp that wrote other CTAs' shared memory arrives with release
+// semantics; the other warps arrive relaxed (they published nothing, and a release arrival fences each
+// warp's prior memory operations).  Every thread waits with acquire semantics, so the released writes
+// are visible to all readers after it.  `writer` must be uniform across the warp (.aligned).
+__device__ __forceinline__ void cluster_barrier(bool writer) {
+    if (writer) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    else asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // FULL: the row fills the cluster exactly (row_len == C * 256 * 4 * VPT), so no vector needs a bounds
 // predicate.
 template <int C, int VPT, bool FULL>
@@ -96,7 +106,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
     }
     // every CTA's pushes are complete and visible after this barrier; afterwards a CTA reads only its
     // own shared memory, so no CTA can leave while another still reads from it
-    cluster.sync();
+    cluster_barrier(warp == 0);
     m = lowest_value<float>();
 #pragma unroll
     for (int r = 0; r < C; ++r) m = (m < max_slot[r]) ? max_slot[r] : m;
@@ -122,7 +132,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
         w = warp_sum(w);
         if (lane < C) *cluster.map_shared_rank(&sum_slot[rank], lane) = w;
     }
-    cluster.sync();
+    cluster_barrier(warp == 0);
     s = 0.0f;
 #pragma unroll
     for (int r = 0; r < C; ++r) s = __fadd_rn(s, sum_slot[r]);
