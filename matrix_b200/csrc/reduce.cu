@@ -51,6 +51,10 @@ struct Pair {
     T v;
     int32_t i;
 };
+template <typename S>
+struct IsPair : std::false_type {};
+template <typename T>
+struct IsPair<Pair<T>> : std::true_type {};
 
 template <typename T>
 __device__ __forceinline__ T shfl_xor(T v, int mask) {
@@ -761,7 +765,23 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
 #pragma unroll
     for (int j = 0; j < V; ++j) partial[threadIdx.x * V + j] = st[j];
     __syncthreads();
-    if (ty == 0 && active) {
+    if constexpr (IsPair<S>::value) {
+        // (value, index) states: the tile's tx * V outputs are finished by all threads, consecutive
+        // outputs on consecutive threads (coalesced stores).  Output q (lane x = q / V, element j = q % V)
+        // sits at partial[t * tx * V + q] for row group t and merges them in ascending t, the order of
+        // the single-thread merge below (B200, ArgMax over axis 1 of [16f, 8192, 1024]: int8 0.45 ->
+        // 0.60, int16 0.71 -> 0.76, Float16 0.87 -> 0.91 of the measured copy bandwidth; for value
+        // states, whose merges are cheap, one warp finishing alone measured faster)
+        const uint32_t tile_outputs = a.tx * V;
+        const uint32_t tile_col = tile * tile_outputs;
+        const uint64_t gbase = (uint64_t)o * a.inner + tile_col;
+        for (uint32_t q = threadIdx.x; q < tile_outputs && tile_col + q < a.inner; q += kBlock) {
+            S s = partial[q];
+            for (uint32_t t = 1; t < ty_count; ++t) R::merge(s, partial[t * tile_outputs + q]);
+            if (a.split == 1) R::store(a.out, gbase + q, s);
+            else static_cast<S*>(a.partials)[(uint64_t)part * a.outputs + gbase + q] = s;
+        }
+    } else if (ty == 0 && active) {
         for (uint32_t t = 1; t < ty_count; ++t) {
 #pragma unroll
             for (int j = 0; j < V; ++j) R::merge(st[j], partial[(t * a.tx + tx) * V + j]);
