@@ -72,15 +72,15 @@ def _cpu(line, **spec):
 
 
 def run_all(dev, stream, configs=None, scale=1, cpu_hook=None):
-    """configs: names to run (default all: C1 C3 C4 C5a C5b, and F2 F3 F4 for the statistics, astype
-    and pointwise kernels); scale: divide each config's leading extent by this (small cases for
-    profiling)."""
+    """configs: names to run (default all: C1 C3 C4 C5a C5b, and F2 ... F7 for the statistics, astype,
+    pointwise, mixed-dtype, half-precision and 1- / 2-byte kernels); scale: divide each config's leading
+    extent by this (small cases for profiling)."""
     global _CPU_HOOK
     _CPU_HOOK = cpu_hook
     peak = _peak()
     g = torch.Generator(device=dev)
     out = []
-    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4", "F5", "F6"}
+    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4", "F5", "F6", "F7"}
 
     # C1: Sum over the last axis of f32 [1024, 4096] ~ N(0,1)
     if "C1" in want:
@@ -103,6 +103,8 @@ def run_all(dev, stream, configs=None, scale=1, cpu_hook=None):
         _f5(out, dev, stream, g, peak, scale)
     if "F6" in want:
         _f6(out, dev, stream, g, peak, scale)
+    if "F7" in want:
+        _f7(out, dev, stream, g, peak, scale)
     torch.cuda.empty_cache()
     return out
 
@@ -336,3 +338,26 @@ def _f6(out, dev, stream, g, peak, scale):
     ms = _time(lambda: backend.reduce("sum", y, 1), stream)
     out.append(_line("F6-bf16-sum", "Sum(axis=1) bf16 [8, 2^28] (4 GiB)", y.numel() * 2, ms, peak))
     del y
+
+
+def _f7(out, dev, stream, g, peak, scale):
+    """The packed (value, index) folds of the 1- and 2-byte integer types, 512 MiB of int8 or 1 GiB of
+    int16 each (values 0..99): ArgMax over a strided axis at C3's layout (int8 first, so a profile that
+    skips two column-kernel launches lands on it), int8 ArgMax over rows of 32,768, int16 ArgMax over a
+    strided axis."""
+    g.manual_seed(11)
+    c0 = max(64 // scale, 1)
+    x = torch.randint(0, 100, (c0, 8192, 1024), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+    ms = _time(lambda: backend.reduce("argmax", x, 1), stream)
+    out.append(_line("F7-i8-argmax-cols", "ArgMax(axis=1) int8 [64,8192,1024]", x.numel() + c0 * 1024 * 4, ms, peak))
+    del x
+    r0 = max(16384 // scale, 1)
+    y = torch.randint(0, 100, (r0, 32768), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+    ms = _time(lambda: backend.reduce("argmax", y, 1), stream)
+    out.append(_line("F7-i8-argmax-rows", "ArgMax(axis=-1) int8 [16384,32768]", y.numel() + r0 * 4, ms, peak))
+    del y
+    z = torch.randint(0, 100, (c0, 8192, 1024), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+    ms = _time(lambda: backend.reduce("argmax", z, 1), stream)
+    out.append(_line("F7-i16-argmax-cols", "ArgMax(axis=1) int16 [64,8192,1024]", z.numel() * 2 + c0 * 1024 * 4, ms,
+                     peak))
+    del z
