@@ -203,21 +203,21 @@ def binary(op: str, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None =
            meta: BinaryMeta | None = None) -> torch.Tensor:
     """a <op> b with broadcasting, evaluated through mtxc_broadcast_binary.  Operands of different
     dtypes are promoted as the reference does (promote_types, astype first): in one pass through
-    mtxc_broadcast_binary_mixed where it covers the pair (a Float result with a Float operand), else with
-    an explicit astype of the operand(s) whose dtype differs."""
+    mtxc_broadcast_binary_mixed when the promoted dtype is one of the two (e.g. Float with Int32, Int64
+    with Int32), else with an explicit astype of both operands (e.g. Float16 with Int32 -> Float)."""
     if a.dtype != b.dtype:
         if op not in MIXED_OPS:
             raise _abi.MtxcError(_abi.ERR_UNSUPPORTED_DTYPE, "max / min of mixed dtypes: cast one operand first")
         ca, cb = dtype_code(a.dtype), dtype_code(b.dtype)
         common = lib().mtxc_promote_types(ca, cb)
-        if common == 0 and 0 in (ca, cb):
+        if common in (ca, cb) and common in CODE_TO_TORCH:
             if meta is None:
                 meta = binary_meta(list(a.shape), _check_strides(a), list(b.shape), _check_strides(b))
             if out is None:
-                out = torch.empty(meta.out_shape, dtype=torch.float32, device=a.device)
+                out = torch.empty(meta.out_shape, dtype=CODE_TO_TORCH[common], device=a.device)
             shape, sr, sa, sb = meta.arrays
-            check(lib().mtxc_broadcast_binary_mixed(_abi.BINARY_OPS[op], 0, ca, cb, out.data_ptr(), a.data_ptr(),
-                                                     b.data_ptr(), meta.cdims, shape, sr, sa, sb))
+            check(lib().mtxc_broadcast_binary_mixed(_abi.BINARY_OPS[op], common, ca, cb, out.data_ptr(),
+                                                     a.data_ptr(), b.data_ptr(), meta.cdims, shape, sr, sa, sb))
             return out
         t = CODE_TO_TORCH[common]
         a = a if a.dtype == t else astype(a, t, make_contig=False)

@@ -7,42 +7,67 @@
 // as the op reads it gives the same bits with one pass over the data: for an int32 [N] + float [N] add,
 // 12 bytes per element move instead of 20.
 //
-// Covered here: a Float result with one Float operand and one operand of any other dtype (the common
-// mixed case: an integer, half or Bool tensor meeting a float one), for the promoting ops Add, Sub, Mul,
-// Div and Equal.  The metadata is the op's own (broadcast_shapes + collapse_dims over the result and
-// the two operands).  Other combinations use mtxc_astype then mtxc_broadcast_binary.
+// Covered here: every pair of operand dtypes whose promoted dtype is one of the two (a Float result with a
+// Float operand and any other; Int64 with Int32 or a narrower integer; a half type with Bool; ...), for the
+// promoting ops Add, Sub, Mul, Div and Equal.  The operand of the result's dtype is read as it is, the other
+// converted as it is read (convert<>, the conversion of mtxc_astype), and the op is apply<> in the result
+// dtype, as in mtxc_broadcast_binary.  Pairs that promote to a third dtype (e.g. Float16 with Int32 ->
+// Float) use mtxc_astype then mtxc_broadcast_binary.  The metadata is the op's own (broadcast_shapes +
+// collapse_dims over the result and the two operands).
 #include "elementwise.cuh"
 #include "ops.cuh"
+#include "promote.h"
 
 namespace mtxc {
 namespace {
 
-template <int OP, typename SA, typename SB>
+template <typename T>
+constexpr int code_of() {
+    if constexpr (std::is_same_v<T, float>) return MTXC_FLOAT;
+    else if constexpr (std::is_same_v<T, __half>) return MTXC_FLOAT16;
+    else if constexpr (std::is_same_v<T, __nv_bfloat16>) return MTXC_BFLOAT16;
+    else if constexpr (std::is_same_v<T, int32_t>) return MTXC_INT32;
+    else if constexpr (std::is_same_v<T, uint32_t>) return MTXC_UINT32;
+    else if constexpr (std::is_same_v<T, int64_t>) return MTXC_INT64;
+    else if constexpr (std::is_same_v<T, uint64_t>) return MTXC_UINT64;
+    else if constexpr (std::is_same_v<T, int16_t>) return MTXC_INT16;
+    else if constexpr (std::is_same_v<T, uint16_t>) return MTXC_UINT16;
+    else if constexpr (std::is_same_v<T, int8_t>) return MTXC_INT8;
+    else if constexpr (std::is_same_v<T, uint8_t>) return MTXC_UINT8;
+    else return MTXC_BOOL;
+}
+
+// result D = promote_types(SA, SB); each operand converted to D as it is read, the op in D
+template <int OP, typename D, typename SA, typename SB>
 struct MixedOp {
-    using Out = float;
+    using Out = D;
     using In0 = SA;
     using In1 = SB;
     using In2 = SA;
     static constexpr int kArity = 2;
-    __device__ __forceinline__ float operator()(SA a, SB b, SA) const {
-        return apply<OP, float>(convert<float, SA>(a), convert<float, SB>(b));
+    __device__ __forceinline__ D operator()(SA a, SB b, SA) const {
+        return apply<OP, D>(convert<D, SA>(a), convert<D, SB>(b));
     }
 };
 
+// D: the result dtype, which one operand (`a` when d_is_a) already has; the other operand's dtype is
+// `other`.  Instantiates the kernel only for pairs the promotion table maps to D.
 template <int OP>
-int launch_mixed(int a_dtype, int b_dtype, const ew::MapDesc& m, int sms, cudaStream_t st, bool& known) {
+int launch_mixed(int dtype, int other, bool d_is_a, const ew::MapDesc& m, int sms, cudaStream_t st, bool& known) {
     int rc = MTXC_OK;
-    if (a_dtype == MTXC_FLOAT) {
-        known = dispatch_dtype(b_dtype, [&](auto* tag) {
-            using SB = std::remove_pointer_t<decltype(tag)>;
-            rc = ew::launch_map<MixedOp<OP, float, SB>>(m, sms, st);
+    bool has_kernel = false;
+    dispatch_dtype(dtype, [&](auto* dtag) {
+        using D = std::remove_pointer_t<decltype(dtag)>;
+        dispatch_dtype(other, [&](auto* stag) {
+            using S = std::remove_pointer_t<decltype(stag)>;
+            if constexpr (!std::is_same_v<D, S> && promote_code(code_of<D>(), code_of<S>()) == code_of<D>()) {
+                has_kernel = true;
+                if (d_is_a) rc = ew::launch_map<MixedOp<OP, D, D, S>>(m, sms, st);
+                else rc = ew::launch_map<MixedOp<OP, D, S, D>>(m, sms, st);
+            }
         });
-    } else {
-        known = dispatch_dtype(a_dtype, [&](auto* tag) {
-            using SA = std::remove_pointer_t<decltype(tag)>;
-            rc = ew::launch_map<MixedOp<OP, SA, float>>(m, sms, st);
-        });
-    }
+    });
+    known = has_kernel;
     return rc;
 }
 
@@ -60,11 +85,11 @@ extern "C" int mtxc_broadcast_binary_mixed(int op, int dtype, int a_dtype, int b
         op != MTXC_BINARY_EQUAL)
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: only the promoting ops (add, sub, mul, "
                                                "div, equal)");
-    if (dtype != MTXC_FLOAT || (a_dtype != MTXC_FLOAT && b_dtype != MTXC_FLOAT))
-        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, "mtxc_broadcast_binary_mixed: needs a Float result and a Float "
-                                                "operand (use mtxc_astype + mtxc_broadcast_binary)");
     if (mtxc_promote_types(a_dtype, b_dtype) != dtype)
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: dtype is not promote_types(a, b)");
+    if (a_dtype == b_dtype || (a_dtype != dtype && b_dtype != dtype))
+        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, "mtxc_broadcast_binary_mixed: needs operands of two dtypes, one of "
+                                                "them the result's (use mtxc_astype + mtxc_broadcast_binary)");
     if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: cdims > MTXC_MAX_DIMS");
     if (cdims && (!shape || !r_strides || !a_strides || !b_strides))
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: null metadata pointer");
@@ -80,14 +105,16 @@ extern "C" int mtxc_broadcast_binary_mixed(int op, int dtype, int a_dtype, int b
     m.ss[0] = a_strides;
     m.ss[1] = b_strides;
     ThreadCtx& c = ctx();
+    const bool d_is_a = a_dtype == dtype;
+    const int other = d_is_a ? b_dtype : a_dtype;
     bool known = false;
     int rc = MTXC_OK;
     switch (op) {
-        case MTXC_BINARY_ADD: rc = launch_mixed<MTXC_BINARY_ADD>(a_dtype, b_dtype, m, c.sm_count, c.stream(), known); break;
-        case MTXC_BINARY_SUB: rc = launch_mixed<MTXC_BINARY_SUB>(a_dtype, b_dtype, m, c.sm_count, c.stream(), known); break;
-        case MTXC_BINARY_MUL: rc = launch_mixed<MTXC_BINARY_MUL>(a_dtype, b_dtype, m, c.sm_count, c.stream(), known); break;
-        case MTXC_BINARY_DIV: rc = launch_mixed<MTXC_BINARY_DIV>(a_dtype, b_dtype, m, c.sm_count, c.stream(), known); break;
-        default: rc = launch_mixed<MTXC_BINARY_EQUAL>(a_dtype, b_dtype, m, c.sm_count, c.stream(), known); break;
+        case MTXC_BINARY_ADD: rc = launch_mixed<MTXC_BINARY_ADD>(dtype, other, d_is_a, m, c.sm_count, c.stream(), known); break;
+        case MTXC_BINARY_SUB: rc = launch_mixed<MTXC_BINARY_SUB>(dtype, other, d_is_a, m, c.sm_count, c.stream(), known); break;
+        case MTXC_BINARY_MUL: rc = launch_mixed<MTXC_BINARY_MUL>(dtype, other, d_is_a, m, c.sm_count, c.stream(), known); break;
+        case MTXC_BINARY_DIV: rc = launch_mixed<MTXC_BINARY_DIV>(dtype, other, d_is_a, m, c.sm_count, c.stream(), known); break;
+        default: rc = launch_mixed<MTXC_BINARY_EQUAL>(dtype, other, d_is_a, m, c.sm_count, c.stream(), known); break;
     }
     if (!known)
         return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_broadcast_binary_mixed: no kernel for ") +

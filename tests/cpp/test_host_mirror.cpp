@@ -314,6 +314,21 @@ static void test_promotion_and_pointwise(std::mt19937& rng) {
     for (int i = 0; ok && i < 64; ++i) ok = p16[i] == (int16_t)((int)u8[i] * (int)i8[i]);
     EXPECT(ok, "Int16 product");
 
+    // Int64 - Int32 -> Int64: Int32 converted inside the op's kernel (no AsType node in front)
+    std::vector<int64_t> wide64(64);
+    std::vector<int32_t> narrow32(64);
+    for (int i = 0; i < 64; ++i) {
+        wide64[i] = (int64_t)(rng() % 2000001) - 1000000;
+        narrow32[i] = (int32_t)(rng() % 2001) - 1000;
+    }
+    matrix D64 = matrix::from_host(wide64.data(), {64}, dtype::Int64) - matrix::from_host(narrow32.data(), {64}, dtype::Int32);
+    D64.eval();
+    EXPECT(D64.type() == dtype::Int64, "Int64 - Int32 is Int64");
+    std::vector<int64_t> d64 = D64.to_host<int64_t>();
+    ok = d64.size() == 64;
+    for (int i = 0; ok && i < 64; ++i) ok = d64[i] == wide64[i] - (int64_t)narrow32[i];
+    EXPECT(ok, "Int64 difference with the promotion fused");
+
     // equal, greater, less, where, floor, full, logical_and
     std::vector<float> x = random_ties(8 * 129, rng), y = random_ties(129, rng);
     for (int k = 0; k < 40; ++k) x[k] = y[k];  // some equal pairs in the first row

@@ -1,5 +1,5 @@
 """GPU parity for binary ops on operands of different dtypes, where the promotion is fused into the op
-(mtxc_broadcast_binary_mixed: a Float result with one Float operand).  The reference evaluates
+(mtxc_broadcast_binary_mixed: a result dtype that one operand already has).  The reference evaluates
 astype(promote_types(a, b)) of the other operand and then the op; the oracle does exactly that, and the
 fused kernel must give the same bits."""
 import numpy as np
@@ -50,3 +50,91 @@ def test_mixed_strided_and_transposed(gpu, port):
     with pytest.raises(Exception):
         gpu.binary("max", fd, idv.T)  # max / min do not promote
     assert torch.cuda.is_available()
+
+
+def _absorbing_pairs():
+    """(result dtype D, other dtype S) with promote_types(D, S) == D, D not Float (covered above)."""
+    from matrix_b200 import _abi
+
+    from tests.test_oracle_pin_pointwise import ALL_CODES
+
+    lib = _abi.lib()
+    return [(d, s) for d in ALL_CODES for s in ALL_CODES
+            if d != 0 and s != d and lib.mtxc_promote_types(d, s) == d]
+
+
+def _safe(rng, code, n, nonzero):
+    """Values of dtype `code` small enough that no op below overflows the promoted dtype, and nonzero
+    where they divide (integer division by zero and INT_MIN / -1 are undefined in C++ and trap on x86)."""
+    from tests.test_oracle_pin_pointwise import STORAGE
+
+    if code == 7:
+        return np.ones(n, dtype=np.bool_) if nonzero else rng.integers(0, 2, n).astype(np.bool_)
+    if code in (1, 10):
+        return values(rng, code, n)
+    lo = -100 if np.issubdtype(STORAGE[code], np.signedinteger) else 0
+    v = rng.integers(lo, 101, n)
+    if nonzero:
+        v[v == 0] = 7
+    return v.astype(STORAGE[code])
+
+
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div", "equal"])
+def test_mixed_result_of_one_operand(gpu, port, op):
+    """Every pair of operand dtypes whose promoted dtype is one of the two, other than Float (Int64 with
+    Int32 and the narrower integers, Int32 with Int16 / UInt32 / ..., a half type with Bool, ...): the
+    fused kernel against the reference's evaluation (astype of the other operand, then the op in the
+    result dtype), both operand orders, bit for bit."""
+    import torch
+
+    from matrix_b200.backend import CODE_TO_TORCH
+
+    pairs = _absorbing_pairs()
+    assert len(pairs) == 29
+    rng = np.random.default_rng(500)
+    for d, s in pairs:
+        for sd, ss in (([64, 1, 96], [1, 16, 96]), ([7, 13], [7, 13]), ([], [5])):
+            for d_first in (True, False):
+                # the divisor (second operand) must stay nonzero after the conversion
+                xd = _safe(rng, d, int(np.prod(sd)), nonzero=op == "div" and not d_first).reshape(sd)
+                xs = _safe(rng, s, int(np.prod(ss)), nonzero=op == "div" and d_first).reshape(ss)
+                xs_as_d = port.astype(xs, xd.dtype, src_code=s, dst_code=d)
+                if d_first:
+                    a, b, ad, bd = xd, xs_as_d, dev(xd, d), dev(xs, s)
+                else:
+                    a, b, ad, bd = xs_as_d, xd, dev(xs, s), dev(xd, d)
+                want = port.binary(op, np.ascontiguousarray(a), np.ascontiguousarray(b), dtype_code=d)
+                got = gpu.binary(op, ad, bd)
+                gpu.sync()
+                tag = f"{op} D={d} S={s} {'D op S' if d_first else 'S op D'} {sd} {ss}"
+                assert got.dtype == CODE_TO_TORCH[d], tag
+                g = got.cpu().numpy() if d != 10 else got.view(torch.uint16).cpu().numpy()
+                if d == 10:  # BFloat16 bits as float32, so that NaNs (0 / 0) compare as NaNs
+                    g, want = _bf16_as_f32(g), _bf16_as_f32(want)
+                assert_bits_equal(g, want, tag)
+
+
+def _bf16_as_f32(bits):
+    return (np.asarray(bits).astype(np.uint32) << 16).view(np.float32)
+
+
+def test_mixed_third_dtype_is_refused_by_the_fused_entry(gpu):
+    """A pair that promotes to a third dtype (Float16 with Int32 -> Float) has no fused kernel: the entry
+    point says so, and the driver evaluates it with astype + op instead."""
+    import ctypes as C
+
+    import torch
+
+    from matrix_b200 import _abi
+
+    lib = _abi.lib()
+    a = torch.ones(8, dtype=torch.float16, device="cuda")
+    b = torch.ones(8, dtype=torch.int32, device="cuda")
+    out = torch.empty(8, dtype=torch.float32, device="cuda")
+    u = _abi.u32_array
+    rc = lib.mtxc_broadcast_binary_mixed(0, 0, 1, 3, C.c_void_p(out.data_ptr()), C.c_void_p(a.data_ptr()),
+                                         C.c_void_p(b.data_ptr()), 1, u([8]), u([1]), u([1]), u([1]))
+    assert rc == _abi.ERR_UNSUPPORTED_DTYPE
+    got = gpu.binary("add", a, b)
+    gpu.sync()
+    assert got.dtype == torch.float32 and bool((got == 2).all())
