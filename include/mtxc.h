@@ -304,12 +304,11 @@ int mtxc_broadcast_binary(int op, int dtype, void* r, const void* a, const void*
  * promote_types(a_dtype, b_dtype), which is what the reference evaluates (astype of the operand whose dtype
  * differs, then the op: Matrix.mm:8312-8382), bit for bit -- but in one pass, without writing and
  * re-reading a converted copy.  Same metadata as mtxc_broadcast_binary (the strides of the operands as
- * given; the reference's astype keeps them).  Supported: op ADD, SUB, MUL, DIV or EQUAL; two different
- * operand dtypes (not Complex64) whose promoted dtype is one of them (Float with any other dtype; Int64 with
- * Int32, Int16, Int8, UInt32, UInt16, UInt8 or Bool; Int32 with Int16, Int8, UInt32, UInt16, UInt8 or Bool;
- * any dtype with Bool; ...).  Pairs that promote to a third dtype (Float16 with Int32 -> Float, ...):
- * MTXC_ERR_UNSUPPORTED_DTYPE (evaluate astype + mtxc_broadcast_binary instead); dtype other than
- * promote_types(a_dtype, b_dtype): MTXC_ERR_INVALID_ARGUMENT. */
+ * given; the reference's astype keeps them).  Supported: op ADD, SUB, MUL, DIV or EQUAL; any two different
+ * operand dtypes but Complex64, whether the promoted dtype is one of them (Float with Int32, Int64 with
+ * Int32, ...) or a third (Float16 with Int32 -> Float, UInt8 with Int8 -> Int16, ...).  Complex64:
+ * MTXC_ERR_UNSUPPORTED_DTYPE; dtype other than promote_types(a_dtype, b_dtype), or a_dtype == b_dtype:
+ * MTXC_ERR_INVALID_ARGUMENT. */
 int mtxc_broadcast_binary_mixed(int op, int dtype, int a_dtype, int b_dtype, void* r, const void* a, const void* b,
                                 uint32_t cdims, const uint32_t* shape, const uint32_t* r_strides,
                                 const uint32_t* a_strides, const uint32_t* b_strides);

@@ -202,15 +202,14 @@ MIXED_OPS = ("add", "sub", "mul", "div", "equal")
 def binary(op: str, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
            meta: BinaryMeta | None = None) -> torch.Tensor:
     """a <op> b with broadcasting, evaluated through mtxc_broadcast_binary.  Operands of different
-    dtypes are promoted as the reference does (promote_types, astype first): in one pass through
-    mtxc_broadcast_binary_mixed when the promoted dtype is one of the two (e.g. Float with Int32, Int64
-    with Int32), else with an explicit astype of both operands (e.g. Float16 with Int32 -> Float)."""
+    dtypes are promoted as the reference does (promote_types, astype of both operands first), in one pass
+    through mtxc_broadcast_binary_mixed: each operand is converted to the promoted dtype as it is read."""
     if a.dtype != b.dtype:
         if op not in MIXED_OPS:
             raise _abi.MtxcError(_abi.ERR_UNSUPPORTED_DTYPE, "max / min of mixed dtypes: cast one operand first")
         ca, cb = dtype_code(a.dtype), dtype_code(b.dtype)
         common = lib().mtxc_promote_types(ca, cb)
-        if common in (ca, cb) and common in CODE_TO_TORCH:
+        if common in CODE_TO_TORCH:
             if meta is None:
                 meta = binary_meta(list(a.shape), _check_strides(a), list(b.shape), _check_strides(b))
             if out is None:

@@ -48,7 +48,7 @@ def _stale(obj: Path, deps: list[Path]) -> bool:
 def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
     LIBDIR.mkdir(exist_ok=True)
-    headers = sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    headers = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
     jobs = []
     objs = []
     for src in sorted(CSRC.glob("*.cu")):

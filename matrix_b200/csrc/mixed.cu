@@ -12,43 +12,12 @@
 // promoting ops Add, Sub, Mul, Div and Equal.  The operand of the result's dtype is read as it is, the other
 // converted as it is read (convert<>, the conversion of mtxc_astype), and the op is apply<> in the result
 // dtype, as in mtxc_broadcast_binary.  Pairs that promote to a third dtype (e.g. Float16 with Int32 ->
-// Float) use mtxc_astype then mtxc_broadcast_binary.  The metadata is the op's own (broadcast_shapes +
+// Float) are in mixed3.cu, reached from the same entry point.  The metadata is the op's own (broadcast_shapes +
 // collapse_dims over the result and the two operands).
-#include "elementwise.cuh"
-#include "ops.cuh"
-#include "promote.h"
+#include "mixed.cuh"
 
 namespace mtxc {
 namespace {
-
-template <typename T>
-constexpr int code_of() {
-    if constexpr (std::is_same_v<T, float>) return MTXC_FLOAT;
-    else if constexpr (std::is_same_v<T, __half>) return MTXC_FLOAT16;
-    else if constexpr (std::is_same_v<T, __nv_bfloat16>) return MTXC_BFLOAT16;
-    else if constexpr (std::is_same_v<T, int32_t>) return MTXC_INT32;
-    else if constexpr (std::is_same_v<T, uint32_t>) return MTXC_UINT32;
-    else if constexpr (std::is_same_v<T, int64_t>) return MTXC_INT64;
-    else if constexpr (std::is_same_v<T, uint64_t>) return MTXC_UINT64;
-    else if constexpr (std::is_same_v<T, int16_t>) return MTXC_INT16;
-    else if constexpr (std::is_same_v<T, uint16_t>) return MTXC_UINT16;
-    else if constexpr (std::is_same_v<T, int8_t>) return MTXC_INT8;
-    else if constexpr (std::is_same_v<T, uint8_t>) return MTXC_UINT8;
-    else return MTXC_BOOL;
-}
-
-// result D = promote_types(SA, SB); each operand converted to D as it is read, the op in D
-template <int OP, typename D, typename SA, typename SB>
-struct MixedOp {
-    using Out = D;
-    using In0 = SA;
-    using In1 = SB;
-    using In2 = SA;
-    static constexpr int kArity = 2;
-    __device__ __forceinline__ D operator()(SA a, SB b, SA) const {
-        return apply<OP, D>(convert<D, SA>(a), convert<D, SB>(b));
-    }
-};
 
 // D: the result dtype, which one operand (`a` when d_is_a) already has; the other operand's dtype is
 // `other`.  Instantiates the kernel only for pairs the promotion table maps to D.
@@ -87,9 +56,9 @@ extern "C" int mtxc_broadcast_binary_mixed(int op, int dtype, int a_dtype, int b
                                                "div, equal)");
     if (mtxc_promote_types(a_dtype, b_dtype) != dtype)
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: dtype is not promote_types(a, b)");
-    if (a_dtype == b_dtype || (a_dtype != dtype && b_dtype != dtype))
-        return fail(MTXC_ERR_UNSUPPORTED_DTYPE, "mtxc_broadcast_binary_mixed: needs operands of two dtypes, one of "
-                                                "them the result's (use mtxc_astype + mtxc_broadcast_binary)");
+    if (a_dtype == b_dtype)
+        return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: operands of one dtype (use "
+                                               "mtxc_broadcast_binary)");
     if (cdims > MTXC_MAX_DIMS) return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: cdims > MTXC_MAX_DIMS");
     if (cdims && (!shape || !r_strides || !a_strides || !b_strides))
         return fail(MTXC_ERR_INVALID_ARGUMENT, "mtxc_broadcast_binary_mixed: null metadata pointer");
@@ -105,10 +74,17 @@ extern "C" int mtxc_broadcast_binary_mixed(int op, int dtype, int a_dtype, int b
     m.ss[0] = a_strides;
     m.ss[1] = b_strides;
     ThreadCtx& c = ctx();
-    const bool d_is_a = a_dtype == dtype;
-    const int other = d_is_a ? b_dtype : a_dtype;
     bool known = false;
     int rc = MTXC_OK;
+    if (a_dtype != dtype && b_dtype != dtype) {  // promoted to a third dtype (mixed3.cu)
+        rc = launch_mixed3(op, dtype, a_dtype, b_dtype, m, c.sm_count, c.stream(), known);
+        if (!known)
+            return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_broadcast_binary_mixed: no kernel for ") +
+                                                        dtype_name(a_dtype) + " with " + dtype_name(b_dtype));
+        return rc;
+    }
+    const bool d_is_a = a_dtype == dtype;
+    const int other = d_is_a ? b_dtype : a_dtype;
     switch (op) {
         case MTXC_BINARY_ADD: rc = launch_mixed<MTXC_BINARY_ADD>(dtype, other, d_is_a, m, c.sm_count, c.stream(), known); break;
         case MTXC_BINARY_SUB: rc = launch_mixed<MTXC_BINARY_SUB>(dtype, other, d_is_a, m, c.sm_count, c.stream(), known); break;

@@ -161,7 +161,7 @@ public:
         if (t == EvalType::COMPILE_TRACE) return;
         if (evaluated) return;
         evaluated = true;
-        if (a_.type() != b_.type())  // promotion fused into the op (the result dtype is one operand's)
+        if (a_.type() != b_.type())  // promotion fused into the op
             check(mtxc_broadcast_binary_mixed(op_, (int)out.type(), (int)a_.type(), (int)b_.type(), out.data(),
                                               a_.data(), b_.data(), cdims_, shape_, sr_, sa_, sb_),
                   "mtxc_broadcast_binary_mixed");
@@ -426,11 +426,9 @@ matrix make_binary(int op, const matrix& a, const matrix& b) {
     if (!promotes && a.type() != b.type())
         throw std::runtime_error("max / min(a, b) of mixed dtypes: cast one operand with astype first");
     const dtype common = promote_types(a.type(), b.type());
-    // a result dtype that one operand already has (Float with any other dtype, Int64 with Int32, ...): the
-    // other operand's conversion happens inside the op's kernel (mtxc_broadcast_binary_mixed), same bits as
-    // astype + op without the promoted copy
-    const bool fused = promotes && a.type() != b.type() && (a.type() == common || b.type() == common) &&
-                       common != dtype::Complex64;
+    // the conversion of both operands happens inside the op's kernel (mtxc_broadcast_binary_mixed), same
+    // bits as astype + op without the promoted copies
+    const bool fused = promotes && a.type() != b.type() && common != dtype::Complex64;
     const matrix lhs = (a.type() == common || fused) ? a : a.astype(common);
     const matrix rhs = (b.type() == common || fused) ? b : b.astype(common);
     std::vector<size_m> out_shape;

@@ -1,5 +1,5 @@
 """GPU parity for binary ops on operands of different dtypes, where the promotion is fused into the op
-(mtxc_broadcast_binary_mixed: a result dtype that one operand already has).  The reference evaluates
+(mtxc_broadcast_binary_mixed: every pair of dtypes but Complex64).  The reference evaluates
 astype(promote_types(a, b)) of the other operand and then the op; the oracle does exactly that, and the
 fused kernel must give the same bits."""
 import numpy as np
@@ -118,9 +118,46 @@ def _bf16_as_f32(bits):
     return (np.asarray(bits).astype(np.uint32) << 16).view(np.float32)
 
 
-def test_mixed_third_dtype_is_refused_by_the_fused_entry(gpu):
-    """A pair that promotes to a third dtype (Float16 with Int32 -> Float) has no fused kernel: the entry
-    point says so, and the driver evaluates it with astype + op instead."""
+def _third_dtype_pairs():
+    """(a dtype, b dtype, promoted dtype) with the promoted dtype neither operand's, both orders."""
+    from matrix_b200 import _abi
+
+    from tests.test_oracle_pin_pointwise import ALL_CODES
+
+    lib = _abi.lib()
+    return [(a, b, lib.mtxc_promote_types(a, b)) for a in ALL_CODES for b in ALL_CODES
+            if a != b and lib.mtxc_promote_types(a, b) not in (a, b)]
+
+
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div", "equal"])
+def test_mixed_third_dtype(gpu, port, op):
+    """Every pair of operand dtypes that promotes to a third dtype (Float16 with Int32 -> Float, UInt8
+    with Int8 -> Int16, Int16 with UInt32 -> Int32, ...), both orders: the fused kernel, which converts
+    both operands as it reads them, against the reference's evaluation (astype of both, then the op),
+    bit for bit."""
+    from matrix_b200.backend import CODE_TO_TORCH
+    from tests.test_oracle_pin_pointwise import STORAGE
+
+    pairs = _third_dtype_pairs()
+    assert len(pairs) == 52
+    rng = np.random.default_rng(600)
+    for ca, cb, d in pairs:
+        for sa, sb in (([64, 1, 96], [1, 16, 96]), ([7, 13], [7, 13]), ([], [5])):
+            xa = _safe(rng, ca, int(np.prod(sa)), nonzero=False).reshape(sa)
+            xb = _safe(rng, cb, int(np.prod(sb)), nonzero=op == "div").reshape(sb)
+            a_d = port.astype(xa, STORAGE[d], src_code=ca, dst_code=d)
+            b_d = port.astype(xb, STORAGE[d], src_code=cb, dst_code=d)
+            want = port.binary(op, np.ascontiguousarray(a_d), np.ascontiguousarray(b_d), dtype_code=d)
+            got = gpu.binary(op, dev(xa, ca), dev(xb, cb))
+            gpu.sync()
+            tag = f"{op} {ca} with {cb} -> {d} {sa} {sb}"
+            assert got.dtype == CODE_TO_TORCH[d], tag
+            assert_bits_equal(got.cpu().numpy(), want, tag)
+
+
+def test_mixed_entry_refusals(gpu):
+    """mtxc_broadcast_binary_mixed refuses Complex64 operands, operands of one dtype, and a result dtype
+    other than promote_types(a, b)."""
     import ctypes as C
 
     import torch
@@ -132,9 +169,15 @@ def test_mixed_third_dtype_is_refused_by_the_fused_entry(gpu):
     b = torch.ones(8, dtype=torch.int32, device="cuda")
     out = torch.empty(8, dtype=torch.float32, device="cuda")
     u = _abi.u32_array
-    rc = lib.mtxc_broadcast_binary_mixed(0, 0, 1, 3, C.c_void_p(out.data_ptr()), C.c_void_p(a.data_ptr()),
-                                         C.c_void_p(b.data_ptr()), 1, u([8]), u([1]), u([1]), u([1]))
-    assert rc == _abi.ERR_UNSUPPORTED_DTYPE
-    got = gpu.binary("add", a, b)
+
+    def call(dtype, ca, cb):
+        return lib.mtxc_broadcast_binary_mixed(0, dtype, ca, cb, C.c_void_p(out.data_ptr()),
+                                               C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), 1, u([8]),
+                                               u([1]), u([1]), u([1]))
+
+    assert call(9, 9, 3) == _abi.ERR_UNSUPPORTED_DTYPE  # Complex64
+    assert call(1, 1, 1) == _abi.ERR_INVALID_ARGUMENT  # one dtype
+    assert call(1, 1, 3) == _abi.ERR_INVALID_ARGUMENT  # Float16 with Int32 is Float, not Float16
+    assert call(0, 1, 3) == _abi.OK
     gpu.sync()
-    assert got.dtype == torch.float32 and bool((got == 2).all())
+    assert bool((out == 2).all())
