@@ -617,11 +617,11 @@ def run_sharded(args):
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # a bounded sleep kernel (~0.1 ms per step, outside the timed region) keeps the GPU busy while the
+    # a bounded sleep kernel (~0.5 ms per step, outside the timed region) keeps the GPU busy while the
     # host queues the K steps, so the events time the device work rather than the host's launch rate
-    # (C1's 16 MiB step is shorter than one Python launch; C4's sharded step is shorter than the
-    # Python that enqueues its reduction, NCCL all-gather and merge)
-    torch.cuda._sleep(200_000 * args.steps)
+    # (C1's 16 MiB step is shorter than one Python launch; a C4 step on 8 GPUs is ~24 us of device work
+    # behind ~130 us of Python enqueueing its reduction, NCCL all-gather and merge, measured on one B200)
+    torch.cuda._sleep(1_000_000 * args.steps)
     e0.record(stream)
     for _ in range(args.steps):
         result = step()
