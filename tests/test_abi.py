@@ -114,3 +114,25 @@ def test_column_chunk_hook_clamps():
     assert fn(0) == 7
     assert fn(1 << 20) == 1
     assert fn(65535) == 65535
+
+
+def test_every_mixed_pair_has_a_fused_kernel_family():
+    """mtxc_broadcast_binary_mixed serves every pair of two different dtypes (Complex64 aside) from two
+    kernel families: the promoted dtype is one operand's (mixed.cu, any result dtype), or a third one
+    (mixed3.cu, which instantiates only Float, Int16 and Int32 results).  The promotion table must keep
+    the third dtypes inside that set, and the split is 40 + 26 of the 66 pairs."""
+    from matrix_b200 import _abi
+
+    lib = _abi.lib()
+    codes = [0, 1, 2, 3, 4, 5, 6, 7, 8, 10, 11, 12]
+    own = third = 0
+    for i, a in enumerate(codes):
+        for b in codes[i + 1:]:
+            d = lib.mtxc_promote_types(a, b)
+            assert d == lib.mtxc_promote_types(b, a)
+            if d in (a, b):
+                own += 1
+            else:
+                assert d in (0, 4, 3), (a, b, d)  # Float, Int16, Int32
+                third += 1
+    assert (own, third) == (40, 26)
