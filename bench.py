@@ -1,27 +1,27 @@
 """Benchmark of the reduce / broadcast hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--suite]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5b|c2|...]
 
-Metric: reduce/broadcast GB/s (algorithmic HBM bytes per second, whole job)
-and its fraction of the B200 HBM roofline, against the reference's CPU path.
+Metric: reduce/broadcast GB/s (algorithmic HBM bytes per second, whole job) and its fraction of
+the B200 HBM roofline, against the reference's CPU path.
 
-Workload (one "step"): benchmark config 2, the broadcasted Add and Mul of float32
-a[256,1,4096] ~ U(-1,1) with b[1,512,4096] ~ U(-1,1) into [256,512,4096] (2 GiB each),
-evaluated through the C ABI (mtxc_broadcast_binary) with the metadata the reference's
-operator+ / operator* build.  Algorithmic bytes per op: out 2^31 + a 2^22 + b 2^23 =
-2,160,066,560.  Inputs are synthetic (seeded), as no dataset is named for this benchmark.
+Headline workload (default, one "step"): benchmark config 5b, the largest config, a full Sum of
+2^32 float32 values ~ N(0,1) (16 GiB), held as [8, 2^29] because 2^32 elements exceed the reference's
+32-bit size_m, and evaluated as x.sum(1).sum(0).  The rows are sharded over the GPUs (one process per
+GPU, torchrun); each rank reduces its rows with mtxc_reduce (sum(1), the HBM stream), and sum(0) over
+the sharded axis is mtxc_reduce_sharded: the local sum of the rank's partials, an NCCL all-gather of
+one value per rank and the ordered merge, all enqueued by the C ABI.  Strong scaling: the total is fixed
+at 2^32 elements whatever N.  The exchange of step k runs on a side stream and overlaps the row
+reduction of step k + 1; the last exchange is inside the timed region.  Algorithmic bytes per step:
+17,179,869,184 (the input read once).  Inputs are synthetic (seeded per row), as no dataset is named.
 
-Multi-GPU (torchrun, one rank per GPU): weak scaling.  The global a is [256*N, 1, 4096],
-sharded along its leading axis; each rank evaluates its shard against a replicated b.  The
-op needs no collective.  Time is measured with CUDA events on the launching stream and the
-maximum over ranks is reported.
+`--impl reference` times the reference's own CPU Sum loop (Matrix.mm:15193-15205, compiled from the
+reference tree into oracle/_ref/libmtx_ref.so) on a bounded sample of the same workload, one slice of
+the flattened input per host thread.
 
-`--impl reference` times the reference's own CPU loop for the same ops (the broadcast
-lambdas of Matrix.mm:7475-7567, compiled from the reference tree into
-oracle/_ref/libmtx_ref.so), one slice of output rows per host thread, on a bounded sample.
-
-`--suite` additionally prints one line per other benchmark config (C1, C3, C4, C5a, C5b);
-those lines are diagnostics, not the headline.
+`--workload c2` times config 2 (broadcast Add + Mul f32 a[256,1,4096] (op) b[1,512,4096], weak scaling,
+no collective) with the same instrumentation; `--workload c1|c3|c4|c5a` time the other configs sharded
+over the GPUs; `--suite` prints one device-time line per config (diagnostics, not the headline).
 """
 from __future__ import annotations
 
@@ -56,6 +56,23 @@ WORKLOAD = "C2: broadcast Add+Mul f32 a[256,1,4096] (op) b[1,512,4096] -> [256,5
 FALLBACK_HBM_GBS = 6650.0
 
 
+# config 5b: the headline
+C5B_ROWS, C5B_COLS = 8, 1 << 29
+C5B_WORKLOAD = ("C5b: full Sum of f32 2^32 ~ N(0,1) held as [8, 2^29] (16 GiB), x.sum(1).sum(0); rows sharded "
+                "over the GPUs, sum(0) over the sharded axis = NCCL all-gather of the per-rank partials + ordered merge")
+
+
+def fill_c5b_rows(x, first_row: int) -> None:
+    """Seeded synthetic input of config 5b: global row r ~ N(0,1) from its own seed (1000 + r), so the
+    tensor is the same whatever the number of GPUs it is sharded over."""
+    import torch
+
+    g = torch.Generator(device=x.device)
+    for r in range(x.shape[0]):
+        g.manual_seed(1000 + first_row + r)
+        x[r].normal_(generator=g)
+
+
 def measured_peak():
     p = REPO / "MEASURED_PEAKS.json"
     try:
@@ -71,6 +88,19 @@ def profile_traffic():
     try:
         for line in p.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def profile_traffic_c5b():
+    """DRAM bytes (read + write) per input byte of reduce_rows_kernel's C5b launch, from the committed
+    ncu summary of a smaller case of the same kernel (the traffic grows in proportion to the input)."""
+    p = REPO / "profiles" / "reduce_rows_c5b_traffic.txt"
+    try:
+        for line in p.read_text().splitlines():
+            if line.startswith("dram_bytes_per_input_byte:"):
                 return float(line.split(":", 1)[1])
     except OSError:
         pass
@@ -224,6 +254,67 @@ def cpu_baseline_line(threads: int, target_s: float = 10.0):
                       f"{threads} thread(s) over row slices, {dt:.2f} s"}
 
 
+def cpu_sum_runner(ev, sample, threads: int):
+    """One pass of the reference's Sum loop over the flat float32 `sample`: `threads` contiguous slices,
+    each summed by the loop on its own host thread (the loop itself is single-threaded: Matrix.mm:
+    15193-15205), then the slices' partial sums added in order."""
+    n = sample.size
+    per = [n * t // threads for t in range(threads + 1)]
+    metas = {}
+    parts = [np.float32(0)] * threads
+
+    def work(t):
+        lo, hi = per[t], per[t + 1]
+        if hi <= lo:
+            return
+        m = metas.setdefault(hi - lo, ev.reduce_meta([hi - lo], [1], 0))
+        parts[t] = ev.reduce_raw("sum", sample, lo, m)
+
+    def run():
+        ths = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        acc = np.float32(0)
+        for v in parts:
+            acc = np.float32(acc + np.float32(v))
+        return acc
+
+    return run
+
+
+def cpu_c5b_sampler(threads: int, target_s: float, sample=None):
+    """(run, elements, kind): a bounded sample of config 5b (a prefix of the flattened input, or seeded
+    N(0,1) values when no sample is given) sized so one pass takes about target_s seconds."""
+    ev, kind = cpu_evaluator()
+    threads = max(1, threads)
+    if sample is None:
+        sample = np.random.default_rng([5, 0]).standard_normal(1 << 27, dtype=np.float32)
+    n = min(sample.size, max(threads * 4096, 1 << 22))
+    t0 = time.perf_counter()
+    cpu_sum_runner(ev, sample[:n], threads)()
+    dt = max(time.perf_counter() - t0, 1e-6)
+    n = int(min(sample.size, max(threads * 4096, n * target_s / dt)))
+    return cpu_sum_runner(ev, sample[:n], threads), n, kind
+
+
+def cpu_c5b_line(threads: int, target_s: float, sample=None):
+    run, n, kind = cpu_c5b_sampler(threads, target_s / 8, sample)
+    reps, dt = 0, 0.0
+    while reps == 0 or dt < 0.5 * target_s:
+        t0 = time.perf_counter()
+        run()
+        dt += time.perf_counter() - t0
+        reps += 1
+    what = ("the reference CPU Sum loop (Matrix.mm:15193-15205) compiled from its tree" if kind == "reference"
+            else "oracle restatement of the Sum loop")
+    return {"value": round(n * 4 * reps / dt / 1e9, 4), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"C5b: the first {n:,} of the 2^32 elements ({n * 4 / 2**20:.0f} MiB), x{reps}, {what}, "
+                      f"{threads} thread(s) over contiguous slices of the flattened input, partials added in "
+                      f"order, {dt:.2f} s"}
+
+
 def suite_cpu_hook():
     """CPU leg of the --suite lines: the reference's own loop (oracle/_ref, else the restatement) on a
     leading-axis slice of the config's input, timed on one host core, and the GPU's result for the same
@@ -278,11 +369,29 @@ def suite_cpu_hook():
 # reference arm
 # ------------------------------------------------------------------------------------------
 def run_reference(args):
+    """The reference's own CPU path for the selected workload, on rank 0 only, with every host thread."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    run, rows, bytes_per, kind = cpu_c2_sampler(threads, target_s=2.0)
+    if args.workload == "c2":
+        run, rows, bytes_per, kind = cpu_c2_sampler(threads, target_s=2.0)
+        workload = {"workload": WORKLOAD, "ops": list(OPS), "sample_rows": rows,
+                    "parallelism": f"{threads} host threads"}
+        sample = f"{rows} of 256 rows of a per step ({rows}x512x4096 outputs per op), one row slice per thread"
+        scaling, data = "weak", "synthetic (seeded U(-1,1))"
+    elif args.workload == "c5b":
+        # each step a bounded sample: about a minute for the whole run, at most 0.25 s per step
+        per_step = min(0.25, 60.0 / max(1, args.steps + args.warmup))
+        run, n, kind = cpu_c5b_sampler(threads, per_step)
+        bytes_per = n * 4
+        workload = {"workload": C5B_WORKLOAD, "sample_elements": n, "parallelism": f"{threads} host threads"}
+        sample = (f"the first {n:,} of the 2^32 elements per step ({bytes_per / 2**20:.0f} MiB, seeded N(0,1)), one "
+                  f"contiguous slice per thread, each summed by the reference loop, partials added in order")
+        scaling, data = "strong", "synthetic (seeded N(0,1))"
+    else:
+        print(json.dumps({"impl": "reference", "unavailable": f"--impl reference covers c5b and c2, not {args.workload}"}))
+        return 0
     for _ in range(args.warmup):
         run()
     times = []
@@ -295,11 +404,9 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded U(-1,1))",
-        "config": {"workload": WORKLOAD, "ops": list(OPS), "sample_rows": rows, "parallelism": f"{threads} host threads"},
-        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": f"{rows} of 256 rows of a per step ({rows}x512x4096 outputs per op), one row slice per thread"},
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": data,
+        "config": workload,
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -309,7 +416,7 @@ def run_reference(args):
 # ------------------------------------------------------------------------------------------
 # our arm
 # ------------------------------------------------------------------------------------------
-def run_ours(args):
+def run_c2(args):
     import torch
     import torch.distributed as dist
 
@@ -475,6 +582,206 @@ def run_ours(args):
     return 0
 
 
+def run_c5b(args):
+    """The headline: config 5b, a full Sum of 2^32 f32 values, rows sharded over the ranks (strong
+    scaling), through the C ABI: mtxc_reduce for sum(1) on the main stream, mtxc_reduce_sharded for sum(0)
+    (local sum, NCCL all-gather, ordered merge) on a side stream, double-buffered so the exchange of one
+    step overlaps the next step's row reduction."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from matrix_b200 import _abi, backend
+    from matrix_b200.shard import NativeComm, shard_range
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    backend.init(local)
+    L = _abi.lib()
+    main_s = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    comm = NativeComm()
+    cols = args.cols
+    lo, hi = shard_range(C5B_ROWS, world, rank)
+    rows = hi - lo
+    total_bytes = C5B_ROWS * cols * 4
+    local_bytes = rows * cols * 4
+    x = torch.empty((rows, cols), dtype=torch.float32, device=dev)
+    fill_c5b_rows(x, lo)
+    parts = [torch.empty(rows, dtype=torch.float32, device=dev) for _ in range(2)]
+    outs = [torch.empty((), dtype=torch.float32, device=dev) for _ in range(2)]
+    m1 = backend.reduce_meta([rows, cols], [cols, 1], 1)   # x.sum(1): this rank's rows
+    m0 = backend.reduce_meta([rows], [1], 0)               # .sum(0): over the sharded axis
+    f32 = backend.dtype_code(torch.float32)
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    for ev in done:
+        ev.record(main_s)
+
+    def step(k, ev_pair=None):
+        b = k % 2
+        main_s.wait_event(done[b])                       # partial buffer b is free again
+        if ev_pair is not None:
+            ev_pair[0].record(main_s)
+        backend.reduce_launch("sum", x.data_ptr(), f32, parts[b].data_ptr(), m1)
+        if ev_pair is not None:
+            ev_pair[1].record(main_s)
+        ready[b].record(main_s)
+        side.wait_event(ready[b])
+        backend.set_stream(side)
+        backend.reduce_sharded_launch("sum", parts[b].data_ptr(), f32, outs[b].data_ptr(), m0)
+        backend.set_stream(main_s)
+        done[b].record(side)
+        return outs[b]
+
+    result = step(0)
+    torch.cuda.synchronize()
+    sampler = None
+    if rank == 0:
+        uuids = []
+        for i in range(torch.cuda.device_count()):
+            try:
+                uuids.append(str(torch.cuda.get_device_properties(i).uuid))
+            except Exception:
+                pass
+        sampler = ClockSampler(uuids[:world] if world > 1 else uuids[local:local + 1])
+        sampler.start()
+        time.sleep(0.3)
+    for k in range(args.warmup):
+        step(k)
+    main_s.wait_stream(side)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main_s)
+    h0 = time.perf_counter()
+    for k in range(args.steps):
+        result = step(k, pairs[k])
+    host_s = time.perf_counter() - h0
+    main_s.wait_stream(side)                             # the last exchange is inside the timed region
+    e1.record(main_s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = e0.elapsed_time(e1)
+    launch_ms = [a.elapsed_time(b) for a, b in pairs]
+    clocks = sampler.stop() if sampler else None
+
+    # correctness gate: the fp64 sum of the same tensor (torch, a reference value only) and the float-sum
+    # rule |got - exact| <= 1e-5 * sum|x|
+    exact = torch.zeros((), dtype=torch.float64, device=dev)
+    absum = torch.zeros((), dtype=torch.float64, device=dev)
+    for r in range(rows):
+        exact += x[r].sum(dtype=torch.float64)
+        absum += x[r].abs().sum(dtype=torch.float64)
+    # e2e through the C ABI with host buffers: each rank uploads its rows from pinned memory, reduces,
+    # exchanges and reads the result back into pinned memory, every step
+    e2e_steps = 0 if args.no_e2e else 3
+    e2e_ms = 0.0
+    if e2e_steps:
+        hbuf = C.c_void_p()
+        _abi.check(L.mtxc_host_alloc(local_bytes, C.byref(hbuf)))
+        hout = C.c_void_p()
+        _abi.check(L.mtxc_host_alloc(4, C.byref(hout)))
+        _abi.check(L.mtxc_download(hbuf, x.data_ptr(), local_bytes))
+        _abi.check(L.mtxc_sync())
+
+        def e2e_step():
+            _abi.check(L.mtxc_upload(x.data_ptr(), hbuf, local_bytes))
+            backend.reduce_launch("sum", x.data_ptr(), f32, parts[0].data_ptr(), m1)
+            backend.reduce_sharded_launch("sum", parts[0].data_ptr(), f32, outs[0].data_ptr(), m0)
+            _abi.check(L.mtxc_download(hout, outs[0].data_ptr(), 4))
+            _abi.check(L.mtxc_sync())
+
+        e2e_step()
+        if world > 1:
+            dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(main_s)
+        for _ in range(e2e_steps):
+            e2e_step()
+        a1.record(main_s)
+        torch.cuda.synchronize()
+        e2e_ms = a0.elapsed_time(a1)
+        e2e_result = C.c_float.from_address(hout.value).value
+        _abi.check(L.mtxc_host_free(hbuf))
+        _abi.check(L.mtxc_host_free(hout))
+    got = float(result.item())
+    ok = abs(got - float(exact.item())) <= 1e-5 * float(absum.item())
+    if e2e_steps:
+        ok = ok and e2e_result == got  # the same kernels on the same data: the same bits
+    t = torch.tensor([elapsed_ms, e2e_ms, host_s * 1e3, 0.0 if ok else 1.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms, host_ms, bad = (float(v) for v in t.tolist())
+    ok = bad == 0.0
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        avg_launch_s = statistics.mean(launch_ms) / 1e3
+        achieved = local_bytes / avg_launch_s / 1e9
+        per_byte = profile_traffic_c5b()
+        value = total_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) per row)",
+            "config": {"workload": C5B_WORKLOAD if cols == C5B_COLS else f"{C5B_WORKLOAD} ([8, {cols}] case)",
+                       "elements": C5B_ROWS * cols, "bytes_per_step": total_bytes,
+                       "l2": "input (16 GiB; 16/N GiB per GPU) far larger than L2: every step streams it from HBM",
+                       "parallelism": f"strong: {C5B_ROWS} rows over {world} GPU(s) ({rows} per GPU), sum(0) over the "
+                                      f"sharded axis by mtxc_reduce_sharded (NCCL all-gather + ordered merge)"},
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "traffic": round(per_byte * local_bytes) if per_byte else None,
+                         "kernel": "reduce_rows_kernel<SUM,float,256> (+ its split finalize)",
+                         "bytes_per_launch": local_bytes,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, a read+write copy burst)"
+                         if peak_kind == "measured" else "fallback 6.65 TB/s",
+                         "traffic_source": "ncu DRAM read+write bytes per input byte of a [8, 2^24] launch "
+                                           "(profiles/reduce_rows_c5b_traffic.txt), scaled to this launch"},
+            "clocks": clocks,
+            "e2e": {"value": round(total_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 3) if e2e_steps else None,
+                    "unit": UNIT, "h2d_bytes_per_step": total_bytes if e2e_steps else 0,
+                    "d2h_bytes_per_step": 4 * world if e2e_steps else 0, "steps": e2e_steps,
+                    "path": "per rank: mtxc_upload of its rows from pinned host memory + mtxc_reduce + "
+                            "mtxc_reduce_sharded + mtxc_download of the result into pinned memory + mtxc_sync"},
+            "host_enqueue_ms_per_step": round(host_ms / args.steps, 4),
+            "within_tolerance_of_fp64": ok,
+            "gpu_launches": 4 * args.steps,
+        }
+        if world == 1 and not args.no_cpu:
+            sample = x[0, : 1 << 28].cpu().numpy()
+            line["cpu_baseline"] = cpu_c5b_line(os.cpu_count() or 1, args.cpu_seconds, sample)
+            one = cpu_c5b_line(1, max(2.0, args.cpu_seconds / 3), sample)
+            line["cpu_baseline"]["single_thread"] = {"value": one["value"], "cores": 1, "sample": one["sample"]}
+        print(json.dumps(line), flush=True)
+        if args.suite:
+            from matrix_b200 import suite
+
+            del x
+            torch.cuda.empty_cache()
+            cfgs = args.suite_configs.split(",") if args.suite_configs else None
+            hook = None if args.no_cpu else suite_cpu_hook()
+            for extra in suite.run_all(dev, main_s, cfgs, args.suite_scale, cpu_hook=hook):
+                print(json.dumps(extra), flush=True)
+    comm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0 if ok else 1
+
+
 def sustained_copy_gbs(dev, stream, ms_target: float) -> float:
     """Bandwidth of a plain device copy of random f32 data (torch's copy kernel, used only as a
     reference denominator), run back to back for about `ms_target` ms: what a memory stream sustains
@@ -506,17 +813,17 @@ def sustained_copy_gbs(dev, stream, ms_target: float) -> float:
 # ------------------------------------------------------------------------------------------
 def run_sharded(args):
     """A benchmark config sharded over the GPUs on its leading axis (strong scaling: the total is fixed).
-    C5b: full Sum of f32 2^32 elements (as [8, 2^29], 16 GiB); C4: Sum over axes (0, 2) of f32
-    [32, 4096, 2048]; for both the sharded axis is a reduced one, so a step is the local kernels, the NCCL
-    all-gather of the per-rank partials and the ordered merge.  C1 (Sum of the last axis), C3 (Max and
-    ArgMax over axis 1) and C5a (fused softmax) shard an axis they do not reduce: no collective."""
+    C4: Sum over axes (0, 2) of f32 [32, 4096, 2048]; the sharded axis is a reduced one, so a step is the
+    local sum(2) and mtxc_reduce_sharded for sum(0) (local sum, NCCL all-gather of the per-rank partials,
+    ordered merge).  C1 (Sum of the last axis), C3 (Max and ArgMax over axis 1) and C5a (fused softmax)
+    shard an axis they do not reduce: no collective.  (C5b, the headline, is run_c5b.)"""
     import datetime
 
     import torch
     import torch.distributed as dist
 
     from matrix_b200 import _abi, backend
-    from matrix_b200.shard import reduce_sharded, shard_range
+    from matrix_b200.shard import NativeComm, reduce_sharded, shard_range
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -530,12 +837,9 @@ def run_sharded(args):
     backend.init(local)
     stream = torch.cuda.current_stream(dev)
     wl = args.workload
-    collective = wl in ("c4", "c5b")
-    if wl == "c5b":
-        rows, cols = 8, 1 << 29
-        shape = (rows, cols)
-        desc = "C5b: full Sum of f32 2^32 ~ N(0,1) as [8, 2^29] (16 GiB), rows sharded, all-gather + ordered merge"
-    elif wl == "c4":
+    collective = wl == "c4"
+    comm = NativeComm() if collective else None
+    if wl == "c4":
         rows, cols = 32, 4096 * 2048
         shape = (32, 4096, 2048)
         desc = "C4: Sum over axes (0,2) of f32 [32,4096,2048] ~ N(0,1), axis 0 sharded, all-gather + ordered merge"
@@ -573,12 +877,16 @@ def run_sharded(args):
     else:
         total_bytes = rows * cols * 4
 
-    # C4 / C5b: the local reduction of step k + 1 overlaps the exchange of step k.  The local partials
-    # go to one of two buffers on the main stream; the all-gather and the ordered merge of that buffer
-    # run on a side stream, which waits for the partials, and the main stream does not overwrite a
-    # buffer before the side stream is done with it.
+    # C4: the local reduction of step k + 1 overlaps the exchange of step k.  The local partials go to
+    # one of two buffers on the main stream; the all-gather and the ordered merge of that buffer run on a
+    # side stream, which waits for the partials, and the main stream does not overwrite a buffer before
+    # the side stream is done with it.
     side = torch.cuda.Stream(dev)
-    parts = [backend.reduce("sum", x, 1 if wl == "c5b" else 2) for _ in range(2)]
+    if collective:
+        parts = [backend.reduce("sum", x, 2) for _ in range(2)]
+        local_meta = backend.reduce_meta(list(x.shape), list(x.stride()), 2)
+        shard_meta = backend.reduce_meta(list(parts[0].shape), list(parts[0].stride()), 0)
+        merged = [torch.empty(4096, dtype=torch.float32, device=dev) for _ in range(2)]
     done = [torch.cuda.Event(), torch.cuda.Event()]
     for ev in done:
         ev.record(stream)
@@ -588,14 +896,14 @@ def run_sharded(args):
         k = counter[0] % 2
         counter[0] += 1
         stream.wait_event(done[k])                                # buffer k free again
-        backend.reduce("sum", x, 1 if wl == "c5b" else 2, out=parts[k])   # local axis: no collective
+        backend.reduce("sum", x, 2, out=parts[k], meta=local_meta)  # local axis: no collective
         ready = torch.cuda.Event()
         ready.record(stream)
         side.wait_event(ready)
         with torch.cuda.stream(side):
             backend.set_stream(side)
             try:
-                r = reduce_sharded("sum", parts[k], 0, rows)      # sharded axis: gather + merge
+                r = reduce_sharded("sum", parts[k], 0, rows, comm=comm, out=merged[k], meta=shard_meta)
             finally:
                 backend.set_stream(stream)
             done[k].record(side)
@@ -631,20 +939,30 @@ def run_sharded(args):
     torch.cuda.synchronize()
     dist.barrier()
     ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev if world > 1 else "cpu")
+    # the same steps without the pre-roll: what a caller sees when the host's enqueue rate limits the device
+    e0.record(stream)
+    h0 = time.perf_counter()
+    for _ in range(args.steps):
+        result = step()
+    host_ms = (time.perf_counter() - h0) * 1e3
+    if collective:
+        stream.wait_stream(side)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms_visible = e0.elapsed_time(e1)
+    t = torch.tensor([ms, ms_visible, host_ms], dtype=torch.float64, device=dev if world > 1 else "cpu")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0])
+    ms, ms_visible, host_ms = (float(v) for v in t.tolist())
     # correctness against torch on the same tensor (a reference value only, never the measured path)
     if collective:
-        dims = tuple(range(1, x.dim())) if wl == "c5b" else (0, 2)
+        dims = (0, 2)
         ref = x.sum(dim=dims, dtype=torch.float64)
         absum = x.abs().sum(dim=dims, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(ref)
             dist.all_reduce(absum)
-        ref = ref.sum() if wl == "c5b" else ref
-        absum = absum.sum() if wl == "c5b" else absum
         ok = bool(((result.double() - ref).abs() <= 1e-5 * absum + 1e-30).all())
     elif wl == "c1":
         ok = bool(((result.double() - x.sum(1, dtype=torch.float64)).abs()
@@ -667,8 +985,15 @@ def run_sharded(args):
                 "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) per row)",
                 "config": {"workload": desc, "parallelism": f"axis 0 sharded over {world} GPU(s)",
                            "l2": "input L2-resident (16 MiB)" if wl == "c1" else "input larger than L2"},
-                "frac_of_hbm_peak": round(value / world / peak, 4), "within_tolerance_of_fp64": ok}
+                "frac_of_hbm_peak": round(value / world / peak, 4), "within_tolerance_of_fp64": ok,
+                "host_visible": {"value": round(total_bytes * args.steps / (ms_visible / 1e3) / 1e9, 2),
+                                 "ms_per_step": round(ms_visible / args.steps, 4),
+                                 "host_enqueue_ms_per_step": round(host_ms / args.steps, 4),
+                                 "note": "the same steps timed without the pre-roll sleep: device time including "
+                                         "any gaps the host's enqueue rate leaves"}}
         print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.close()
     dist.barrier()
     dist.destroy_process_group()
     return 0 if ok else 1
@@ -685,19 +1010,23 @@ def main():
     ap.add_argument("--suite-scale", type=int, default=1, help="divide the configs' leading extent (small cases)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--rows", type=int, default=256, help="leading rows of a per rank (256 = C2; smaller for ncu)")
+    ap.add_argument("--rows", type=int, default=256, help="c2: leading rows of a per rank (256 = C2; smaller for ncu)")
+    ap.add_argument("--cols", type=int, default=C5B_COLS, help="c5b: row length (2^29 = C5b; smaller for ncu)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
-    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5a", "c5b"], default="c2",
-                    help="c2 (default headline) or another config sharded over the GPUs: c1, c3, c5a (no "
-                         "collective), c4, c5b (all-gather + ordered merge of the reduced-axis partials)")
+    ap.add_argument("--workload", choices=["c5b", "c2", "c1", "c3", "c4", "c5a"], default="c5b",
+                    help="c5b (default headline: the largest config, strong scaling with the exchange), c2 (weak "
+                         "scaling, no collective), or another config sharded over the GPUs: c1, c3, c5a (no "
+                         "collective), c4 (all-gather + ordered merge of the reduced-axis partials)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload != "c2":
-        return run_sharded(args)
-    return run_ours(args)
+    if args.workload == "c5b":
+        return run_c5b(args)
+    if args.workload == "c2":
+        return run_c2(args)
+    return run_sharded(args)
 
 
 if __name__ == "__main__":

@@ -46,7 +46,8 @@ enum {
     MTXC_ERR_CUDA = 4,            /* a CUDA runtime call or kernel launch failed */
     MTXC_ERR_TIMEOUT = 5,         /* a bounded device-side wait gave up */
     MTXC_ERR_NOT_INITIALIZED = 6, /* mtxc_init was not called on this thread */
-    MTXC_ERR_WORKSPACE = 7        /* the thread's workspace cannot hold the split partials */
+    MTXC_ERR_WORKSPACE = 7,       /* the thread's workspace cannot hold the split partials */
+    MTXC_ERR_COMM = 8             /* NCCL missing or an NCCL call failed (multi-GPU entry points) */
 };
 
 /* dtype codes: identical to the reference's `enum class dtype` (matrix.h:35-51). */
@@ -361,6 +362,54 @@ int mtxc_pointwise(int op, int dtype, void* dst, const void* const* inputs, uint
 #define MTXC_SOFTMAX_MAX_ROW 65536u
 int mtxc_softmax_lastdim(int dtype, void* dst, const void* src, uint64_t rows, uint32_t row_len,
                          uint64_t src_row_stride, uint64_t dst_row_stride);
+
+/* ------------------------------------------------------------------------------------------
+ * Multi-GPU: one communicator per GPU for reductions over an axis sharded across the GPUs of a node
+ * (benchmark configs 4 and 5b).  The reference drives a single Metal device through one GPUManager
+ * (Mods/GPUManager.h:53-54); these entry points are the multi-device half of the layer that replaces
+ * it (the `mtxc_comm_init` / `mtxc_allreduce` exports a multi-GPU drop-in needs).  One process (or host
+ * thread) per GPU; each calls mtxc_init(device) and then mtxc_comm_init with the same unique id.
+ * NCCL (libnccl.so.2) is loaded at run time, reusing the copy already in the process if there is one;
+ * a one-rank communicator does not need it.
+ *
+ * The exchange is an all-gather of the per-rank partials plus a merge in rank order on every rank
+ * (mtxc_merge_partials): every rank ends with the same result, float sums are deterministic, and Max /
+ * ArgMax keep the first-index rule across GPUs.  Everything is enqueued on the calling thread's stream;
+ * like every collective, all ranks must make the same calls in the same order.
+ * ---------------------------------------------------------------------------------------- */
+#define MTXC_COMM_ID_BYTES 128
+
+/* Writes a new unique id (MTXC_COMM_ID_BYTES bytes) for one communicator.  Call on one rank and hand
+ * the bytes to the others out of band (a store, MPI, a file).  MTXC_ERR_COMM when NCCL is missing. */
+int mtxc_comm_unique_id(void* id, size_t bytes);
+
+/* Joins the calling thread (bound to its device by mtxc_init) to a communicator of nranks ranks as
+ * rank `rank`.  Blocks until all nranks ranks have joined (ncclCommInitRank).  Allocates the gather
+ * buffer the exchanges use, buffer_bytes (0: 16 MiB), once, here: the exchanges never allocate.  One
+ * communicator per thread; mtxc_comm_destroy (or mtxc_shutdown) releases it.  nranks == 1 needs no id and
+ * no NCCL. */
+int mtxc_comm_init(int nranks, int rank, const void* id, size_t buffer_bytes);
+int mtxc_comm_destroy(void);
+int mtxc_comm_size(int* nranks, int* rank);
+
+/* A reduction over an axis that is sharded across the ranks: this rank holds a contiguous slice of the
+ * reduced axis, described exactly as for mtxc_reduce (reduce_len = the slice's length, which may be 0).
+ * On return every rank's dst holds the reduction over the whole axis, as mtxc_reduce over the unsharded
+ * tensor would give it: integer sums, Max / Min and ArgMax / ArgMin bit-exact; float sums add the ranks'
+ * partial sums in rank order (within rounding of the unsharded sum).  ArgMax / ArgMin write int32 global
+ * indices and need index_offsets: a host array of nranks entries, the global index of each rank's first
+ * element (the same array on every rank); it is ignored (may be NULL) for the other ops.  Steps, on the
+ * thread's stream: the local reduction into this rank's slot of the gather buffer, the in-place NCCL
+ * all-gather, the ordered merge into dst.  MTXC_ERR_WORKSPACE when nranks x outputs partials do not fit
+ * the communicator's buffer. */
+int mtxc_reduce_sharded(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride, uint32_t reduce_len,
+                        uint32_t cdims, const uint32_t* shape, const uint32_t* dst_strides,
+                        const uint32_t* src_strides, const int64_t* index_offsets);
+
+/* In-place all-reduce of `count` elements of buf (op SUM, MAX or MIN) across the ranks: every rank ends
+ * with buf = the ranks' buffers combined in rank order (SUM: ordered adds, integers wrap; MAX / MIN: a
+ * later rank's value replaces an earlier one's only when strictly better).  Identical on every rank. */
+int mtxc_allreduce(int op, int dtype, void* buf, uint64_t count);
 
 /* ------------------------------------------------------------------------------------------
  * Compiled trace: record the kernels one execute pass enqueues and replay them.  The B200

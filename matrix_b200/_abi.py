@@ -19,6 +19,8 @@ ERR_CUDA = 4
 ERR_TIMEOUT = 5
 ERR_NOT_INITIALIZED = 6
 ERR_WORKSPACE = 7
+ERR_COMM = 8
+COMM_ID_BYTES = 128
 
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
 BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5, "equal": 6}
@@ -88,6 +90,12 @@ def lib() -> C.CDLL:
             "mtxc_reduce_stat_dtype": (i32, [i32, i32, u32]),
             "mtxc_pointwise_collapse": (u32, [U32P, u32, U32P, u32, U32P, U32P]),
             "mtxc_pointwise": (i32, [i32, i32, vp, C.POINTER(vp), u32, u32, U32P, U32P]),
+            "mtxc_comm_unique_id": (i32, [vp, sz]),
+            "mtxc_comm_init": (i32, [i32, i32, vp, sz]),
+            "mtxc_comm_destroy": (i32, []),
+            "mtxc_comm_size": (i32, [C.POINTER(i32), C.POINTER(i32)]),
+            "mtxc_reduce_sharded": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P, C.POINTER(C.c_int64)]),
+            "mtxc_allreduce": (i32, [i32, i32, vp, u64]),
             "mtxc_graph_begin": (i32, []),
             "mtxc_graph_end": (i32, [C.POINTER(vp)]),
             "mtxc_graph_launch": (i32, [vp]),

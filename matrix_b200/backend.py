@@ -353,6 +353,28 @@ def reduce_pair(op: str, x: torch.Tensor, axis: int, keepdims: bool = False, met
     return vals, idx
 
 
+def reduce_sharded_launch(op: str, x_ptr: int, dtype: int, out_ptr: int, meta: ReduceMeta, offsets=None) -> None:
+    """mtxc_reduce_sharded: this rank's slice of the reduced axis (`meta` describes it), the NCCL
+    all-gather of every rank's partials and the ordered merge, on the thread's stream; needs the thread's
+    communicator (shard.NativeComm).  offsets: the global index of each rank's first element (ArgMax /
+    ArgMin)."""
+    import ctypes
+
+    shape, s_out, s_in = meta.arrays
+    offs = (ctypes.c_int64 * len(offsets))(*[int(o) for o in offsets]) if offsets is not None else None
+    check(lib().mtxc_reduce_sharded(_abi.REDUCE_OPS[op], dtype, out_ptr, x_ptr, meta.rstride & 0xFFFFFFFF, meta.rlen,
+                                    meta.cdims, shape, s_out, s_in, offs))
+
+
+def allreduce(op: str, buf: torch.Tensor) -> torch.Tensor:
+    """In-place all-reduce (sum / max / min, rank-order merge) of a contiguous tensor across the
+    communicator's ranks (mtxc_allreduce)."""
+    if not buf.is_contiguous():
+        raise ValueError("allreduce needs a contiguous tensor")
+    check(lib().mtxc_allreduce(_abi.REDUCE_OPS[op], dtype_code(buf.dtype), buf.data_ptr(), buf.numel()))
+    return buf
+
+
 def merge_partials(op: str, values: torch.Tensor, indices: torch.Tensor | None = None, offsets=None):
     """Merges shard partials stacked on axis 0 ([parts, ...]) in shard order (mtxc_merge_partials).
     Returns the merged values (sum / max / min) or (values, global indices) (argmax / argmin)."""

@@ -78,7 +78,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
             if out.strip() and (verbose or ptxas_info):
                 print(out, file=sys.stderr)
     if jobs or not LIB.exists() or _stale(LIB, objs):
-        run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)])
+        run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs), "-ldl"])
     # the C++ host mirror of the reference API (mtx.hpp), a plain C++ library over the C ABI
     host_srcs = sorted(HOST.glob("*.cpp"))
     if host_srcs and (not HOST_LIB.exists() or _stale(HOST_LIB, [*host_srcs, *HOST.glob("*.hpp"), LIB, *headers])):

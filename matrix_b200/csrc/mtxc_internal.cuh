@@ -14,6 +14,8 @@
 
 namespace mtxc {
 
+struct CommState;  // comm.cu: the thread's multi-GPU communicator
+
 // ------------------------------------------------------------------------------------------
 // Runtime context: one per host thread, the analogue of the reference's thread-local command
 // buffer and encoder (Mods/GPUManager.h:57-58).
@@ -27,11 +29,14 @@ struct ThreadCtx {
     size_t workspace_bytes = 0;
     bool own_workspace = false;
     int sm_count = 148;
+    CommState* comm = nullptr;           // set by mtxc_comm_init
     std::string last_error;
     cudaStream_t stream() const { return has_user_stream ? user_stream : own_stream; }
 };
 
 ThreadCtx& ctx();
+// Destroys the calling thread's communicator, if any (comm.cu).
+void comm_release();
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t err, const char* what);
 // Checks that mtxc_init ran on this thread; returns MTXC_OK or an error status.

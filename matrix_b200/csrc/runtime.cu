@@ -107,6 +107,7 @@ int mtxc_shutdown(void) {
     ThreadCtx& c = ctx();
     if (c.device < 0) return MTXC_OK;
     cudaSetDevice(c.device);
+    comm_release();
     if (c.own_stream) {
         cudaStreamSynchronize(c.own_stream);
         cudaStreamDestroy(c.own_stream);

@@ -8,7 +8,9 @@
 // elements in registers.  The row maximum and the row sum are reduced per warp (shuffles), per CTA
 // (shared memory) and across the cluster through distributed shared memory: each CTA pushes its
 // partial into a slot of every CTA of the cluster, one cluster barrier later each CTA combines the C
-// slots in rank order from its own shared memory, so all CTAs of a row agree on m and s.
+// slots in rank order from its own shared memory, so all CTAs of a row agree on m and s.  A first
+// cluster barrier (arrive at entry, wait before the first push) guarantees every peer CTA is running
+// before its shared memory is written.
 //
 // Arithmetic follows the trace element by element: m is the reference Max (start from -FLT_MAX, an
 // element replaces it only when strictly greater, so NaN never wins); t = x - m and e = expf(t) are
@@ -87,6 +89,10 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
                                lowest_value<float>());
         }
     }
+    // Distributed shared memory may be written only once every CTA of the cluster is known to be
+    // running.  Every thread arrives here, with its loads still in flight (relaxed: nothing to publish
+    // yet), and waits just before the first push into a peer CTA's shared memory below.
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     float m = lowest_value<float>();
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
@@ -98,6 +104,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads)
     m = warp_max(m);
     if (lane == 0) warp_part[warp] = m;
     __syncthreads();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA of the cluster has started
     if (warp == 0) {
         float w = lane < kThreads / 32 ? warp_part[lane] : lowest_value<float>();
         w = warp_max(w);

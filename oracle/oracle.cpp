@@ -425,6 +425,24 @@ int orc_promote(int a, int b) {
 }
 
 // ---------------------------------------------------------------------------
+// Full Sum of a contiguous tensor: matrix::sum() (Matrix.mm:15215-15218) is flatten(0, -1).sum(0), one
+// output whose run is every element in memory order, summed by the Sum loop (Matrix.mm:15201-15204:
+// acc = 0; acc += x, in T).  The count is 64-bit because benchmark config 5b's 2^32 elements do not fit
+// the reference's 32-bit size_m (its flatten would wrap the extent to 0); the loop is otherwise the
+// reference's, sequential on one thread.
+// ---------------------------------------------------------------------------
+int orc_sum_flat(int dtype, void* out, const void* in, uint64_t n) {
+    const bool ok = with_type(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        const T* p = static_cast<const T*>(in);
+        T acc = static_cast<T>(0);
+        for (uint64_t i = 0; i < n; ++i) acc = add_wrap<T>(acc, p[i]);
+        *static_cast<T*>(out) = acc;
+    });
+    return ok ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------
 // Axis reductions.  op: 0 Sum, 1 Max, 2 Min, 3 ArgMax, 4 ArgMin.
 //   Sum    Matrix.mm:15187-15207   acc = 0; acc += x            (T accumulator)
 //   Max    Matrix.mm:14894-14914   acc = lowest; std::max(acc, x)

@@ -99,6 +99,8 @@ class CpuEval:
         fn("astype", i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
         fn("pointwise_collapse", u32, [U32P, u32, U32P, u32, U32P, U32P])
         fn("pointwise", i32, [i32, i32, vp, C.POINTER(vp), u32, u32, U32P, U32P, u64] + extra)
+        if prefix == "orc_":
+            fn("sum_flat", i32, [i32, vp, vp, u64])
         if prefix == "ref_":
             fn("equal", i32, [i32, vp, vp, vp, u32, U32P, U32P, U32P, U32P, u64])
 
@@ -181,6 +183,19 @@ class CpuEval:
         if rc != 0:
             raise RuntimeError(f"{self.prefix}reduce failed")
         return out[:total].reshape(meta["out_shape"])
+
+    def sum_flat(self, x: np.ndarray, dtype_code=None):
+        """x.sum() for a contiguous x of any size: one sequential sum over every element in memory order
+        (the restatement only; the reference's own loop cannot count past 2^32 - 1 elements)."""
+        if "sum_flat" not in self._f:
+            raise NotImplementedError("sum_flat is the restatement's (port()) only")
+        if not x.flags.c_contiguous:
+            raise ValueError("sum_flat needs a contiguous array")
+        out = np.zeros(1, dtype=x.dtype)
+        code = DTYPES[x.dtype] if dtype_code is None else dtype_code
+        if self._f["sum_flat"](code, out.ctypes.data, x.ctypes.data, x.size) != 0:
+            raise RuntimeError("orc_sum_flat failed")
+        return out[0]
 
     def reduce(self, op, x: np.ndarray, axis: int, keepdims=False, dtype_code=None):
         """x.op(axis, keepdims).eval_cpu() for a (possibly strided) numpy view x.  dtype_code

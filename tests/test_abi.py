@@ -53,6 +53,14 @@ def test_calls_before_init_fail_cleanly():
     assert lib.mtxc_pointwise(0, 0, None, ptrs, 2, 1, arr([4]), arr([], 24)) == _abi.ERR_NOT_INITIALIZED
     assert lib.mtxc_softmax_lastdim(0, None, None, 1, 4, 4, 4) == _abi.ERR_NOT_INITIALIZED
     assert lib.mtxc_sync() == _abi.ERR_NOT_INITIALIZED
+    # the multi-GPU entry points: no device bound, no communicator
+    assert lib.mtxc_comm_init(2, 0, b"\0" * _abi.COMM_ID_BYTES, 0) == _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_reduce_sharded(0, 0, None, None, 1, 4, 1, arr([4]), arr([1]), arr([4]), None) == \
+        _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_allreduce(0, 0, None, 4) == _abi.ERR_NOT_INITIALIZED
+    n, r = C.c_int(-1), C.c_int(-1)
+    assert lib.mtxc_comm_size(C.byref(n), C.byref(r)) == _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_comm_destroy() == 0
     size = C.c_size_t(123)
     assert lib.mtxc_workspace_size(C.byref(size)) == 0 and size.value == 0
 
@@ -136,3 +144,22 @@ def test_every_mixed_pair_has_a_fused_kernel_family():
                 assert d in (0, 4, 3), (a, b, d)  # Float, Int16, Int32
                 third += 1
     assert (own, third) == (40, 26)
+
+
+def test_comm_unique_id_needs_no_gpu():
+    """mtxc_comm_unique_id loads NCCL at run time (no link-time dependency) and draws an id on the host;
+    a buffer shorter than MTXC_COMM_ID_BYTES is refused."""
+    from matrix_b200 import _abi
+
+    lib = _abi.lib()
+    short = C.create_string_buffer(16)
+    assert lib.mtxc_comm_unique_id(short, 16) == _abi.ERR_INVALID_ARGUMENT
+    ids = []
+    for _ in range(2):
+        buf = C.create_string_buffer(_abi.COMM_ID_BYTES)
+        rc = lib.mtxc_comm_unique_id(buf, _abi.COMM_ID_BYTES)
+        assert rc == 0, lib.mtxc_last_error()
+        ids.append(buf.raw)
+    assert ids[0] != ids[1] and any(ids[0])
+    out = subprocess.run(["ldd", str(_abi.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "nccl" not in out

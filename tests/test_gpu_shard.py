@@ -78,6 +78,45 @@ def test_merge_partials_of_simulated_shards(gpu, port, op, dtype):
         assert_bits_equal(m.cpu().numpy(), want, f"merged {op}")
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.int32], ids=["f32", "i32"])
+def test_reduce_sharded_native_one_rank(gpu, port, dtype):
+    """mtxc_reduce_sharded with a one-rank communicator (no NCCL involved): the local kernels, the
+    gather-buffer slots and the merge must give the unsharded reduction; mtxc_allreduce is the identity;
+    a gather buffer too small for the partials is refused with MTXC_ERR_WORKSPACE."""
+    import torch
+
+    from matrix_b200 import _abi
+    from matrix_b200.shard import NativeComm, reduce_sharded
+
+    rng = np.random.default_rng(9)
+    shape = [37, 129, 33]
+    if dtype == np.float32:
+        x = (np.floor(rng.standard_normal(shape) * 4) / 4).astype(np.float32)
+        x[4, 2, :] = np.nan
+    else:
+        x = make_values(rng, int(np.prod(shape)), dtype, "full").reshape(shape)
+    xd = torch.from_numpy(x).cuda()
+    with NativeComm() as comm:
+        assert (comm.world, comm.rank) == (1, 0)
+        for op in ("sum", "max", "min", "argmax", "argmin"):
+            got = reduce_sharded(op, xd, 0, shape[0], comm=comm)
+            gpu.sync()
+            want = port.reduce(op, x, 0)
+            if op == "sum" and dtype == np.float32:
+                x64 = x.astype(np.float64)
+                assert_sum_close(got.cpu().numpy(), want, np.abs(x64).sum(0), "native sum", exact=x64.sum(0))
+            else:
+                assert_bits_equal(got.cpu().numpy(), want, f"native {op}")
+        buf = xd[0].clone().reshape(-1)
+        gpu.allreduce("max", buf)
+        gpu.sync()
+        assert_bits_equal(buf.cpu().numpy(), x[0].reshape(-1), "one-rank allreduce")
+    with NativeComm(buffer_bytes=256) as small:
+        with pytest.raises(_abi.MtxcError) as e:
+            reduce_sharded("sum", xd, 0, shape[0], comm=small)
+        assert e.value.code == _abi.ERR_WORKSPACE
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

@@ -256,3 +256,21 @@ def test_product_broadcast_shapes_and_promotion_match_oracle(port):
         for b in range(13):
             assert L.mtxc_promote_types(a, b) == port.promote(a, b)
     assert L.mtxc_promote_types(13, 0) == -1
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.int32, np.float16, np.uint8])
+def test_flat_sum_matches_reference_loop(port, ref, dtype):
+    """The restatement's full Sum with a 64-bit count (config 5b's 2^32 elements exceed size_m) equals the
+    reference's own Sum loop, run as x.flatten().sum(0), bit for bit wherever the latter can count."""
+    rng = np.random.default_rng(12)
+    for n in (0, 1, 7, 4096, 1 << 20, 3_000_001):
+        if dtype == np.float32:
+            x = rng.standard_normal(n).astype(np.float32)
+        elif dtype == np.float16:
+            x = rng.standard_normal(n).astype(np.float16)
+        else:
+            info = np.iinfo(dtype)
+            x = rng.integers(info.min, info.max, n, dtype=np.int64).astype(dtype)
+        want = ref.reduce("sum", x, 0) if n else np.zeros((), dtype=dtype)
+        got = port.sum_flat(x)
+        assert np.asarray(got).tobytes() == np.asarray(want, dtype=dtype).reshape(()).tobytes(), (n, got, want)
