@@ -80,8 +80,9 @@ enum { MTXC_BINARY_ADD = 0, MTXC_BINARY_SUB = 1, MTXC_BINARY_MUL = 2, MTXC_BINAR
 enum { MTXC_UNARY_EXP = 0, MTXC_UNARY_SQRT = 1 };
 
 /* The make_pointwise family (Matrix.mm:13511-13604): GreaterPrimitive, LessPrimitive,
- * LogicalAndPrimitive, WherePrimitive, FloorPrimitive, FullPrimitive. */
-enum { MTXC_PW_GREATER = 0, MTXC_PW_LESS = 1, MTXC_PW_LOGICAL_AND = 2, MTXC_PW_WHERE = 3, MTXC_PW_FLOOR = 4, MTXC_PW_FULL = 5 };
+ * LogicalAndPrimitive, WherePrimitive, FloorPrimitive, FullPrimitive, Arctan2Primitive, ArcsinPrimitive. */
+enum { MTXC_PW_GREATER = 0, MTXC_PW_LESS = 1, MTXC_PW_LOGICAL_AND = 2, MTXC_PW_WHERE = 3, MTXC_PW_FLOOR = 4, MTXC_PW_FULL = 5,
+       MTXC_PW_ARCTAN2 = 6, MTXC_PW_ARCSIN = 7 };
 
 /* ------------------------------------------------------------------------------------------
  * Runtime.  Replaces GPUManager's device / queue / per-thread command buffer layer
@@ -263,17 +264,24 @@ int mtxc_merge_partials(int op, int dtype, void* dst, int32_t* dst_indices, cons
  * critical loops that cannot afford the device-wide synchronisation cudaMalloc / cudaFree imply, or
  * deployments whose memory budget is fixed up front.  mtxc_reduce needs scratch memory when it splits a
  * reduced axis across CTAs (the per-split partials), and takes it from the thread's workspace, which
- * mtxc_init allocates.  This entry point computes the same reduction, with the same kernels, the same
- * arguments and the same results, but keeps the partials in a statically sized array that is part of
- * the library's device image (MTXC_NOALLOC_SCRATCH_BYTES, 4 MiB; every GPU that loads the library
- * holds it until the process exits).  It calls no allocator: no cudaMalloc, cudaFree or library
- * routine that allocates.  (Call mtxc_init with MTXC_WORKSPACE_MB=0 in the environment to keep the
- * runtime from allocating its own workspace as well.)
+ * mtxc_init allocates.  This entry point computes the same reduction, with the same kernels and the same
+ * arguments, but keeps the partials in a statically sized array that is part of the library's device
+ * image (MTXC_NOALLOC_SCRATCH_BYTES, 4 MiB; every GPU that loads the library holds it until the process
+ * exits).  It calls no allocator: no cudaMalloc, cudaFree or library routine that allocates.  (Call
+ * mtxc_init with MTXC_WORKSPACE_MB=0 in the environment to keep the runtime from allocating its own
+ * workspace as well.)
+ *
+ * Results: identical to mtxc_reduce's whenever mtxc_reduce's workspace holds the same split (the default
+ * 64 MiB workspace always does).  With a smaller workspace mtxc_reduce splits the axis less, so a float
+ * Sum may round differently -- both stay within the float-sum tolerance of the CPU -- while integer sums,
+ * Max / Min and ArgMax / ArgMin are identical whatever the split.
  *
  *   - A reduction whose partials would need more than MTXC_NOALLOC_SCRATCH_BYTES is rejected with
  *     MTXC_ERR_WORKSPACE and a message giving both sizes; mtxc_reduce_workspace_bytes tells in advance.
  *   - The first call on each device looks up the array's device address with that device current
- *     (cudaGetSymbolAddress) and caches it; make that first call before any stream capture.
+ *     (cudaGetSymbolAddress) and caches it; make that first call before any stream capture.  The cache
+ *     assumes the device is not reset behind the library: after a cudaDeviceReset, call mtxc_shutdown
+ *     (which drops the device's cached address) and mtxc_init before the next call.
  *   - All calls on a device share the one array, and it keeps whatever the last call left in it.
  *     Nothing in it has to start at zero (every partial is written before it is read), but calls that
  *     overlap on the GPU -- on different streams or from different threads -- race on it: order them. */
@@ -342,12 +350,26 @@ int mtxc_astype(int dst_dtype, int src_dtype, void* dst, const void* src, uint32
  *   WHERE (Bool cond, a, b of dtype)        -> dtype: cond ? a : b (inputs ordered cond, a, b)
  *   FLOOR (1 input)                         -> dtype: floor for float-likes, identity otherwise
  *   FULL (1 input, the broadcast value)     -> dtype: the value
- * Results are bit-exact with the CPU backends (Matrix.mm:13741-14166).  The output must not exceed
+ *   ARCTAN2 (2 Float inputs)                -> Float: atan2(a, b) (arctan2_backend_cpu, Matrix.mm:13608)
+ *   ARCSIN (1 Float input)                  -> Float: asin(x)     (arcsin_backend_cpu, Matrix.mm:13680)
+ * Results are bit-exact with the CPU backends (Matrix.mm:13741-14166), except ARCTAN2 / ARCSIN, which call
+ * CUDA's atan2f / asinf: within 3 ulp of the CPU's std::atan2 / std::asin (the frontends cast the inputs
+ * to Float first, Matrix.mm:13573-13580).  The output must not exceed
  * 2^32 - 1 elements (make_pointwise's limit).  An empty output needs no call: its collapsed rank is 0,
  * as for a single element, and the reference's backends return before reading anything
  * (`if (!output.total_size) return;`). */
 int mtxc_pointwise(int op, int dtype, void* dst, const void* const* inputs, uint32_t n_inputs, uint32_t cdims,
                    const uint32_t* shape, const uint32_t* strides);
+
+/* matrix::arange(start, stop, step, type) (Matrix.mm:13595-13604) evaluated: dst[i] = start + i * step for
+ * i < count (count = max(0, ceil((stop - start) / step)), computed by the frontend), replacing
+ * arange_backend_gpu (Matrix.mm:14407).  start and step are device pointers to one element of dtype each
+ * (the primitive's two scalar inputs, dtype_cast to the output type); dst is contiguous.  Integers:
+ * (T)((uint64)start + (uint64)i * (uint64)step), wrapping; Float / Float16 / BFloat16:
+ * float(start) + float(i) * float(step) with each operation rounded once (no fused multiply-add), then
+ * rounded to the dtype.  Bit-exact with the CPU backend (Matrix.mm:14167-14180).  Bool:
+ * MTXC_ERR_UNSUPPORTED_DTYPE, as arange refuses it; count > 2^32 - 1: MTXC_ERR_SHAPE. */
+int mtxc_arange(int dtype, void* dst, const void* start, const void* step, uint64_t count);
 
 /* Fused evaluation of the reference's softmax trace over the last axis of contiguous float rows
  *     m = x.max(-1, true); e = matrix::exp(x - m); y = e / e.sum(-1, true)

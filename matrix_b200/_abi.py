@@ -26,7 +26,8 @@ REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
 BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5, "equal": 6}
 UNARY_OPS = {"exp": 0, "sqrt": 1}
 STATS = {"mean": 0, "rms": 1, "norm": 2}
-POINTWISE_OPS = {"greater": 0, "less": 1, "logical_and": 2, "where": 3, "floor": 4, "full": 5}
+POINTWISE_OPS = {"greater": 0, "less": 1, "logical_and": 2, "where": 3, "floor": 4, "full": 5, "arctan2": 6,
+                 "arcsin": 7}
 
 
 class MtxcError(RuntimeError):
@@ -96,6 +97,7 @@ def lib() -> C.CDLL:
             "mtxc_comm_size": (i32, [C.POINTER(i32), C.POINTER(i32)]),
             "mtxc_reduce_sharded": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P, C.POINTER(C.c_int64)]),
             "mtxc_allreduce": (i32, [i32, i32, vp, u64]),
+            "mtxc_arange": (i32, [i32, vp, vp, vp, u64]),
             "mtxc_graph_begin": (i32, []),
             "mtxc_graph_end": (i32, [C.POINTER(vp)]),
             "mtxc_graph_launch": (i32, [vp]),

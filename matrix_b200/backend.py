@@ -302,15 +302,17 @@ def pointwise_meta(shapes, strides) -> PointwiseMeta:
 
 
 def pointwise(op: str, inputs, out: torch.Tensor | None = None, meta: PointwiseMeta | None = None) -> torch.Tensor:
-    """greater / less / logical_and / where / floor / full through mtxc_pointwise.  inputs are device
-    tensors already in their common dtype (where: cond bool, then a and b)."""
+    """greater / less / logical_and / where / floor / full / arctan2 / arcsin through mtxc_pointwise.  inputs
+    are device tensors already in their common dtype (where: cond bool, then a and b; arctan2 / arcsin:
+    float32, as the frontends cast them)."""
     import ctypes
 
     if meta is None:
         meta = pointwise_meta([list(t.shape) for t in inputs], [_check_strides(t) for t in inputs])
     data = inputs[-1]
     code = dtype_code(data.dtype)
-    odt = torch.bool if op in ("greater", "less", "logical_and") else data.dtype
+    odt = (torch.bool if op in ("greater", "less", "logical_and") else
+           torch.float32 if op in ("arctan2", "arcsin") else data.dtype)
     if out is None:
         out = torch.empty(meta.out_shape, dtype=odt, device=data.device)
     if out.numel() == 0:  # the reference's backends return before reading anything
@@ -319,6 +321,17 @@ def pointwise(op: str, inputs, out: torch.Tensor | None = None, meta: PointwiseM
     cshape, cstr = meta.arrays
     check(lib().mtxc_pointwise(_abi.POINTWISE_OPS[op], code, out.data_ptr(), ptrs, len(inputs), meta.cdims, cshape,
                                cstr))
+    return out
+
+
+def arange(start: torch.Tensor, step: torch.Tensor, count: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """matrix::arange evaluated by mtxc_arange: count elements start + i * step; start and step are
+    one-element device tensors of the output dtype (matrix::scalar(start, type), matrix::scalar(step, type))."""
+    if start.dtype != step.dtype or start.numel() != 1 or step.numel() != 1:
+        raise ValueError("arange: start and step are one element each of the output dtype")
+    if out is None:
+        out = torch.empty(count, dtype=start.dtype, device=start.device)
+    check(lib().mtxc_arange(dtype_code(start.dtype), out.data_ptr(), start.data_ptr(), step.data_ptr(), count))
     return out
 
 

@@ -37,6 +37,8 @@ struct ThreadCtx {
 ThreadCtx& ctx();
 // Destroys the calling thread's communicator, if any (comm.cu).
 void comm_release();
+// Drops mtxc_reduce_noalloc's cached scratch address for a device (reduce.cu).
+void noalloc_forget(int device);
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t err, const char* what);
 // Checks that mtxc_init ran on this thread; returns MTXC_OK or an error status.

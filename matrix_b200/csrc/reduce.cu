@@ -1220,6 +1220,9 @@ namespace {
 constexpr int kMaxNoallocDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_address[kMaxNoallocDevices] = {};
+// The size the refusal check compares against: the array's size, lowered only by the test hook
+// mtxc_debug_set_noalloc_limit (not in the public header) so tests can reach the refusal at small sizes.
+std::atomic<size_t> g_noalloc_limit{MTXC_NOALLOC_SCRATCH_BYTES};
 
 // In host code `g_noalloc_scratch` is only a host-side stand-in for the array; handing it to a kernel
 // would fault (or, where the GPU can reach host memory, silently use the wrong memory).  Its device
@@ -1245,6 +1248,14 @@ int noalloc_scratch_address(int device, void** out) {
 
 }  // namespace
 
+// Forgets the cached scratch address of `device` (mtxc_shutdown): a device reset behind the library
+// reloads its device image, so the next first call looks the address up again.
+void mtxc::noalloc_forget(int device) {
+    if (device < 0 || device >= kMaxNoallocDevices) return;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    g_noalloc_address[device] = nullptr;
+}
+
 extern "C" int mtxc_reduce_noalloc(int op, int dtype, void* dst, const void* src, uint32_t reduce_stride,
                                    uint32_t reduce_len, uint32_t cdims, const uint32_t* shape,
                                    const uint32_t* dst_strides, const uint32_t* src_strides) {
@@ -1264,10 +1275,10 @@ extern "C" int mtxc_reduce_noalloc(int op, int dtype, void* dst, const void* src
     if (!known)
         return fail(MTXC_ERR_UNSUPPORTED_DTYPE,
                     std::string("mtxc_reduce_noalloc: no kernel for dtype ") + dtype_name(dtype));
-    if (need > MTXC_NOALLOC_SCRATCH_BYTES)
+    const size_t limit = g_noalloc_limit.load(std::memory_order_relaxed);
+    if (need > limit)
         return fail(MTXC_ERR_WORKSPACE, "mtxc_reduce_noalloc: this reduction splits into " + std::to_string(need) +
-                                            " bytes of partials, more than the " +
-                                            std::to_string(MTXC_NOALLOC_SCRATCH_BYTES) +
+                                            " bytes of partials, more than the " + std::to_string(limit) +
                                             "-byte static scratch; use mtxc_reduce with a workspace");
     void* scratch = nullptr;
     if (need) {
@@ -1308,6 +1319,13 @@ extern "C" int mtxc_reduce_pair(int op, int dtype, void* dst_values, int32_t* ds
     if (!known)
         return fail(MTXC_ERR_UNSUPPORTED_DTYPE, std::string("mtxc_reduce_pair: no kernel for dtype ") + dtype_name(dtype));
     return rc;
+}
+
+// Test hook: the size mtxc_reduce_noalloc's refusal compares against (clamped to the array's size; 0 restores
+// it); returns the previous value.  The array itself keeps its size.
+extern "C" size_t mtxc_debug_set_noalloc_limit(size_t bytes) {
+    const size_t v = bytes == 0 || bytes > MTXC_NOALLOC_SCRATCH_BYTES ? (size_t)MTXC_NOALLOC_SCRATCH_BYTES : bytes;
+    return g_noalloc_limit.exchange(v);
 }
 
 // Test hook: rows per chunk of the packed column fold (clamped to 1 .. 65,535); returns the previous value.

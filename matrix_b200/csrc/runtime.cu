@@ -108,6 +108,7 @@ int mtxc_shutdown(void) {
     if (c.device < 0) return MTXC_OK;
     cudaSetDevice(c.device);
     comm_release();
+    noalloc_forget(c.device);
     if (c.own_stream) {
         cudaStreamSynchronize(c.own_stream);
         cudaStreamDestroy(c.own_stream);

@@ -2,8 +2,10 @@
 #include "mtx.hpp"
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <set>
 
 #include "mtxc.h"
@@ -72,19 +74,25 @@ uint64_t span(const std::vector<size_m>& shape, const std::vector<size_m>& strid
 
 // Allocate-or-adopt the output and fill the tape's cache (primitives.cpp:2866-2882), before the
 // single COMPILE_TRACE return.
-void allocate_output(Primitive& p, matrix& out) {
-    if (!p.out_buffer)
-        p.out_buffer = std::make_shared<Buffer>(std::max<uint64_t>(span(out.shape(), out.strides()), 1) *
-                                                dtype_size(out.type()));
-    out.ensure_buffer(p.out_buffer);
+// Bytes of device memory a node's output needs.
+size_t output_bytes(const matrix& out) {
+    return std::max<uint64_t>(span(out.shape(), out.strides()), 1) * dtype_size(out.type());
 }
 
-// DFS into an input that is still a graph node.
+// Allocate-or-adopt the output and fill the tape's cache (primitives.cpp:2866-2882), before the
+// single COMPILE_TRACE return.  The handle always takes the tape's current buffer: a compiled
+// function rebinds a graph's output to each call's own buffer.
+void allocate_output(Primitive& p, matrix& out) {
+    if (!p.out_buffer) p.out_buffer = std::make_shared<Buffer>(output_bytes(out));
+    out.rebind_buffer(p.out_buffer);
+}
+
+// DFS into an input that is still a graph node; the handle follows the node's current buffer.
 void eval_input(matrix& in, EvalType t) {
     if (in.has_tape()) {
         auto p = in.tape_ptr();
         if (!p->evaluated || t == EvalType::COMPILE_TRACE) p->eval(in, t);
-        in.ensure_buffer(p->out_buffer);
+        in.rebind_buffer(p->out_buffer);
     }
 }
 
@@ -129,6 +137,15 @@ public:
     int axis() const { return axis_; }
     bool keepdims() const { return keepdims_; }
     const matrix& input() const { return input_; }
+    void metadata(uint32_t& cdims, uint32_t& rstride, uint32_t& rlen, uint32_t* shape, uint32_t* s_out,
+                  uint32_t* s_in) const {
+        cdims = cdims_;
+        rstride = rstride_;
+        rlen = rlen_;
+        std::memcpy(shape, shape_, sizeof(shape_));
+        std::memcpy(s_out, s_out_, sizeof(s_out_));
+        std::memcpy(s_in, s_in_, sizeof(s_in_));
+    }
 
 private:
     int op_;
@@ -393,7 +410,104 @@ std::shared_ptr<Primitive> match_softmax(const matrix& y) {
     return std::make_shared<FusedSoftmaxPrimitive>(x);
 }
 
-void fuse_graph(matrix& root) {
+// Max and ArgMax (or Min and ArgMin) of one input, axis and keepdims, evaluated from a single read
+// (mtxc_reduce_pair) when compile() sees both among the roots it compiles together.  The two outputs stay
+// separate nodes (PairOutPrimitive: the value side and the index side) that share this launch.
+class PairOutPrimitive;
+struct ReducePair {
+    int op = MTXC_REDUCE_MAX;  // MAX or MIN
+    matrix input;
+    uint32_t cdims = 0, rstride = 0, rlen = 0;
+    uint32_t shape[MTXC_MAX_DIMS] = {}, s_out[MTXC_MAX_DIMS] = {}, s_in[MTXC_MAX_DIMS] = {};
+    std::weak_ptr<PairOutPrimitive> side[2];  // [0] values, [1] indices
+    size_t side_bytes[2] = {0, 0};
+    std::shared_ptr<Buffer> spare[2];         // for a side whose node no longer exists
+    void run();
+};
+
+class PairOutPrimitive : public Primitive {
+public:
+    PairOutPrimitive(std::shared_ptr<ReducePair> pair, int side) : pair_(std::move(pair)), side_(side) {}
+    void eval(matrix& out, EvalType t) override {
+        eval_input(pair_->input, t);
+        allocate_output(*this, out);
+        if (t == EvalType::COMPILE_TRACE) return;
+        if (evaluated) return;
+        pair_->run();
+    }
+    void clear_trace_checks() override {
+        evaluated = false;
+        if (pair_->input.has_tape()) pair_->input.tape_ptr()->clear_trace_checks();
+    }
+    std::vector<matrix*> inputs() override { return {&pair_->input}; }
+    const char* name() const override {
+        static const char* n[2][2] = {{"PairMax", "PairArgMax"}, {"PairMin", "PairArgMin"}};
+        return n[pair_->op == MTXC_REDUCE_MAX ? 0 : 1][side_];
+    }
+    void extra_bindings(std::vector<const void*>& sig) const override {
+        if (auto other = pair_->side[1 - side_].lock()) sig.push_back(other->out_buffer ? other->out_buffer->ptr : nullptr);
+    }
+
+private:
+    std::shared_ptr<ReducePair> pair_;
+    int side_;
+};
+
+void ReducePair::run() {
+    void* ptrs[2];
+    std::shared_ptr<PairOutPrimitive> nodes[2];
+    for (int k = 0; k < 2; ++k) {
+        nodes[k] = side[k].lock();
+        if (nodes[k] && !nodes[k]->out_buffer) nodes[k]->out_buffer = std::make_shared<Buffer>(side_bytes[k]);
+        if (!nodes[k] && !spare[k]) spare[k] = std::make_shared<Buffer>(side_bytes[k]);
+        ptrs[k] = nodes[k] ? nodes[k]->out_buffer->ptr : spare[k]->ptr;
+    }
+    check(mtxc_reduce_pair(op, (int)input.type(), ptrs[0], static_cast<int32_t*>(ptrs[1]), input.data(), rstride, rlen,
+                           cdims, shape, s_out, s_in),
+          "mtxc_reduce_pair");
+    for (auto& n : nodes)
+        if (n) n->evaluated = true;
+}
+
+bool same_source(const matrix& a, const matrix& b) {
+    if (a.tape() || b.tape()) return a.tape() == b.tape();
+    return a.buffer() && a.buffer() == b.buffer() && a.data() == b.data() && a.shape() == b.shape() &&
+           a.strides() == b.strides() && a.type() == b.type();
+}
+
+// Roots r1 = x.max(axis, k) and r2 = x.argmax(axis, k) (or min / argmin) become the two sides of one
+// ReducePair.
+void fuse_pairs(const std::vector<matrix*>& roots) {
+    for (size_t i = 0; i < roots.size(); ++i) {
+        auto* v = dynamic_cast<const ReducePrimitive*>(roots[i]->tape());
+        if (!v || (v->op() != MTXC_REDUCE_MAX && v->op() != MTXC_REDUCE_MIN)) continue;
+        const int want = v->op() == MTXC_REDUCE_MAX ? MTXC_REDUCE_ARGMAX : MTXC_REDUCE_ARGMIN;
+        for (size_t j = 0; j < roots.size(); ++j) {
+            auto* a = dynamic_cast<const ReducePrimitive*>(roots[j]->tape());
+            if (!a || a->op() != want || a->axis() != v->axis() || a->keepdims() != v->keepdims() ||
+                !same_source(a->input(), v->input()))
+                continue;
+            auto pair = std::make_shared<ReducePair>();
+            pair->op = v->op();
+            pair->input = v->input();
+            v->metadata(pair->cdims, pair->rstride, pair->rlen, pair->shape, pair->s_out, pair->s_in);
+            auto vs = std::make_shared<PairOutPrimitive>(pair, 0);
+            auto is = std::make_shared<PairOutPrimitive>(pair, 1);
+            pair->side[0] = vs;
+            pair->side[1] = is;
+            pair->side_bytes[0] = output_bytes(*roots[i]);
+            pair->side_bytes[1] = output_bytes(*roots[j]);
+            roots[i]->set_tape(vs);
+            roots[j]->set_tape(is);
+            roots[i]->rebind_buffer(nullptr);
+            roots[j]->rebind_buffer(nullptr);
+            break;
+        }
+    }
+}
+
+void fuse_graph(const std::vector<matrix*>& roots) {
+    fuse_pairs(roots);
     std::set<const Primitive*> seen;
     std::function<void(matrix&)> visit = [&](matrix& m) {
         if (!m.has_tape()) return;
@@ -402,7 +516,68 @@ void fuse_graph(matrix& root) {
         if (!seen.insert(p).second) return;
         for (matrix* in : p->inputs()) visit(*in);
     };
-    visit(root);
+    for (matrix* r : roots) visit(*r);
+}
+
+// A compiled function's input (the reference's SwapLeafPrimitive): a leaf whose memory is bound per call
+// (out_buffer: an alias of the caller's input).  It never counts as evaluated, so every consumer's handle
+// follows the current binding.
+class SwapLeafPrimitive : public Primitive {
+public:
+    void eval(matrix& out, EvalType) override {
+        if (!out_buffer) throw std::runtime_error("compiled graph: input is not bound");
+        out.rebind_buffer(out_buffer);
+    }
+    void clear_trace_checks() override {}
+    std::vector<matrix*> inputs() override { return {}; }
+    const char* name() const override { return "SwapLeaf"; }
+};
+
+// arange's generator (ArangePrimitive; backend Matrix.mm:14167-14180, 14407): two one-element inputs
+class ArangePrimitive : public Primitive {
+public:
+    ArangePrimitive(const matrix& start, const matrix& step) : start_(start), step_(step) {}
+    void eval(matrix& out, EvalType t) override {
+        eval_input(start_, t);
+        eval_input(step_, t);
+        allocate_output(*this, out);
+        if (t == EvalType::COMPILE_TRACE) return;
+        if (evaluated) return;
+        evaluated = true;
+        check(mtxc_arange((int)out.type(), out.data(), start_.data(), step_.data(), out.total_size()), "mtxc_arange");
+    }
+    void clear_trace_checks() override { evaluated = false; }
+    std::vector<matrix*> inputs() override { return {&start_, &step_}; }
+    const char* name() const override { return "Arange"; }
+
+private:
+    matrix start_, step_;
+};
+
+void require_pointwise_real(dtype t) {
+    if (t == dtype::Complex64 || (unsigned)t > (unsigned)dtype::UInt64)
+        throw std::invalid_argument("pointwise operation requires a real dtype");
+}
+
+// matrix::scalar<double>(v, t): one element holding static_cast<T>(v) (dtype_cast, matrix.h:260-267)
+matrix scalar_from_double(double v, dtype t) {
+    uint8_t bytes[8] = {};
+    switch (t) {
+        case dtype::Float: { float x = (float)v; std::memcpy(bytes, &x, 4); break; }
+        case dtype::Float16: { _Float16 x = (_Float16)v; std::memcpy(bytes, &x, 2); break; }
+        case dtype::BFloat16: { __bf16 x = (__bf16)v; std::memcpy(bytes, &x, 2); break; }
+        case dtype::UInt8: { uint8_t x = (uint8_t)v; std::memcpy(bytes, &x, 1); break; }
+        case dtype::Int8: { int8_t x = (int8_t)v; std::memcpy(bytes, &x, 1); break; }
+        case dtype::Int16: { int16_t x = (int16_t)v; std::memcpy(bytes, &x, 2); break; }
+        case dtype::UInt16: { uint16_t x = (uint16_t)v; std::memcpy(bytes, &x, 2); break; }
+        case dtype::Int32: { int32_t x = (int32_t)v; std::memcpy(bytes, &x, 4); break; }
+        case dtype::UInt32: { uint32_t x = (uint32_t)v; std::memcpy(bytes, &x, 4); break; }
+        case dtype::Int64: { int64_t x = (int64_t)v; std::memcpy(bytes, &x, 8); break; }
+        case dtype::UInt64: { uint64_t x = (uint64_t)v; std::memcpy(bytes, &x, 8); break; }
+        case dtype::Bool: { bytes[0] = v != 0.0; break; }
+        default: throw std::invalid_argument("scalar: unsupported dtype");
+    }
+    return matrix::from_host(bytes, {}, t);
 }
 
 matrix make_reduce(int op, const matrix& x, int axis, bool keepdims) {
@@ -501,7 +676,10 @@ dtype promote_types(dtype a, dtype b) { return (dtype)mtxc_promote_types((int)a,
 void init(int device) { check(mtxc_init(device), "mtxc_init"); }
 
 Buffer::Buffer(size_t n) : bytes(n) { check(mtxc_alloc(n, &ptr), "mtxc_alloc"); }
-Buffer::~Buffer() { mtxc_free(ptr); }
+Buffer::Buffer(void* alias, size_t n, std::shared_ptr<Buffer> owner) : ptr(alias), bytes(n), owner_(std::move(owner)) {}
+Buffer::~Buffer() {
+    if (!owner_) mtxc_free(ptr);
+}
 
 // ------------------------------------------------------------------------------------------
 // matrix
@@ -552,7 +730,7 @@ matrix matrix::min(int axis, bool keepdims) const { return make_reduce(MTXC_REDU
 matrix matrix::argmax(int axis, bool keepdims) const { return make_reduce(MTXC_REDUCE_ARGMAX, *this, axis, keepdims); }
 matrix matrix::argmin(int axis, bool keepdims) const { return make_reduce(MTXC_REDUCE_ARGMIN, *this, axis, keepdims); }
 
-matrix matrix::sum() const { return flat("sum()").sum(0); }
+matrix matrix::sum() const { return flatten(0, -1).sum(0); }
 
 matrix operator+(const matrix& a, const matrix& b) { return make_binary(MTXC_BINARY_ADD, a, b); }
 matrix operator-(const matrix& a, const matrix& b) { return make_binary(MTXC_BINARY_SUB, a, b); }
@@ -629,18 +807,83 @@ matrix matrix::full(const std::vector<size_m>& shape, const matrix& value, dtype
 matrix matrix::mean(int axis, bool keepdims) const { return make_stat(MTXC_STAT_MEAN, *this, axis, keepdims); }
 matrix matrix::rms(int axis, bool keepdims) const { return make_stat(MTXC_STAT_RMS, *this, axis, keepdims); }
 matrix matrix::norm(int axis, bool keepdims) const { return make_stat(MTXC_STAT_NORM, *this, axis, keepdims); }
-matrix matrix::flat(const char* what) const {
-    // flatten(0, -1): a contiguous (or lazy, hence contiguous) matrix viewed as 1-D
-    if (!contiguous(shape_, strides_)) throw std::runtime_error(std::string(what) + ": flatten needs a contiguous matrix");
-    const uint64_t n = total_size();
-    if (n > 0xFFFFFFFFull) throw std::invalid_argument(std::string(what) + ": more elements than size_m can count");
+matrix matrix::mean() const { return flatten(0, -1).mean(0); }
+matrix matrix::rms() const { return flatten(0, -1).rms(0); }
+matrix matrix::norm() const { return flatten(0, -1).norm(0); }
+
+matrix matrix::sum(int start, int end, bool keepdims) const { return flatten(start, end).sum(start, keepdims); }
+matrix matrix::max(int start, int end, bool keepdims) const { return flatten(start, end).max(start, keepdims); }
+matrix matrix::min(int start, int end, bool keepdims) const { return flatten(start, end).min(start, keepdims); }
+matrix matrix::max() const { return flatten(0, -1).max(0); }
+matrix matrix::min() const { return flatten(0, -1).min(0); }
+
+matrix matrix::arctan2(const matrix& a, const matrix& b) {
+    require_pointwise_real(a.type());
+    require_pointwise_real(b.type());
+    std::vector<matrix> ins{pointwise_cast(a, dtype::Float), pointwise_cast(b, dtype::Float)};
+    return make_pointwise(MTXC_PW_ARCTAN2, ins, pointwise_shape(ins), dtype::Float);
+}
+matrix matrix::arcsin(const matrix& x) {
+    require_pointwise_real(x.type());
+    return make_pointwise(MTXC_PW_ARCSIN, {pointwise_cast(x, dtype::Float)}, x.shape(), dtype::Float);
+}
+matrix matrix::arange(double start, double stop, double step, dtype t) {
+    require_pointwise_real(t);
+    if (t == dtype::Bool) throw std::invalid_argument("arange does not support Bool");
+    if (!std::isfinite(start) || !std::isfinite(stop) || !std::isfinite(step) || step == 0)
+        throw std::invalid_argument("arange requires finite bounds and a finite nonzero step");
+    const double length = std::max(0.0, std::ceil((stop - start) / step));
+    if (!std::isfinite(length) || length > 4294967295.0) throw std::overflow_error("arange exceeds 32-bit indexing");
+    const size_m n = (size_m)length;
+    matrix out;
+    out.set_layout({n}, {1}, t);
+    out.set_tape(std::make_shared<ArangePrimitive>(scalar_from_double(start, t), scalar_from_double(step, t)));
+    return out;
+}
+
+matrix matrix::flatten(int start, int end) const {
+    const int d = (int)dims();
+    if (d == 0) {
+        matrix f = *this;
+        f.set_layout({1}, {1}, type_, offset_);
+        return f;
+    }
+    if (end < 0) end += d;
+    if (start < 0) start += d;
+    if (start < 0 || end >= d || start > end) throw std::invalid_argument("flatten: axes out of range");
+    // the range's non-unit axes must chain (each steps by the extent of the next) to merge as a view; the
+    // last of them gives the merged stride
+    uint64_t merged = 1;
+    std::vector<int> real;
+    for (int i = start; i <= end; ++i) {
+        merged *= shape_[i];
+        if (shape_[i] != 1) real.push_back(i);
+    }
+    if (merged > 0xFFFFFFFFull) throw std::invalid_argument("flatten: more elements than size_m can count");
+    bool adjacent = true;
+    for (size_t k = 0; k + 1 < real.size(); ++k)
+        if ((uint64_t)strides_[real[k]] != (uint64_t)strides_[real[k + 1]] * shape_[real[k + 1]]) adjacent = false;
+    if (merged == 0) adjacent = true;
+    if (!adjacent) {  // the reference's reshape with a new buffer: a contiguous copy first
+        matrix c = astype(type_, true);
+        return c.flatten(start, end);
+    }
+    const size_m stride = real.empty() ? 1 : strides_[real.back()];
+    std::vector<size_m> sh, st;
+    for (int i = 0; i < start; ++i) {
+        sh.push_back(shape_[i]);
+        st.push_back(strides_[i]);
+    }
+    sh.push_back((size_m)merged);
+    st.push_back(stride);
+    for (int i = end + 1; i < d; ++i) {
+        sh.push_back(shape_[i]);
+        st.push_back(strides_[i]);
+    }
     matrix f = *this;
-    f.set_layout({(size_m)n}, {1}, type_, offset_);
+    f.set_layout(sh, st, type_, offset_);
     return f;
 }
-matrix matrix::mean() const { return flat("mean()").mean(0); }
-matrix matrix::rms() const { return flat("rms()").rms(0); }
-matrix matrix::norm() const { return flat("norm()").norm(0); }
 
 namespace {
 matrix evaluated_view_source(const matrix& m) {
@@ -685,48 +928,266 @@ matrix matrix::reshape(const std::vector<size_m>& shape) const {
     return v;
 }
 
-void matrix::eval() {
-    Range range("mtx::eval");
-    if (!tape_) return;
-    if (tape_->evaluated) {
-        ensure_buffer(tape_->out_buffer);
+// ------------------------------------------------------------------------------------------
+// Execution: execute passes recorded per binding
+// ------------------------------------------------------------------------------------------
+struct GraphCache {
+    std::map<std::vector<const void*>, std::shared_ptr<void>> passes;
+};
+
+namespace {
+
+constexpr size_t kMaxRecordedPasses = 8;
+// Set while a pass is being recorded: a compiled function evaluated inside it launches its kernels
+// directly, so they become part of the enclosing recording.
+thread_local bool t_recording = false;
+
+// Every device pointer a pass binds, in DFS order: each node's identity and output buffer (and a fused
+// node's sibling outputs) and each leaf's data.  A recorded pass is valid exactly while these are unchanged.
+void collect_bindings(matrix& m, std::vector<const void*>& sig, std::set<const Primitive*>& seen) {
+    if (!m.has_tape()) {
+        sig.push_back(m.data());
         return;
     }
-    tape_->eval(*this, EvalType::EVAL_INSTANTLY);
-    ensure_buffer(tape_->out_buffer);
-    check(mtxc_sync(), "mtxc_sync");
+    Primitive* p = m.tape_ptr().get();
+    if (!seen.insert(p).second) return;
+    sig.push_back(p);
+    sig.push_back(p->out_buffer ? p->out_buffer->ptr : nullptr);
+    p->extra_bindings(sig);
+    for (matrix* in : p->inputs()) collect_bindings(*in, sig, seen);
 }
 
-void matrix::compile() {
-    Range range("mtx::compile");
-    if (!tape_) return;
-    fuse_graph(*this);
-    tape_->eval(*this, EvalType::COMPILE_TRACE);
-    ensure_buffer(tape_->out_buffer);
-    graph_.reset();
+void eval_roots(const std::vector<matrix*>& roots, EvalType t) {
+    for (matrix* r : roots) {
+        r->tape_ptr()->eval(*r, t);
+        r->rebind_buffer(r->tape_ptr()->out_buffer);
+    }
 }
 
-void matrix::execute() {
-    Range range("mtx::execute");
-    if (!tape_) return;
-    if (!tape_->out_buffer) compile();
-    if (!graph_) {
-        tape_->clear_trace_checks();
+// One execute pass over compiled roots: replays the pass recorded for the current bindings, or records one
+// (up to kMaxRecordedPasses per graph), or -- past that, or inside an enclosing recording -- launches the
+// kernels directly.  A replay therefore never runs with another call's device pointers.
+void run_pass(const std::vector<matrix*>& roots, GraphCache& cache, bool sync) {
+    for (matrix* r : roots) r->tape_ptr()->clear_trace_checks();
+    if (t_recording) {
+        eval_roots(roots, EvalType::EXEC_TRACE);
+        return;
+    }
+    std::vector<const void*> sig;
+    std::set<const Primitive*> seen;
+    for (matrix* r : roots) collect_bindings(*r, sig, seen);
+    auto it = cache.passes.find(sig);
+    if (it == cache.passes.end() && cache.passes.size() < kMaxRecordedPasses) {
         check(mtxc_graph_begin(), "mtxc_graph_begin");
+        t_recording = true;
         try {
-            tape_->eval(*this, EvalType::EXEC_TRACE);
+            eval_roots(roots, EvalType::EXEC_TRACE);
         } catch (...) {
+            t_recording = false;
             void* g = nullptr;
             mtxc_graph_end(&g);
             if (g) mtxc_graph_destroy(g);
             throw;
         }
+        t_recording = false;
         void* g = nullptr;
         check(mtxc_graph_end(&g), "mtxc_graph_end");
-        graph_ = std::shared_ptr<void>(g, [](void* p) { mtxc_graph_destroy(p); });
+        it = cache.passes.emplace(sig, std::shared_ptr<void>(g, [](void* q) { mtxc_graph_destroy(q); })).first;
     }
-    check(mtxc_graph_launch(graph_.get()), "mtxc_graph_launch");
+    if (it != cache.passes.end()) check(mtxc_graph_launch(it->second.get()), "mtxc_graph_launch");
+    else eval_roots(roots, EvalType::EXEC_TRACE);
+    if (sync) check(mtxc_sync(), "mtxc_sync");
+}
+
+std::vector<matrix*> with_tapes(const std::vector<matrix*>& roots) {
+    std::vector<matrix*> rs;
+    for (matrix* r : roots)
+        if (r && r->has_tape()) rs.push_back(r);
+    return rs;
+}
+
+// ------------------------------------------------------------------------------------------
+// Compiled functions (jit_graph_gpu / multi_jit_graph_gpu)
+// ------------------------------------------------------------------------------------------
+struct JitGraph {
+    std::vector<std::shared_ptr<SwapLeafPrimitive>> leaves;
+    std::vector<matrix> samples;  // the layouts callers' inputs must have
+    std::vector<matrix> outputs;  // the compiled roots
+    GraphCache cache;
+};
+
+// One call of a compiled function: its inputs and the nodes of its outputs.
+struct JitCall {
+    std::shared_ptr<JitGraph> g;
+    std::vector<matrix> inputs;
+    std::vector<std::weak_ptr<Primitive>> outs;
+    std::vector<size_t> out_bytes;
+    std::vector<std::shared_ptr<Buffer>> spare;  // for an output whose node no longer exists
+    void run();
+};
+
+// The node a call's output carries (CompiledNodePrimitive / MultiInputCompilePrimitive): evaluating any
+// output of the call runs the compiled graph once for all of them.
+class JitOutputPrimitive : public Primitive {
+public:
+    JitOutputPrimitive(std::shared_ptr<JitCall> call, size_t index) : call_(std::move(call)), index_(index) {}
+    void eval(matrix& out, EvalType t) override {
+        for (matrix& in : call_->inputs) eval_input(in, t);
+        allocate_output(*this, out);
+        if (t == EvalType::COMPILE_TRACE) return;
+        if (evaluated) return;
+        call_->run();
+    }
+    void clear_trace_checks() override {
+        evaluated = false;
+        for (matrix& in : call_->inputs)
+            if (in.has_tape()) in.tape_ptr()->clear_trace_checks();
+    }
+    std::vector<matrix*> inputs() override {
+        std::vector<matrix*> v;
+        for (matrix& in : call_->inputs) v.push_back(&in);
+        return v;
+    }
+    const char* name() const override { return call_->outs.size() == 1 ? "CompiledNode" : "MultiInputCompile"; }
+    void extra_bindings(std::vector<const void*>& sig) const override {
+        for (size_t k = 0; k < call_->outs.size(); ++k)
+            if (k != index_)
+                if (auto n = call_->outs[k].lock()) sig.push_back(n->out_buffer ? n->out_buffer->ptr : nullptr);
+    }
+
+private:
+    std::shared_ptr<JitCall> call_;
+    size_t index_;
+};
+
+void JitCall::run() {
+    // the caller's inputs go to the compiled graph's inputs (primitives.cpp:3938, 4187-4189) ...
+    for (size_t i = 0; i < inputs.size(); ++i) {
+        const matrix& in = inputs[i];
+        const size_t bytes = std::max<uint64_t>(span(in.shape(), in.strides()), 1) * dtype_size(in.type());
+        g->leaves[i]->out_buffer = std::make_shared<Buffer>(in.data(), bytes, in.buffer());
+    }
+    // ... and each owning node of the graph writes straight into the call's output (:3951-3956, 4191-4205)
+    std::vector<std::shared_ptr<Primitive>> nodes(outs.size());
+    if (spare.size() < outs.size()) spare.resize(outs.size());
+    for (size_t k = 0; k < outs.size(); ++k) {
+        nodes[k] = outs[k].lock();
+        std::shared_ptr<Buffer> buf;
+        if (nodes[k]) {
+            if (!nodes[k]->out_buffer) nodes[k]->out_buffer = std::make_shared<Buffer>(out_bytes[k]);
+            buf = nodes[k]->out_buffer;
+        } else {
+            if (!spare[k]) spare[k] = std::make_shared<Buffer>(out_bytes[k]);
+            buf = spare[k];
+        }
+        g->outputs[k].tape_ptr()->out_buffer = buf;
+    }
+    std::vector<matrix*> roots;
+    for (matrix& o : g->outputs) roots.push_back(&o);
+    run_pass(roots, g->cache, false);
+    for (auto& n : nodes)
+        if (n) n->evaluated = true;
+    for (auto& leaf : g->leaves) leaf->out_buffer.reset();  // hold no caller memory between calls
+}
+
+}  // namespace
+
+void matrix::eval() {
+    Range range("mtx::eval");
+    if (!tape_) return;
+    if (tape_->evaluated) {
+        rebind_buffer(tape_->out_buffer);
+        return;
+    }
+    tape_->eval(*this, EvalType::EVAL_INSTANTLY);
+    rebind_buffer(tape_->out_buffer);
     check(mtxc_sync(), "mtxc_sync");
+}
+
+void matrix::compile(const std::vector<matrix*>& roots) {
+    Range range("mtx::compile");
+    const std::vector<matrix*> rs = with_tapes(roots);
+    if (rs.empty()) return;
+    fuse_graph(rs);
+    eval_roots(rs, EvalType::COMPILE_TRACE);
+    auto cache = std::make_shared<GraphCache>();
+    for (matrix* r : rs) r->graphs_ = cache;
+}
+
+void matrix::execute(const std::vector<matrix*>& roots) {
+    Range range("mtx::execute");
+    const std::vector<matrix*> rs = with_tapes(roots);
+    if (rs.empty()) return;
+    bool compiled = true;
+    for (matrix* r : rs) compiled = compiled && r->tape_->out_buffer && r->graphs_;
+    if (!compiled) compile(rs);
+    run_pass(rs, *rs[0]->graphs_, true);
+}
+
+void matrix::compile() { compile(std::vector<matrix*>{this}); }
+void matrix::execute() { execute(std::vector<matrix*>{this}); }
+
+std::function<std::vector<matrix>(const std::vector<matrix>&)> matrix::multi_jit_graph_gpu(
+    std::function<std::vector<matrix>(std::vector<matrix>)> func, const std::vector<matrix>& sample_inputs) {
+    auto g = std::make_shared<JitGraph>();
+    std::vector<matrix> inner;
+    for (const matrix& s0 : sample_inputs) {
+        matrix s = s0;
+        if (s.tape_) s.eval();
+        auto leaf = std::make_shared<SwapLeafPrimitive>();
+        leaf->out_buffer = std::make_shared<Buffer>(
+            s.data(), std::max<uint64_t>(span(s.shape_, s.strides_), 1) * dtype_size(s.type_), s.buffer_);
+        matrix sl;
+        sl.set_layout(s.shape_, s.strides_, s.type_);
+        sl.set_tape(leaf);
+        g->leaves.push_back(leaf);
+        g->samples.push_back(sl);
+        inner.push_back(sl);
+    }
+    g->outputs = func(inner);
+    std::set<const Primitive*> distinct;
+    for (const matrix& o : g->outputs) {
+        // the reference refuses a graph whose output is its input (primitives.cpp:3953-3956)
+        if (!o.tape_ || dynamic_cast<const SwapLeafPrimitive*>(o.tape_.get()))
+            throw std::runtime_error("CompiledNodePrimitive: Head Tail Collision - cannot chop");
+        if (!distinct.insert(o.tape_.get()).second)
+            throw std::invalid_argument("multi_jit_graph_gpu: the outputs must be distinct nodes");
+    }
+    std::vector<matrix*> roots;
+    for (matrix& o : g->outputs) roots.push_back(&o);
+    compile(roots);
+    for (auto& leaf : g->leaves) leaf->out_buffer.reset();  // calls bind their own inputs
+    return [g](const std::vector<matrix>& inputs) -> std::vector<matrix> {
+        if (inputs.size() != g->samples.size())
+            throw std::invalid_argument("compiled function: wrong number of inputs");
+        for (size_t i = 0; i < inputs.size(); ++i) {
+            const matrix& a = inputs[i];
+            const matrix& b = g->samples[i];
+            if (a.shape() != b.shape() || a.strides() != b.strides() || a.type() != b.type())
+                throw std::invalid_argument("compiled function: an input's shape, strides or dtype differ from the sample's");
+        }
+        auto call = std::make_shared<JitCall>();
+        call->g = g;
+        call->inputs = inputs;
+        std::vector<matrix> outs;
+        for (size_t k = 0; k < g->outputs.size(); ++k) {
+            const matrix& o = g->outputs[k];
+            matrix r;
+            r.set_layout(o.shape(), o.strides(), o.type());
+            auto node = std::make_shared<JitOutputPrimitive>(call, k);
+            r.set_tape(node);
+            call->outs.push_back(node);
+            call->out_bytes.push_back(output_bytes(r));
+            outs.push_back(r);
+        }
+        return outs;
+    };
+}
+
+std::function<matrix(const matrix&)> matrix::jit_graph_gpu(std::function<matrix(matrix)> func, matrix sample) {
+    auto multi = multi_jit_graph_gpu([func](std::vector<matrix> in) { return std::vector<matrix>{func(in[0])}; },
+                                     {sample});
+    return [multi](const matrix& input) -> matrix { return multi({input})[0]; };
 }
 
 void matrix::clear_trace_checks() {
@@ -735,7 +1196,7 @@ void matrix::clear_trace_checks() {
 
 std::vector<uint8_t> matrix::to_host_bytes() const {
     matrix m = *this;
-    if (m.tape_ && !m.tape_->evaluated && !m.graph_) m.eval();
+    if (m.tape_ && !m.tape_->evaluated && !m.graphs_) m.eval();
     if (m.tape_) m.ensure_buffer(m.tape_->out_buffer);
     const size_t es = dtype_size(type_);
     std::vector<uint8_t> out(total_size() * es);

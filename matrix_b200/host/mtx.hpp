@@ -11,12 +11,16 @@
 //               matrix::exp / sqrt(x) with promotion to Float16 or wider      (Matrix.mm:6798-6811, 6934-6947)
 //               x.astype(t, make_contig)                                       (Matrix.mm:8384-8398)
 //               matrix::greater / less / logical_and / where / floor / full    (Matrix.mm:13572-13593)
+//               matrix::arctan2 / arcsin / arange                              (Matrix.mm:13573-13604)
+//               x.sum / max / min(start, end, keepdims), x.max(), x.min(), x.flatten(start, end)
 //               matrix::scalar(v, t)                                           (a 0-d matrix holding dtype_cast<t>(v))
 //   primitives  allocate-or-adopt the output, return before computing under COMPILE_TRACE, run once
 //               per pass (`evaluated`), then call the backend (primitives.cpp:2836-2902)
 //   evaluation  eval() = compile + execute in one pass; compile() allocates every output and fuses
-//               the softmax trace; execute() runs kernels only -- the first execute is recorded into a
-//               CUDA graph, later ones replay it (Matrix.mm:8415-8475)
+//               the softmax trace (and Max + ArgMax roots compiled together); execute() runs kernels
+//               only -- recorded into a CUDA graph per binding of device pointers, replayed while the
+//               binding holds (Matrix.mm:8415-8475); jit_graph_gpu / multi_jit_graph_gpu hand each call's
+//               buffers to a compiled graph (Matrix.mm:1076-1149)
 // mean / rms / norm build one fused node (mtxc_reduce_stat: one read of x) whose result and dtype are
 // those of the reference's composition (sum, scalar division, sqrt); the other frontends build the
 // reference's own nodes.
@@ -30,6 +34,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -53,14 +58,19 @@ enum class EvalType { EVAL_AUTO = 0, EVAL_INSTANTLY = 1, COMPILE_TRACE = 2, EXEC
 // Binds the calling thread to a device (mtxc_init); call once per thread before building graphs.
 void init(int device = 0);
 
-// Device memory owned by one or more matrices (the reference's buffer + refCount).
+// Device memory owned by one or more matrices (the reference's buffer + refCount).  An alias refers to
+// memory another Buffer owns (a caller's input handed to a compiled graph) and keeps that owner alive.
 struct Buffer {
     void* ptr = nullptr;
     size_t bytes = 0;
     explicit Buffer(size_t n);
+    Buffer(void* alias, size_t n, std::shared_ptr<Buffer> owner);
     ~Buffer();
     Buffer(const Buffer&) = delete;
     Buffer& operator=(const Buffer&) = delete;
+
+private:
+    std::shared_ptr<Buffer> owner_;  // set for an alias, which frees nothing
 };
 
 class matrix;
@@ -75,7 +85,13 @@ public:
     virtual void clear_trace_checks() = 0;
     virtual std::vector<matrix*> inputs() = 0;
     virtual const char* name() const = 0;
+    // device pointers this node writes besides out_buffer (a fused node's sibling outputs): part of the
+    // binding a recorded pass is keyed on
+    virtual void extra_bindings(std::vector<const void*>&) const {}
 };
+
+// Recorded execute passes of one graph, keyed by every device pointer the pass binds (defined in mtx.cpp).
+struct GraphCache;
 
 class matrix {
 public:
@@ -91,6 +107,17 @@ public:
     matrix argmax(int axis, bool keepdims = false) const;
     matrix argmin(int axis, bool keepdims = false) const;
     matrix sum() const;  // all elements (flatten then sum(0), Matrix.mm:15215-15218)
+    // axes start..end flattened into one and reduced (flatten(start, end).op(start, keepdims):
+    // Matrix.mm:15210-15213, 14917-14920, 15061-15064); max() / min() over all elements (14922-14925,
+    // 15066-15069)
+    matrix sum(int start, int end, bool keepdims = false) const;
+    matrix max(int start, int end, bool keepdims = false) const;
+    matrix min(int start, int end, bool keepdims = false) const;
+    matrix max() const;
+    matrix min() const;
+    // axes start..end merged into one (Matrix.mm:623-657): a view when they are contiguous with each
+    // other, else a contiguous copy first (the reference's reshape with a new buffer)
+    matrix flatten(int start_dim = 0, int end_dim = -1) const;
     matrix mean(int axis, bool keepdims = false) const;
     matrix rms(int axis, bool keepdims = false) const;
     matrix norm(int axis, bool keepdims = false) const;
@@ -116,6 +143,12 @@ public:
     static matrix where(const matrix& cond, const matrix& a, const matrix& b);
     static matrix floor(const matrix& x);
     static matrix full(const std::vector<size_m>& shape, const matrix& value, dtype t);
+    // arctan2(a, b) / arcsin(x) on inputs cast to Float, Float output (Matrix.mm:13573-13580)
+    static matrix arctan2(const matrix& a, const matrix& b);
+    static matrix arcsin(const matrix& x);
+    // max(0, ceil((stop - start) / step)) elements start + i * step of dtype t (Matrix.mm:13595-13604)
+    static matrix arange(double start, double stop, double step = 1, dtype t = dtype::Float);
+    static matrix arange(double stop, dtype t = dtype::Float) { return arange(0, stop, 1, t); }
 
     // views of an evaluated matrix (no copy: new strides / offset over the same buffer)
     matrix transpose(int a, int b) const;
@@ -125,8 +158,22 @@ public:
     // evaluation
     void eval();                // compile + execute in one pass, then synchronise
     void compile();             // allocate every output (COMPILE_TRACE), fuse the softmax trace
-    void execute();             // kernels only; recorded into a CUDA graph the first time, replayed after
+    void execute();             // kernels only; recorded into a CUDA graph per set of bound device
+                                // pointers (first execute with them), replayed while they stay bound
     void clear_trace_checks();  // resets `evaluated` down the graph before re-running a pass
+    // several roots compiled as one graph (fusions across roots: Max + ArgMax, Min + ArgMin of the same
+    // input, axis and keepdims read the input once) and executed as one pass
+    static void compile(const std::vector<matrix*>& roots);
+    static void execute(const std::vector<matrix*>& roots);
+
+    // Compiled functions (Matrix.mm:1076-1149): func is traced once on `sample` (a swap leaf), compiled,
+    // and the returned function builds, per call, a lazy node that hands the caller's input buffer to the
+    // compiled graph's input and the call's own output buffer to the graph's output, then executes the
+    // graph (CompiledNodePrimitive / MultiInputCompilePrimitive, primitives.cpp:3844-4251).  Inputs must
+    // have the samples' shapes, strides and dtypes.  Each call's outputs are distinct buffers.
+    static std::function<matrix(const matrix&)> jit_graph_gpu(std::function<matrix(matrix)> func, matrix sample);
+    static std::function<std::vector<matrix>(const std::vector<matrix>&)> multi_jit_graph_gpu(
+        std::function<std::vector<matrix>(std::vector<matrix>)> func, const std::vector<matrix>& sample_inputs);
 
     // host access (evaluates first)
     std::vector<uint8_t> to_host_bytes() const;
@@ -152,19 +199,19 @@ public:
 
     // used by the primitives
     void ensure_buffer(const std::shared_ptr<Buffer>& adopt);
+    void rebind_buffer(const std::shared_ptr<Buffer>& b) { buffer_ = b; }
     const std::shared_ptr<Buffer>& buffer() const { return buffer_; }
     std::shared_ptr<Primitive> tape_ptr() const { return tape_; }
     void set_tape(std::shared_ptr<Primitive> p) { tape_ = std::move(p); }
     void set_layout(std::vector<size_m> shape, std::vector<size_m> strides, dtype t, uint64_t offset = 0);
 
 private:
-    matrix flat(const char* what) const;  // flatten(0, -1) of a contiguous matrix
     std::shared_ptr<Buffer> buffer_;
     uint64_t offset_ = 0;  // elements
     std::vector<size_m> shape_, strides_;
     dtype type_ = dtype::Float;
     std::shared_ptr<Primitive> tape_;
-    std::shared_ptr<void> graph_;  // the recorded execute pass of the graph rooted here
+    std::shared_ptr<GraphCache> graphs_;  // the recorded execute passes of the graph rooted here
 };
 
 }  // namespace mtx

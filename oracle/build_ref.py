@@ -25,7 +25,7 @@ Pieces taken verbatim (file, anchor; the reference line numbers at the time of w
                      min(a,b) (14764-14781), exp (7014-7063), the sqrt lambda (6878-6925),
                      the equal loop (14522-14538), make_pointwise's collapse (13544-13556), the
                      CPU backends greater / less / logical_and / where / floor / full
-                     (13741-14166)
+                     (13741-14166), arctan2 / arcsin (13608-13738) and arange (14167-14180)
   matrix.h           dtype_cast (260-267), copyCPUinplaceTypeCasted (1474-1544)
   primitives.cpp     ElementwiseDims (6614-6618)
 The member functions are compiled as members of a small stand-in `matrix` struct and stand-in
@@ -376,8 +376,8 @@ uint32_t ref_pointwise_collapse(const uint32_t* out_shape, uint32_t out_dims, co
 
 int ref_pointwise(int op, int dtype_code, void* out, const void* const* inputs, uint32_t n, uint32_t cdims,
                   const uint32_t* shape, const uint32_t* strides, uint64_t total) {
-    static const uint32_t kArity[] = {2, 2, 2, 3, 1, 1};
-    if (op < 0 || op > 5 || n != kArity[op]) return -1;
+    static const uint32_t kArity[] = {2, 2, 2, 3, 1, 1, 2, 1};
+    if (op < 0 || op > 7 || n != kArity[op]) return -1;
     ElementwiseDims cd{};
     cd.dims = cdims;
     for (uint32_t d = 0; d < cdims; ++d) {
@@ -399,9 +399,21 @@ int ref_pointwise(int op, int dtype_code, void* out, const void* const* inputs, 
                 p.cond = in[0]; p.a = in[1]; p.b = in[2]; p.collapsed_dims = cd; o.tape = &p; o.where_backend_cpu(o); break;
             }
             case 4: { FloorPrimitive p; p.input = in[0]; p.collapsed_dims = cd; o.tape = &p; o.floor_backend_cpu(o); break; }
+            case 6: { Arctan2Primitive p; p.a = in[0]; p.b = in[1]; p.collapsed_dims = cd; o.tape = &p; o.arctan2_backend_cpu(o); break; }
+            case 7: { ArcsinPrimitive p; p.input = in[0]; p.collapsed_dims = cd; o.tape = &p; o.arcsin_backend_cpu(o); break; }
             default: { FullPrimitive p; p.value = in[0]; p.collapsed_dims = cd; o.tape = &p; o.full_backend_cpu(o); break; }
         }
     } catch (...) { return -1; }
+    return 0;
+}
+
+int ref_arange(int dtype_code, void* out, const void* start, const void* step, uint64_t count) {
+    matrix s, t, o;
+    s.type = t.type = o.type = (dtype)dtype_code;
+    s.buffer = (void*)start; t.buffer = (void*)step;
+    o.buffer = out; o.total_size = (size_t)count;
+    ArangePrimitive p; p.start = s; p.step = t; o.tape = &p;
+    try { o.arange_backend_cpu(o); } catch (...) { return -1; }
     return 0;
 }
 
@@ -549,6 +561,8 @@ def extract(ref: Path) -> tuple[str, dict]:
         "    void greater_backend_cpu(matrix& output); void less_backend_cpu(matrix& output);\n"
         "    void logical_and_backend_cpu(matrix& output); void where_backend_cpu(matrix& output);\n"
         "    void floor_backend_cpu(matrix& output); void full_backend_cpu(matrix& output);\n"
+        "    void arctan2_backend_cpu(matrix& output); void arcsin_backend_cpu(matrix& output);\n"
+        "    void arange_backend_cpu(matrix& output);\n"
         "};\n"
         "#pragma GCC pop_options\n"
         "struct GreaterPrimitive { matrix a, b; ElementwiseDims collapsed_dims; };\n"
@@ -557,13 +571,19 @@ def extract(ref: Path) -> tuple[str, dict]:
         "struct WherePrimitive { matrix cond, a, b; ElementwiseDims collapsed_dims; };\n"
         "struct FloorPrimitive { matrix input; ElementwiseDims collapsed_dims; };\n"
         "struct FullPrimitive { matrix value; ElementwiseDims collapsed_dims; };\n"
+        "struct Arctan2Primitive { matrix a, b; ElementwiseDims collapsed_dims; };\n"
+        "struct ArcsinPrimitive { matrix input; ElementwiseDims collapsed_dims; };\n"
+        "struct ArangePrimitive { matrix start, step; };\n"
         "struct PointwiseShim { ElementwiseDims collapsed_dims; };\n")
     for key, pat in (("greater_backend_cpu", "void matrix::greater_backend_cpu(matrix& output) {"),
                      ("less_backend_cpu", "void matrix::less_backend_cpu(matrix& output) {"),
                      ("logical_and_backend_cpu", "void matrix::logical_and_backend_cpu(matrix& output) {"),
                      ("where_backend_cpu", "void matrix::where_backend_cpu(matrix& output) {"),
                      ("floor_backend_cpu", "void matrix::floor_backend_cpu(matrix& output) {"),
-                     ("full_backend_cpu", "void matrix::full_backend_cpu(matrix& output) {")):
+                     ("full_backend_cpu", "void matrix::full_backend_cpu(matrix& output) {"),
+                     ("arctan2_backend_cpu", "void matrix::arctan2_backend_cpu(matrix& output) {"),
+                     ("arcsin_backend_cpu", "void matrix::arcsin_backend_cpu(matrix& output) {"),
+                     ("arange_backend_cpu", "void matrix::arange_backend_cpu(matrix& output) {")):
         parts.append(take(matrix_mm, key, matrix_mm.find(pat), False))
 
     wrappers = WRAPPERS

@@ -729,16 +729,18 @@ uint32_t orc_pointwise_collapse(const uint32_t* out_shape, uint32_t out_dims, co
 // ---------------------------------------------------------------------------
 // The make_pointwise family's CPU backends: op 0 greater (Matrix.mm:13803-13874),
 // 1 less (13876-13947), 2 logical_and (13949-14020), 3 where (14022-14103),
-// 4 floor (13741-13801), 5 full (14105-14165).  The output is contiguous and
-// written in order (dst[i++]); input k is read at sum idx * strides[k][axis]
-// (kMaxDims entries per row).  dtype is the inputs' common dtype (Bool for
-// logical_and; the dtype of a and b for where, whose cond is Bool).  Greater,
-// less and logical_and write bool.  cdims == 0 is one element at offset 0.
+// 4 floor (13741-13801), 5 full (14105-14165), 6 arctan2 (13608-13678),
+// 7 arcsin (13680-13738).  The output is contiguous and written in order
+// (dst[i++]); input k is read at sum idx * strides[k][axis] (kMaxDims entries
+// per row).  dtype is the inputs' common dtype (Bool for logical_and; the dtype
+// of a and b for where, whose cond is Bool; Float for arctan2 / arcsin, which
+// write std::atan2(float(a), float(b)) / std::asin(float(x)) as float).
+// Greater, less and logical_and write bool.  cdims == 0 is one element at offset 0.
 // ---------------------------------------------------------------------------
 int orc_pointwise(int op, int dtype, void* out, const void* const* inputs, uint32_t n, uint32_t cdims,
                   const uint32_t* shape, const uint32_t* strides, uint64_t total, int threads) {
-    static const uint32_t kArity[] = {2, 2, 2, 3, 1, 1};
-    if (op < 0 || op > 5 || n != kArity[op] || cdims > kMaxDims) return -1;
+    static const uint32_t kArity[] = {2, 2, 2, 3, 1, 1, 2, 1};
+    if (op < 0 || op > 7 || n != kArity[op] || cdims > kMaxDims) return -1;
     if (op == 2 && dtype != kBool) return -1;
     const bool ok = with_type(dtype, [&](auto* tag) {
         using T = std::remove_pointer_t<decltype(tag)>;
@@ -761,6 +763,13 @@ int orc_pointwise(int op, int dtype, void* out, const void* const* inputs, uint3
                     else if (op == 1) r = x < y;
                     else r = bool(x) && bool(y);
                     static_cast<bool*>(out)[gid] = r;
+                } else if (op == 6) {
+                    const T x = static_cast<const T*>(inputs[0])[offset(gid, 0)];
+                    const T y = static_cast<const T*>(inputs[1])[offset(gid, 1)];
+                    static_cast<float*>(out)[gid] = std::atan2(static_cast<float>(x), static_cast<float>(y));
+                } else if (op == 7) {
+                    const T x = static_cast<const T*>(inputs[0])[offset(gid, 0)];
+                    static_cast<float*>(out)[gid] = std::asin(static_cast<float>(x));
                 } else if (op == 3) {
                     const bool* c = static_cast<const bool*>(inputs[0]);
                     const T* a = static_cast<const T*>(inputs[1]);
@@ -773,6 +782,26 @@ int orc_pointwise(int op, int dtype, void* out, const void* const* inputs, uint3
                 }
             }
         });
+    });
+    return ok ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------
+// arange's CPU backend (Matrix.mm:14167-14180): out[i] = start + i * step in the
+// output type T, for i < count; integers through uint64 arithmetic cast back,
+// float-likes as float(start) + float(i) * float(step) converted by dtype_cast.
+// start and step are one element of T each.  Bool is refused (-1), as arange does.
+// ---------------------------------------------------------------------------
+int orc_arange(int dtype, void* out, const void* start, const void* step, uint64_t count) {
+    if (dtype == kBool) return -1;
+    const bool ok = with_type(dtype, [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        const T a = *static_cast<const T*>(start), b = *static_cast<const T*>(step);
+        T* dst = static_cast<T*>(out);
+        for (uint64_t i = 0; i < count; ++i) {
+            if constexpr (std::is_integral_v<T>) dst[i] = static_cast<T>(uint64_t(a) + uint64_t(i) * uint64_t(b));
+            else dst[i] = cast_elem<T, float>(float(a) + float(i) * float(b));
+        }
     });
     return ok ? 0 : -1;
 }

@@ -40,7 +40,8 @@ STORAGE = {0: np.float32, 1: np.float16, 2: np.uint8, 3: np.int32, 4: np.int16, 
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "argmax": 3, "argmin": 4}
 BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "max": 4, "min": 5, "equal": 6}
 UNARY_OPS = {"exp": 0, "sqrt": 1}
-POINTWISE_OPS = {"greater": 0, "less": 1, "logical_and": 2, "where": 3, "floor": 4, "full": 5}
+POINTWISE_OPS = {"greater": 0, "less": 1, "logical_and": 2, "where": 3, "floor": 4, "full": 5, "arctan2": 6,
+                 "arcsin": 7}
 
 U32P = C.POINTER(C.c_uint32)
 
@@ -99,6 +100,7 @@ class CpuEval:
         fn("astype", i32, [i32, i32, vp, vp, u32, U32P, U32P, U32P, u64] + extra)
         fn("pointwise_collapse", u32, [U32P, u32, U32P, u32, U32P, U32P])
         fn("pointwise", i32, [i32, i32, vp, C.POINTER(vp), u32, u32, U32P, U32P, u64] + extra)
+        fn("arange", i32, [i32, vp, vp, vp, u64])
         if prefix == "orc_":
             fn("sum_flat", i32, [i32, vp, vp, u64])
         if prefix == "ref_":
@@ -317,12 +319,14 @@ class CpuEval:
         return dict(out_shape=shape, cdims=k, shape=cshape, strides=cstr)
 
     def pointwise(self, op, inputs, dtype_code=None):
-        """greater / less / logical_and / where / floor / full over numpy views already cast to their
-        common dtype (cond of where: bool).  Returns the contiguous output."""
+        """greater / less / logical_and / where / floor / full / arctan2 / arcsin over numpy views already
+        cast to their common dtype (cond of where: bool; Float for arctan2 / arcsin).  Returns the
+        contiguous output."""
         meta = self.pointwise_meta(inputs)
         total = int(np.prod(meta["out_shape"], dtype=np.int64)) if meta["out_shape"] else 1
         data = inputs[-1]
-        odt = np.bool_ if op in ("greater", "less", "logical_and") else data.dtype
+        odt = (np.bool_ if op in ("greater", "less", "logical_and") else
+               np.float32 if op in ("arctan2", "arcsin") else data.dtype)
         out = np.zeros(max(total, 1), dtype=odt)
         code = DTYPES[data.dtype] if dtype_code is None else dtype_code
         if op == "logical_and":
@@ -343,6 +347,18 @@ class CpuEval:
                 raise RuntimeError(f"{self.prefix}pointwise failed")
         return out[:total].reshape(meta["out_shape"])
 
+
+    def arange(self, start, step, count: int, dtype, dtype_code=None):
+        """arange's CPU backend: count elements start + i * step of `dtype` (start and step already
+        converted to it, as matrix::scalar does)."""
+        dt = np.dtype(dtype)
+        a = np.array([start], dtype=dt)
+        b = np.array([step], dtype=dt)
+        out = np.zeros(max(count, 1), dtype=dt)
+        code = DTYPES.get(dt, -1) if dtype_code is None else dtype_code
+        if self._f["arange"](code, out.ctypes.data, a.ctypes.data, b.ctypes.data, count) != 0:
+            raise ValueError(f"{self.prefix}arange refused dtype {dt}")
+        return out[:count]
 
     # -- mean / rms / norm: the reference's compositions (Matrix.mm:15220-15276) ------------
     def _scalar_type(self, value: float, code: int) -> int:

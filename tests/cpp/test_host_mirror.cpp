@@ -23,6 +23,8 @@ int orc_reduce(int, int, void*, const void*, uint32_t, uint32_t, uint32_t, const
                const uint32_t*, uint64_t, int);
 int orc_broadcast(int, int, void*, const void*, const void*, uint32_t, const uint32_t*, const uint32_t*, const uint32_t*,
                   uint64_t, int);
+int orc_arange(int, void*, const void*, const void*, uint64_t);
+int orc_sum_flat(int, void*, const void*, uint64_t);
 }
 
 using mtx::dtype;
@@ -412,6 +414,232 @@ static void test_promotion_and_pointwise(std::mt19937& rng) {
            "int32 norm: sqrt of the wrapped sum of wrapped squares");
 }
 
+// Compiled functions (jit_graph_gpu / multi_jit_graph_gpu): every call hands its own input and output
+// buffers to the compiled graph, so calls with different buffers -- including more distinct bindings
+// than the executor records, and calls inside a larger expression -- each compute their own result.
+static void test_jit(std::mt19937& rng) {
+    const std::vector<size_m> shape = {32, 2048};
+    std::normal_distribution<float> d(0.f, 2.f);
+    auto fill = [&](std::vector<float>& v) {
+        for (auto& x : v) x = d(rng);
+    };
+    auto softmax_ref = [&](const std::vector<float>& h) {
+        std::vector<float> y(h.size());
+        for (size_t r = 0; r < shape[0]; ++r) {
+            const float* row = &h[r * shape[1]];
+            float m = -3.4e38f;
+            for (size_t c = 0; c < shape[1]; ++c) m = (m < row[c]) ? row[c] : m;
+            double s = 0;
+            for (size_t c = 0; c < shape[1]; ++c) s += std::exp((double)row[c] - m);
+            for (size_t c = 0; c < shape[1]; ++c) y[r * shape[1] + c] = (float)(std::exp((double)row[c] - m) / s);
+        }
+        return y;
+    };
+    auto close = [](const std::vector<float>& g, const std::vector<float>& c) {
+        if (g.size() != c.size()) return false;
+        for (size_t i = 0; i < g.size(); ++i)
+            if (!(std::fabs(g[i] - c[i]) <= 1e-5f * std::fabs(c[i]) + 1e-30f)) return false;
+        return true;
+    };
+    std::vector<float> h0(total(shape)), h1(total(shape)), h2(total(shape));
+    fill(h0);
+    fill(h1);
+    fill(h2);
+    matrix sample = matrix::from_host(h0.data(), shape, dtype::Float);
+    auto f = matrix::jit_graph_gpu(
+        [](matrix in) {
+            matrix m = in.max(-1, true);
+            matrix e = matrix::exp(in - m);
+            return e / e.sum(-1, true);
+        },
+        sample);
+    matrix x1 = matrix::from_host(h1.data(), shape, dtype::Float);
+    matrix x2 = matrix::from_host(h2.data(), shape, dtype::Float);
+    matrix y1 = f(x1);
+    EXPECT(std::string(y1.tape()->name()) == "CompiledNode", "a call builds a CompiledNode");
+    y1.eval();
+    matrix y2 = f(x2);
+    y2.eval();
+    EXPECT(y1.data() != y2.data(), "each call has its own output buffer");
+    EXPECT(close(y1.to_host<float>(), softmax_ref(h1)), "jit call 1 reads its own input");
+    EXPECT(close(y2.to_host<float>(), softmax_ref(h2)), "jit call 2 reads its own input");
+    // more distinct bindings than the executor records (8): the later calls launch directly
+    bool all = true;
+    std::vector<matrix> keep;
+    for (int k = 0; k < 12; ++k) {
+        matrix y = f(k % 2 ? x2 : x1);
+        y.eval();
+        keep.push_back(y);
+    }
+    for (int k = 0; k < 12; ++k) all = all && close(keep[k].to_host<float>(), softmax_ref(k % 2 ? h2 : h1));
+    EXPECT(all, "twelve calls alternating two inputs, each into its own output");
+    EXPECT(close(y1.to_host<float>(), softmax_ref(h1)), "an earlier call's output is left alone");
+    // a lazy input and a call inside a larger compiled expression, executed twice with new leaf contents
+    std::vector<float> bias(shape[1], 0.5f);
+    matrix b = matrix::from_host(bias.data(), {1, shape[1]}, dtype::Float);
+    matrix z = f(x1 + b) * matrix::scalar(2.0f, dtype::Float);
+    z.compile();
+    z.execute();
+    auto expect_z = [&](const std::vector<float>& h) {
+        std::vector<float> hb(h.size());
+        for (size_t i = 0; i < h.size(); ++i) hb[i] = h[i] + 0.5f;
+        std::vector<float> y = softmax_ref(hb);
+        for (auto& v : y) v *= 2.0f;
+        return y;
+    };
+    EXPECT(close(z.to_host<float>(), expect_z(h1)), "jit call inside a compiled expression");
+    fill(h1);
+    x1.upload(h1.data());
+    z.execute();
+    EXPECT(close(z.to_host<float>(), expect_z(h1)), "the enclosing expression replayed on new contents");
+
+    // multi-output: Max and ArgMax of one input fuse into one read
+    const std::vector<size_m> qs = {16, 300, 96};
+    std::vector<float> q0 = random_ties(total(qs), rng), q1 = random_ties(total(qs), rng);
+    q1[7] = NAN;
+    matrix qsample = matrix::from_host(q0.data(), qs, dtype::Float);
+    auto g = matrix::multi_jit_graph_gpu(
+        [](std::vector<matrix> in) { return std::vector<matrix>{in[0].max(1), in[0].argmax(1), in[0].min(1)}; },
+        {qsample});
+    for (const auto* hq : {&q0, &q1}) {
+        matrix qx = matrix::from_host(hq->data(), qs, dtype::Float);
+        std::vector<matrix> r = g({qx});
+        EXPECT(r.size() == 3 && std::string(r[0].tape()->name()) == "MultiInputCompile", "multi-output call");
+        r[1].eval();  // evaluating one output runs the compiled graph for all three
+        const std::vector<size_m> st = row_major(qs);
+        EXPECT(same_bits_f32(r[0].to_host_bytes(), oracle_reduce(1, *hq, qs, st, 1, false, 0)), "jit max");
+        EXPECT(r[1].to_host_bytes() == oracle_reduce(3, *hq, qs, st, 1, false, 0), "jit argmax (fused with max)");
+        EXPECT(same_bits_f32(r[2].to_host_bytes(), oracle_reduce(2, *hq, qs, st, 1, false, 0)), "jit min");
+    }
+    // the same fusion for roots compiled together without a jit
+    matrix qx = matrix::from_host(q1.data(), qs, dtype::Float);
+    matrix mx = qx.max(1), am = qx.argmax(1);
+    matrix::compile({&mx, &am});
+    EXPECT(std::string(mx.tape()->name()) == "PairMax" && std::string(am.tape()->name()) == "PairArgMax",
+           "compile() of max + argmax roots fuses them");
+    matrix::execute({&mx, &am});
+    EXPECT(same_bits_f32(mx.to_host_bytes(), oracle_reduce(1, q1, qs, row_major(qs), 1, false, 0)), "fused max");
+    EXPECT(am.to_host_bytes() == oracle_reduce(3, q1, qs, row_major(qs), 1, false, 0), "fused argmax");
+
+    // the reference's refusals
+    bool threw = false;
+    try {
+        matrix::jit_graph_gpu([](matrix in) { return in; }, sample);
+    } catch (const std::runtime_error&) {
+        threw = true;
+    }
+    EXPECT(threw, "a graph whose output is its input is refused (head-tail collision)");
+    threw = false;
+    try {
+        f(matrix::from_host(h1.data(), {shape[1], shape[0]}, dtype::Float));
+    } catch (const std::invalid_argument&) {
+        threw = true;
+    }
+    EXPECT(threw, "an input whose layout differs from the sample's is refused");
+}
+
+// Ranged and global reductions (flatten(start, end).op(start, keepdims)), flatten's copy of a
+// non-contiguous range, the arange generator, arctan2 / arcsin
+static void test_ranged_and_generators(std::mt19937& rng) {
+    const std::vector<size_m> shape = {6, 7, 33, 5};
+    std::vector<float> host = random_ties(total(shape), rng);
+    host[11] = NAN;
+    matrix x = matrix::from_host(host.data(), shape, dtype::Float);
+    // x.sum(1, 2) == x.flatten(1, 2).sum(1): the oracle reduces the same data viewed as [6, 231, 5]
+    const std::vector<size_m> fl = {6, 7 * 33, 5};
+    matrix s = x.sum(1, 2);
+    EXPECT(s.shape() == std::vector<size_m>({6, 5}), "sum(1, 2) shape");
+    std::vector<uint8_t> want = oracle_reduce(0, host, fl, row_major(fl), 1, false, 0);
+    std::vector<float> g = s.to_host<float>(), w(want.size() / 4);
+    std::memcpy(w.data(), want.data(), want.size());
+    bool ok = g.size() == w.size();
+    for (size_t i = 0; ok && i < g.size(); ++i) ok = (std::isnan(g[i]) && std::isnan(w[i])) || std::fabs(g[i] - w[i]) <= 1e-3f;
+    EXPECT(ok, "sum(1, 2)");
+    matrix mk = x.max(0, 1, true);
+    const std::vector<size_m> f01 = {42, 33, 5};
+    EXPECT(mk.shape() == std::vector<size_m>({1, 33, 5}), "max(0, 1, keepdims) shape");
+    EXPECT(same_bits_f32(mk.to_host_bytes(), oracle_reduce(1, host, f01, row_major(f01), 0, true, 0)), "max(0, 1, keepdims)");
+    matrix mn = x.min(2, 3);
+    const std::vector<size_m> f23 = {6, 7, 165};
+    EXPECT(same_bits_f32(mn.to_host_bytes(), oracle_reduce(2, host, f23, row_major(f23), 2, false, 0)), "min(2, 3)");
+    const std::vector<size_m> all = {(size_m)total(shape)};
+    EXPECT(same_bits_f32(x.max().to_host_bytes(), oracle_reduce(1, host, all, {1}, 0, false, 0)), "max()");
+    EXPECT(same_bits_f32(x.min().to_host_bytes(), oracle_reduce(2, host, all, {1}, 0, false, 0)), "min()");
+    // a transposed view: axes 0..1 of [7, 6, 33, 5] do not chain, so flatten copies first
+    matrix xt = x.transpose(0, 1);
+    std::vector<float> ht(host.size());
+    for (size_t a = 0; a < 6; ++a)
+        for (size_t b = 0; b < 7; ++b)
+            for (size_t r = 0; r < 33 * 5; ++r) ht[(b * 6 + a) * 165 + r] = host[(a * 7 + b) * 165 + r];
+    matrix ft = xt.max(0, 1);
+    EXPECT(same_bits_f32(ft.to_host_bytes(), oracle_reduce(1, ht, f01, row_major(f01), 0, false, 0)),
+           "max(0, 1) of a transposed view (flatten copies)");
+    // integers: the global sum wraps like the reference's T accumulator
+    std::vector<int32_t> hi(total(shape));
+    std::uniform_int_distribution<int32_t> di(-(1 << 30), 1 << 30);
+    for (auto& v : hi) v = di(rng);
+    matrix xi = matrix::from_host(hi.data(), shape, dtype::Int32);
+    int32_t wsum = 0;
+    orc_sum_flat(3, &wsum, hi.data(), hi.size());
+    EXPECT(xi.sum().to_host<int32_t>()[0] == wsum, "int32 sum() wraps as the reference's loop");
+
+    // arange: float, half, integers with negative steps; Bool refused; the empty range
+    struct Case { double a, b, c; dtype t; int code; };
+    const Case cases[] = {{0, 10, 1, dtype::Float, 0}, {-3.5, 1000, 0.1, dtype::Float, 0}, {0, 300, 0.5, dtype::Float16, 1},
+                          {5, -100, -3, dtype::Int32, 3}, {3, 250, 1, dtype::UInt8, 2}, {250, 0, -1, dtype::Int16, 4},
+                          {0, 1e6, 7, dtype::Int64, 11}, {1, 1, 1, dtype::Float, 0}};
+    for (const Case& c : cases) {
+        matrix r = matrix::arange(c.a, c.b, c.c, c.t);
+        const uint64_t n = r.total_size();
+        EXPECT(n == (uint64_t)std::max(0.0, std::ceil((c.b - c.a) / c.c)), "arange length");
+        std::vector<uint8_t> got = r.to_host_bytes();
+        const size_t es = mtx::dtype_size(c.t);
+        std::vector<uint8_t> a(8), st(8), exp(std::max<uint64_t>(n, 1) * es);
+        switch (c.t) {
+            case dtype::Float: { float u = (float)c.a, v = (float)c.c; std::memcpy(a.data(), &u, 4); std::memcpy(st.data(), &v, 4); break; }
+            case dtype::Float16: { _Float16 u = (_Float16)c.a, v = (_Float16)c.c; std::memcpy(a.data(), &u, 2); std::memcpy(st.data(), &v, 2); break; }
+            case dtype::Int32: { int32_t u = (int32_t)c.a, v = (int32_t)c.c; std::memcpy(a.data(), &u, 4); std::memcpy(st.data(), &v, 4); break; }
+            case dtype::UInt8: { uint8_t u = (uint8_t)c.a, v = (uint8_t)c.c; std::memcpy(a.data(), &u, 1); std::memcpy(st.data(), &v, 1); break; }
+            case dtype::Int16: { int16_t u = (int16_t)c.a, v = (int16_t)c.c; std::memcpy(a.data(), &u, 2); std::memcpy(st.data(), &v, 2); break; }
+            default: { int64_t u = (int64_t)c.a, v = (int64_t)c.c; std::memcpy(a.data(), &u, 8); std::memcpy(st.data(), &v, 8); break; }
+        }
+        orc_arange(c.code, exp.data(), a.data(), st.data(), n);
+        exp.resize(n * es);
+        EXPECT(got == exp, "arange(%g, %g, %g) bit-exact", c.a, c.b, c.c);
+    }
+    bool threw = false;
+    try {
+        matrix::arange(0, 4, 1, dtype::Bool);
+    } catch (const std::invalid_argument&) {
+        threw = true;
+    }
+    EXPECT(threw, "arange refuses Bool");
+
+    // arctan2 (a broadcast operand) and arcsin, against the C library within 3 ulp
+    std::vector<float> ya(64 * 33), xb(33);
+    std::normal_distribution<float> d(0.f, 3.f);
+    for (auto& v : ya) v = d(rng);
+    for (auto& v : xb) v = d(rng);
+    matrix A = matrix::from_host(ya.data(), {64, 33}, dtype::Float), B = matrix::from_host(xb.data(), {33}, dtype::Float);
+    std::vector<float> at = matrix::arctan2(A, B).to_host<float>();
+    std::vector<float> as = matrix::arcsin(A * matrix::scalar(0.3f, dtype::Float)).to_host<float>();
+    auto ulps = [](float p, float q) {
+        int32_t i, j;
+        std::memcpy(&i, &p, 4);
+        std::memcpy(&j, &q, 4);
+        return std::abs((int64_t)i - (int64_t)j);
+    };
+    bool at_ok = at.size() == ya.size(), as_ok = as.size() == ya.size();
+    for (size_t i = 0; at_ok && i < at.size(); ++i) at_ok = ulps(at[i], std::atan2(ya[i], xb[i % 33])) <= 3;
+    for (size_t i = 0; as_ok && i < as.size(); ++i) {
+        const float w2 = std::asin(ya[i] * 0.3f);
+        as_ok = (std::isnan(as[i]) && std::isnan(w2)) || ulps(as[i], w2) <= 3;
+    }
+    EXPECT(at_ok, "arctan2 with a broadcast operand");
+    EXPECT(as_ok, "arcsin");
+    EXPECT(matrix::arctan2(xi, xi).type() == dtype::Float, "arctan2 of Int32 inputs casts them to Float");
+}
+
 int main() {
     mtx::init(0);
     std::mt19937 rng(1234);
@@ -419,6 +647,8 @@ int main() {
     test_binary(rng);
     test_trace(rng);
     test_promotion_and_pointwise(rng);
+    test_jit(rng);
+    test_ranged_and_generators(rng);
     std::printf("host mirror: %d checks, %d failures\n", checks, failures);
     return failures ? 1 : 0;
 }

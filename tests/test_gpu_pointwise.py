@@ -186,3 +186,87 @@ def test_pointwise_errors(gpu):
     assert e.value.code == _abi.ERR_UNSUPPORTED_DTYPE
     with pytest.raises(_abi.MtxcError):
         gpu.astype(torch.zeros(4, dtype=torch.complex64, device="cuda"), torch.float32)
+
+
+ATAN2_ASIN_ULP = 3  # CUDA's atan2f / asinf against glibc's float atan2 / asin (the oracle's std:: calls)
+
+
+def _on_device(view: np.ndarray, base: np.ndarray, base_dev):
+    """The device tensor with `view`'s shape, strides and offset over base_dev (a copy of base)."""
+    import torch
+
+    off = (view.__array_interface__["data"][0] - base.__array_interface__["data"][0]) // view.itemsize
+    return torch.as_strided(base_dev, view.shape, [st // view.itemsize for st in view.strides], off)
+
+
+def test_arctan2_and_arcsin(gpu, port):
+    """arctan2 / arcsin (Float inputs, as the frontends cast them; Matrix.mm:13573-13580): CUDA's atan2f /
+    asinf against the CPU backends' std::atan2 / std::asin, within ATAN2_ASIN_ULP ulp, NaN where the CPU has
+    NaN.  Special values: signed zeros, infinities, NaN, |x| > 1.  Row-broadcast, strided, transposed and
+    single-element layouts."""
+    import torch
+
+    rng = np.random.default_rng(31)
+    a = (rng.standard_normal((257, 1024)) * 5).astype(np.float32)
+    b = (rng.standard_normal((1024,)) * 5).astype(np.float32)
+    a[0, :10] = [0.0, -0.0, 0.0, -0.0, np.inf, -np.inf, np.nan, 1.0, np.inf, -1e-30]
+    b[:10] = [0.0, 0.0, -0.0, -0.0, np.inf, np.inf, 1.0, np.nan, -np.inf, 1e-30]
+    ad, bd = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    cases = [((a, a, ad), (b, b, bd)), ((a[:, ::3], a, ad), (b[::3], b, bd)),
+             ((a.T[:7], a, ad), (a.T[7:14], a, ad)), ((a[:1, :1], a, ad), (b[:1], b, bd))]
+    for (x, xb, xbd), (y, yb, ybd) in cases:
+        got = gpu.pointwise("arctan2", [_on_device(x, xb, xbd), _on_device(y, yb, ybd)])
+        gpu.sync()
+        want = port.pointwise("arctan2", [x, y])
+        g = got.cpu().numpy()
+        assert g.shape == want.shape
+        assert ulp_distance(g, want).max() <= ATAN2_ASIN_ULP, "arctan2 beyond the ulp bound"
+        assert np.array_equal(np.isnan(g), np.isnan(want))
+    x = rng.uniform(-1.25, 1.25, (513, 777)).astype(np.float32)
+    x[0, :8] = [1.0, -1.0, 0.0, -0.0, np.nan, np.inf, 1.0000001, -0.9999999]
+    xd = torch.from_numpy(x).cuda()
+    for v in (x, x[:, 1::2], x[5]):
+        got = gpu.pointwise("arcsin", [_on_device(v, x, xd)]).cpu().numpy()
+        want = port.pointwise("arcsin", [v])
+        assert ulp_distance(got, want).max() <= ATAN2_ASIN_ULP, "arcsin beyond the ulp bound"
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        zero = (got == 0) & (want == 0)
+        assert np.array_equal(np.signbit(got[zero]), np.signbit(want[zero]))
+
+
+@pytest.mark.parametrize("code", [c for c in ALL_CODES if c != 7])
+def test_arange(gpu, port, code):
+    """arange (Matrix.mm:13595-13604, backend 14167-14180): bit-exact against the oracle for every dtype
+    but Bool, incl. negative and fractional steps, wrapping integers, float rounding past 2^24 elements, an
+    empty and a one-element range, and an output that is not 16-byte aligned."""
+    import torch
+
+    from matrix_b200 import _abi
+    from tests.test_oracle_pin_pointwise import bf16_bits
+
+    def scalars(start, step):
+        if code in (0, 1, 10):
+            s32 = np.array([start, step], dtype=np.float32)
+            if code == 0:
+                return s32
+            if code == 1:
+                return s32.astype(np.float16)
+            return bf16_bits(s32)
+        return np.array([int(start), int(step)], dtype=np.int64).astype(STORAGE[code])
+
+    cases = [(0, 1, 0), (0, 1, 1), (3, 2, 1000), (-7, 3, 4099), (100, -1, 300), (0.5, 0.25, 70000),
+             (-1e3, 0.1, 20001), (1, 7, (1 << 25) + 3)]
+    for start, step, n in cases:
+        sv = scalars(start, step)
+        want = port.arange(sv[0], sv[1], n, STORAGE[code], dtype_code=code)
+        st = dev(sv, code)
+        for offset in (0, 1):
+            out = torch.empty(n + offset, dtype=torch_dtype(code), device="cuda")[offset:]
+            gpu.arange(st[0:1], st[1:2], n, out=out)
+            gpu.sync()
+            assert_bits_equal(comparable(host(out, code), code), comparable(want, code),
+                              f"arange {code} {start} {step} {n} offset {offset}")
+    b = torch.ones(2, dtype=torch.bool, device="cuda")
+    with pytest.raises(_abi.MtxcError) as e:
+        gpu.arange(b[0:1], b[1:2], 4)
+    assert e.value.code == _abi.ERR_UNSUPPORTED_DTYPE

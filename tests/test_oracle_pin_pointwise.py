@@ -216,3 +216,47 @@ def test_stat_output_dtypes(port):
                 _, oc = port.stat(kind, x, 1, dtype_code=code)
                 assert L.mtxc_reduce_stat_dtype(k, code, n) == oc, (code, n, kind)
     assert L.mtxc_reduce_stat_dtype(0, 9, 4) == -1 and L.mtxc_reduce_stat_dtype(3, 0, 4) == -1
+
+
+def test_arctan2_and_arcsin_match_reference(port, ref):
+    """arctan2 / arcsin (inputs cast to Float by the frontend): the restatement's loops equal the
+    reference's own backends (std::atan2 / std::asin in float), incl. zeros, infinities, NaN and |x| > 1."""
+    rng = np.random.default_rng(21)
+    a = (rng.standard_normal((33, 65)) * 3).astype(np.float32)
+    b = (rng.standard_normal((65,)) * 3).astype(np.float32)
+    a[0, :8] = [0.0, -0.0, 0.0, -0.0, np.inf, -np.inf, np.nan, 1.0]
+    b[:8] = [0.0, 0.0, -0.0, -0.0, np.inf, np.inf, 1.0, np.nan]
+    for x, y in ((a, b), (a[:, ::2], b[::2]), (a.T.copy()[:5], a.T.copy()[5:10])):
+        got, want = port.pointwise("arctan2", [x, y]), ref.pointwise("arctan2", [x, y])
+        assert got.dtype == np.float32 and got.tobytes() == want.tobytes()
+    x = rng.uniform(-1.2, 1.2, (7, 300)).astype(np.float32)
+    x[0, :6] = [1.0, -1.0, 0.0, -0.0, np.nan, np.inf]
+    for v in (x, x[:, 1::3], x[3]):
+        assert port.pointwise("arcsin", [v]).tobytes() == ref.pointwise("arcsin", [v]).tobytes()
+
+
+@pytest.mark.parametrize("code", [0, 1, 2, 3, 4, 5, 6, 8, 10, 11, 12])
+def test_arange_matches_reference(port, ref, code):
+    """arange's generator (integers through uint64 arithmetic, float-likes as float(start) + float(i) *
+    float(step) without contraction) equals the reference's arange_backend_cpu for every dtype but Bool,
+    which the reference's frontend refuses (Matrix.mm:13597) and the restatement with it."""
+    dt = STORAGE[code]
+    cases = [(0, 1, 0), (0, 1, 1), (3, 2, 1000), (-7, 3, 4099), (100, -1, 300), (0.5, 0.25, 70000),
+             (-1e3, 0.1, 20001), (1, 7, 1 << 20)]
+    for start, step, n in cases:
+        if code in (0, 1, 10):
+            s32, t32 = np.float32(start), np.float32(step)
+            if code == 0:
+                s, t = s32, t32
+            elif code == 1:
+                s, t = np.float16(start), np.float16(step)
+            else:
+                s, t = bf16_bits(np.array([s32]))[0], bf16_bits(np.array([t32]))[0]
+        else:
+            s = np.array(int(start)).astype(np.int64).astype(dt)
+            t = np.array(int(step)).astype(np.int64).astype(dt)
+        got = port.arange(s, t, n, dt, dtype_code=code)
+        want = ref.arange(s, t, n, dt, dtype_code=code)
+        assert got.tobytes() == want.tobytes(), (code, start, step, n)
+    with pytest.raises(ValueError):
+        port.arange(True, True, 4, np.bool_)

@@ -5,9 +5,12 @@ manager that owns all device memory, in latency-critical loops that cannot absor
 synchronisation of cudaMalloc / cudaFree, or under a memory budget fixed up front.  mtxc_reduce keeps
 its split-reduction partials in a workspace that mtxc_init allocates; mtxc_reduce_noalloc keeps them
 in a fixed 4 MiB array that is part of the library's device image instead.  This file checks, through
-the C ABI, that the allocation-free entry point returns what mtxc_reduce returns -- on two calls in a
-row, since every call reuses the same array and finds the previous call's partials in it -- and that a
-reduction needing more scratch than the array holds is refused with a clear error.
+the C ABI, that the allocation-free entry point returns what mtxc_reduce returns and what the CPU
+oracle (the reference's CPU loops, restated) returns -- on two calls in a row, since every call reuses
+the same array and finds the previous call's partials in it -- and that a reduction needing more scratch
+than the array holds is refused with a clear error.  The refusal is reached through a test hook
+(mtxc_debug_set_noalloc_limit, not part of the public header) that lowers the size the check compares
+against: no reduction of a sensible size needs more than the 4 MiB array, which is the point of its size.
 
 The file is named so that pytest collects it last.
 """
@@ -71,12 +74,13 @@ def _inputs(shape, dtype, seed):
     return torch.randint(-(1 << 30), 1 << 30, tuple(shape), generator=g, device="cuda", dtype=tdt)
 
 
-def test_noalloc_matches_mtxc_reduce_on_consecutive_calls(gpu):
+def test_noalloc_matches_mtxc_reduce_on_consecutive_calls(gpu, port):
     import torch
 
     abi = _lib()
     for k, (shape, axis, dtype) in enumerate(CASES):
         x = _inputs(shape, dtype, 100 + k)
+        xh = x.cpu().numpy()
         meta = gpu.reduce_meta(list(x.shape), list(x.stride()), axis)
         for op in OPS:
             need = _scratch_needed(op, x, meta)
@@ -91,35 +95,47 @@ def test_noalloc_matches_mtxc_reduce_on_consecutive_calls(gpu):
                 got.append(out)
             gpu.sync()
             w = want.cpu().numpy()
+            cpu = port.reduce(op, xh, axis)
             for i, out in enumerate(got):
                 g = out.cpu().numpy()
                 tag = f"noalloc call {i + 1} {op} {shape} axis={axis} {np.dtype(dtype).name}"
                 if op == "sum" and dtype == np.float32:
                     x64 = x.double()
                     abs_sum = x64.abs().sum(axis).cpu().numpy()
-                    assert_sum_close(g, w, abs_sum, tag, exact=x64.sum(axis).cpu().numpy())
+                    exact = x64.sum(axis).cpu().numpy()
+                    assert_sum_close(g, w, abs_sum, tag + " vs mtxc_reduce", exact=exact)
+                    assert_sum_close(g, cpu, abs_sum, tag + " vs the oracle", exact=exact)
                 else:
-                    assert_bits_equal(g, w, tag)
+                    assert_bits_equal(g, w, tag + " vs mtxc_reduce")
+                    assert_bits_equal(g, cpu, tag + " vs the oracle")
 
 
 def test_noalloc_refuses_reductions_beyond_its_scratch(gpu):
     import torch
 
     abi = _lib()
-    # int8 ArgMax over a long strided axis with few outputs: many splits of 512 outputs each
-    for n_outer in range(1, 33):
-        x = torch.zeros((n_outer, 65536, 512), dtype=torch.int8, device="cuda")
-        meta = gpu.reduce_meta(list(x.shape), list(x.stride()), 1)
-        if _scratch_needed("argmax", x, meta) > SCRATCH_BYTES:
-            break
-    else:
-        pytest.skip("no case on this device needs more than the static scratch")
-    out = torch.empty(meta.out_shape, dtype=torch.int32, device="cuda")
-    rc = _call("mtxc_reduce_noalloc", "argmax", x, meta, out)
-    assert rc == abi.ERR_WORKSPACE
-    msg = abi.lib().mtxc_last_error().decode()
-    assert "static scratch" in msg and str(SCRATCH_BYTES) in msg
-    # the allocating entry point still handles it
-    abi.check(_call("mtxc_reduce", "argmax", x, meta, out))
+    L = abi.lib()
+    L.mtxc_debug_set_noalloc_limit.restype = ctypes.c_size_t
+    L.mtxc_debug_set_noalloc_limit.argtypes = [ctypes.c_size_t]
+    x = _inputs([8, 1 << 22], np.float32, 7)
+    meta = gpu.reduce_meta(list(x.shape), list(x.stride()), 1)
+    need = _scratch_needed("sum", x, meta)
+    limit = need // 2
+    assert 0 < limit < SCRATCH_BYTES
+    out = torch.full(meta.out_shape, 7.0, device="cuda")
+    prev = L.mtxc_debug_set_noalloc_limit(limit)
+    try:
+        rc = _call("mtxc_reduce_noalloc", "sum", x, meta, out)
+        assert rc == abi.ERR_WORKSPACE
+        msg = L.mtxc_last_error().decode()
+        assert "static scratch" in msg and str(limit) in msg and str(need) in msg, msg
+        gpu.sync()
+        assert bool((out == 7.0).all()), "a refused call must not write its output"
+    finally:
+        L.mtxc_debug_set_noalloc_limit(prev)
+    # at the array's full size the same reduction runs, and the allocating entry point agrees
+    abi.check(_call("mtxc_reduce_noalloc", "sum", x, meta, out))
+    want = torch.empty_like(out)
+    abi.check(_call("mtxc_reduce", "sum", x, meta, want))
     gpu.sync()
-    assert int(out.abs().sum()) == 0
+    assert torch.equal(out, want)
