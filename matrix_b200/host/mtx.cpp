@@ -422,6 +422,7 @@ struct ReducePair {
     std::weak_ptr<PairOutPrimitive> side[2];  // [0] values, [1] indices
     size_t side_bytes[2] = {0, 0};
     std::shared_ptr<Buffer> spare[2];         // for a side whose node no longer exists
+    void prepare();                           // allocates what run() writes
     void run();
 };
 
@@ -431,7 +432,10 @@ public:
     void eval(matrix& out, EvalType t) override {
         eval_input(pair_->input, t);
         allocate_output(*this, out);
-        if (t == EvalType::COMPILE_TRACE) return;
+        if (t == EvalType::COMPILE_TRACE) {
+            pair_->prepare();  // both sides' buffers exist before any recorded pass
+            return;
+        }
         if (evaluated) return;
         pair_->run();
     }
@@ -453,13 +457,20 @@ private:
     int side_;
 };
 
+void ReducePair::prepare() {
+    for (int k = 0; k < 2; ++k) {
+        auto n = side[k].lock();
+        if (n && !n->out_buffer) n->out_buffer = std::make_shared<Buffer>(side_bytes[k]);
+        if (!n && !spare[k]) spare[k] = std::make_shared<Buffer>(side_bytes[k]);
+    }
+}
+
 void ReducePair::run() {
+    prepare();
     void* ptrs[2];
     std::shared_ptr<PairOutPrimitive> nodes[2];
     for (int k = 0; k < 2; ++k) {
         nodes[k] = side[k].lock();
-        if (nodes[k] && !nodes[k]->out_buffer) nodes[k]->out_buffer = std::make_shared<Buffer>(side_bytes[k]);
-        if (!nodes[k] && !spare[k]) spare[k] = std::make_shared<Buffer>(side_bytes[k]);
         ptrs[k] = nodes[k] ? nodes[k]->out_buffer->ptr : spare[k]->ptr;
     }
     check(mtxc_reduce_pair(op, (int)input.type(), ptrs[0], static_cast<int32_t*>(ptrs[1]), input.data(), rstride, rlen,
@@ -675,10 +686,26 @@ dtype promote_types(dtype a, dtype b) { return (dtype)mtxc_promote_types((int)a,
 
 void init(int device) { check(mtxc_init(device), "mtxc_init"); }
 
+namespace {
+// While a pass is being recorded no device memory may be freed (cudaFree would invalidate the capture):
+// buffers released then -- a graph output rebound to a call's own buffer drops its previous one -- are
+// freed once the recording has ended.
+thread_local bool t_defer_frees = false;
+thread_local std::vector<void*> t_deferred_frees;
+
+void release_deferred() {
+    std::vector<void*> v;
+    v.swap(t_deferred_frees);
+    for (void* p : v) mtxc_free(p);
+}
+}  // namespace
+
 Buffer::Buffer(size_t n) : bytes(n) { check(mtxc_alloc(n, &ptr), "mtxc_alloc"); }
 Buffer::Buffer(void* alias, size_t n, std::shared_ptr<Buffer> owner) : ptr(alias), bytes(n), owner_(std::move(owner)) {}
 Buffer::~Buffer() {
-    if (!owner_) mtxc_free(ptr);
+    if (owner_) return;
+    if (t_defer_frees) t_deferred_frees.push_back(ptr);
+    else mtxc_free(ptr);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -980,18 +1007,24 @@ void run_pass(const std::vector<matrix*>& roots, GraphCache& cache, bool sync) {
     if (it == cache.passes.end() && cache.passes.size() < kMaxRecordedPasses) {
         check(mtxc_graph_begin(), "mtxc_graph_begin");
         t_recording = true;
+        t_defer_frees = true;
         try {
             eval_roots(roots, EvalType::EXEC_TRACE);
         } catch (...) {
             t_recording = false;
+            t_defer_frees = false;
             void* g = nullptr;
             mtxc_graph_end(&g);
             if (g) mtxc_graph_destroy(g);
+            release_deferred();
             throw;
         }
         t_recording = false;
+        t_defer_frees = false;
         void* g = nullptr;
-        check(mtxc_graph_end(&g), "mtxc_graph_end");
+        const int rc_end = mtxc_graph_end(&g);
+        release_deferred();
+        check(rc_end, "mtxc_graph_end");
         it = cache.passes.emplace(sig, std::shared_ptr<void>(g, [](void* q) { mtxc_graph_destroy(q); })).first;
     }
     if (it != cache.passes.end()) check(mtxc_graph_launch(it->second.get()), "mtxc_graph_launch");
@@ -1023,6 +1056,7 @@ struct JitCall {
     std::vector<std::weak_ptr<Primitive>> outs;
     std::vector<size_t> out_bytes;
     std::vector<std::shared_ptr<Buffer>> spare;  // for an output whose node no longer exists
+    void prepare();                              // allocates every output buffer run() binds
     void run();
 };
 
@@ -1034,7 +1068,10 @@ public:
     void eval(matrix& out, EvalType t) override {
         for (matrix& in : call_->inputs) eval_input(in, t);
         allocate_output(*this, out);
-        if (t == EvalType::COMPILE_TRACE) return;
+        if (t == EvalType::COMPILE_TRACE) {
+            call_->prepare();  // every output of the call has its buffer before any recorded pass
+            return;
+        }
         if (evaluated) return;
         call_->run();
     }
@@ -1060,6 +1097,15 @@ private:
     size_t index_;
 };
 
+void JitCall::prepare() {
+    if (spare.size() < outs.size()) spare.resize(outs.size());
+    for (size_t k = 0; k < outs.size(); ++k) {
+        auto n = outs[k].lock();
+        if (n && !n->out_buffer) n->out_buffer = std::make_shared<Buffer>(out_bytes[k]);
+        if (!n && !spare[k]) spare[k] = std::make_shared<Buffer>(out_bytes[k]);
+    }
+}
+
 void JitCall::run() {
     // the caller's inputs go to the compiled graph's inputs (primitives.cpp:3938, 4187-4189) ...
     for (size_t i = 0; i < inputs.size(); ++i) {
@@ -1068,19 +1114,11 @@ void JitCall::run() {
         g->leaves[i]->out_buffer = std::make_shared<Buffer>(in.data(), bytes, in.buffer());
     }
     // ... and each owning node of the graph writes straight into the call's output (:3951-3956, 4191-4205)
+    prepare();
     std::vector<std::shared_ptr<Primitive>> nodes(outs.size());
-    if (spare.size() < outs.size()) spare.resize(outs.size());
     for (size_t k = 0; k < outs.size(); ++k) {
         nodes[k] = outs[k].lock();
-        std::shared_ptr<Buffer> buf;
-        if (nodes[k]) {
-            if (!nodes[k]->out_buffer) nodes[k]->out_buffer = std::make_shared<Buffer>(out_bytes[k]);
-            buf = nodes[k]->out_buffer;
-        } else {
-            if (!spare[k]) spare[k] = std::make_shared<Buffer>(out_bytes[k]);
-            buf = spare[k];
-        }
-        g->outputs[k].tape_ptr()->out_buffer = buf;
+        g->outputs[k].tape_ptr()->out_buffer = nodes[k] ? nodes[k]->out_buffer : spare[k];
     }
     std::vector<matrix*> roots;
     for (matrix& o : g->outputs) roots.push_back(&o);

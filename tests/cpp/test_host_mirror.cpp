@@ -640,15 +640,28 @@ static void test_ranged_and_generators(std::mt19937& rng) {
     EXPECT(matrix::arctan2(xi, xi).type() == dtype::Float, "arctan2 of Int32 inputs casts them to Float");
 }
 
+// Runs one test function; an exception counts as a failure with its message instead of ending the run.
+template <typename Fn>
+static void run_test(const char* name, Fn&& fn) {
+    try {
+        fn();
+    } catch (const std::exception& e) {
+        ++checks;
+        ++failures;
+        std::printf("FAIL %s: exception: %s\n", name, e.what());
+    }
+}
+
 int main() {
+    std::setvbuf(stdout, nullptr, _IOLBF, 0);
     mtx::init(0);
     std::mt19937 rng(1234);
-    test_reductions(rng);
-    test_binary(rng);
-    test_trace(rng);
-    test_promotion_and_pointwise(rng);
-    test_jit(rng);
-    test_ranged_and_generators(rng);
+    run_test("reductions", [&] { test_reductions(rng); });
+    run_test("binary", [&] { test_binary(rng); });
+    run_test("trace", [&] { test_trace(rng); });
+    run_test("promotion_and_pointwise", [&] { test_promotion_and_pointwise(rng); });
+    run_test("jit", [&] { test_jit(rng); });
+    run_test("ranged_and_generators", [&] { test_ranged_and_generators(rng); });
     std::printf("host mirror: %d checks, %d failures\n", checks, failures);
     return failures ? 1 : 0;
 }
