@@ -684,6 +684,9 @@ def run_c5b(args):
     for r in range(rows):
         exact += x[r].sum(dtype=torch.float64)
         absum += x[r].abs().sum(dtype=torch.float64)
+    if world > 1:  # each rank holds its own rows: the whole tensor's sums
+        dist.all_reduce(exact)
+        dist.all_reduce(absum)
     # e2e through the C ABI with host buffers: each rank uploads its rows from pinned memory, reduces,
     # exchanges and reads the result back into pinned memory, every step
     e2e_steps = 0 if args.no_e2e else 3
