@@ -691,7 +691,10 @@ template <int OP, typename T, int V>
 __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
     using R = Reducer<OP, T>;
     using S = typename R::State;
-    __shared__ S partial[kBlock * V];
+    // each thread's V states, padded by one so that a warp's stores (one state each, threads VP states
+    // apart) spread over the banks instead of landing V states apart on the same ones
+    constexpr int VP = V + 1;
+    __shared__ S partial[kBlock * VP];
 
     const uint32_t tx = threadIdx.x % a.tx;
     const uint32_t ty = threadIdx.x / a.tx;
@@ -763,12 +766,12 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
         }
     }
 #pragma unroll
-    for (int j = 0; j < V; ++j) partial[threadIdx.x * V + j] = st[j];
+    for (int j = 0; j < V; ++j) partial[threadIdx.x * VP + j] = st[j];
     __syncthreads();
     if constexpr (IsPair<S>::value) {
         // (value, index) states: the tile's tx * V outputs are finished by all threads, consecutive
         // outputs on consecutive threads (coalesced stores).  Output q (lane x = q / V, element j = q % V)
-        // sits at partial[t * tx * V + q] for row group t and merges them in ascending t, the order of
+        // sits at partial[(t * tx + x) * VP + j] for row group t and merges them in ascending t, the order of
         // the single-thread merge below (B200, ArgMax over axis 1 of [16f, 8192, 1024]: int8 0.45 ->
         // 0.60, int16 0.71 -> 0.76, Float16 0.87 -> 0.91 of the measured copy bandwidth; for value
         // states, whose merges are cheap, one warp finishing alone measured faster)
@@ -776,15 +779,16 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
         const uint32_t tile_col = tile * tile_outputs;
         const uint64_t gbase = (uint64_t)o * a.inner + tile_col;
         for (uint32_t q = threadIdx.x; q < tile_outputs && tile_col + q < a.inner; q += kBlock) {
-            S s = partial[q];
-            for (uint32_t t = 1; t < ty_count; ++t) R::merge(s, partial[t * tile_outputs + q]);
+            const uint32_t x = q / V, j = q % V;
+            S s = partial[x * VP + j];
+            for (uint32_t t = 1; t < ty_count; ++t) R::merge(s, partial[(t * a.tx + x) * VP + j]);
             if (a.split == 1) R::store(a.out, gbase + q, s);
             else static_cast<S*>(a.partials)[(uint64_t)part * a.outputs + gbase + q] = s;
         }
     } else if (ty == 0 && active) {
         for (uint32_t t = 1; t < ty_count; ++t) {
 #pragma unroll
-            for (int j = 0; j < V; ++j) R::merge(st[j], partial[(t * a.tx + tx) * V + j]);
+            for (int j = 0; j < V; ++j) R::merge(st[j], partial[(t * a.tx + tx) * VP + j]);
         }
         const uint64_t gid = (uint64_t)o * a.inner + col;
 #pragma unroll
