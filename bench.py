@@ -1077,7 +1077,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--suite", action="store_true", help="also time the other benchmark configs")
-    ap.add_argument("--suite-configs", default="", help="comma-separated subset of C1,C3,C4,C5a,C5b,F2,F3,F4,F5,F6,F7")
+    ap.add_argument("--suite-configs", default="", help="comma-separated subset of C1,C3,C4,C5a,C5b,F2,F3,F4,F5,F6,F7,F8")
     ap.add_argument("--suite-scale", type=int, default=1, help="divide the configs' leading extent (small cases)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

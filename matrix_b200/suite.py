@@ -72,15 +72,15 @@ def _cpu(line, **spec):
 
 
 def run_all(dev, stream, configs=None, scale=1, cpu_hook=None):
-    """configs: names to run (default all: C1 C3 C4 C5a C5b, and F2 ... F7 for the statistics, astype,
-    pointwise, mixed-dtype, half-precision and 1- / 2-byte kernels); scale: divide each config's leading
-    extent by this (small cases for profiling)."""
+    """configs: names to run (default all: C1 C3 C4 C5a C5b, and F2 ... F8 for the statistics, astype,
+    pointwise, mixed-dtype, half-precision and 1- / 2-byte kernels, and every dtype at equal bytes); scale:
+    divide each config's leading extent by this (small cases for profiling)."""
     global _CPU_HOOK
     _CPU_HOOK = cpu_hook
     peak = _peak()
     g = torch.Generator(device=dev)
     out = []
-    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4", "F5", "F6", "F7"}
+    want = set(configs) if configs else {"C1", "C3", "C4", "C5a", "C5b", "F2", "F3", "F4", "F5", "F6", "F7", "F8"}
 
     # C1: Sum over the last axis of f32 [1024, 4096] ~ N(0,1)
     if "C1" in want:
@@ -103,6 +103,8 @@ def run_all(dev, stream, configs=None, scale=1, cpu_hook=None):
         _f5(out, dev, stream, g, peak, scale)
     if "F6" in want:
         _f6(out, dev, stream, g, peak, scale)
+    if "F8" in want:
+        _f8(out, dev, stream, g, peak, scale)
     if "F7" in want:
         _f7(out, dev, stream, g, peak, scale)
     torch.cuda.empty_cache()
@@ -361,3 +363,51 @@ def _f7(out, dev, stream, g, peak, scale):
     out.append(_line("F7-i16-argmax-cols", "ArgMax(axis=1) int16 [64,8192,1024]", z.numel() * 2 + c0 * 1024 * 4, ms,
                      peak))
     del z
+
+
+F8_DTYPES = [torch.float32, torch.float16, torch.bfloat16, torch.int32, torch.uint32, torch.int64, torch.uint64,
+             torch.int16, torch.uint16, torch.int8, torch.uint8, torch.bool]
+
+
+def _f8(out, dev, stream, g, peak, scale):
+    """Every dtype at equal bytes (512 MiB inputs for the 1- to 4-byte types, 1 GiB for the 8-byte ones):
+    broadcast Add a[64f,1,4096] + b[1,512,4096], Sum / Max / ArgMax over the last axis of [4096f, 32768], and
+    Max / ArgMax / Sum over axis 1 of [16f, 8192, 1024], with f = 4 / element size for the narrow types (1
+    otherwise); values 0..99, Bool 0 / 1."""
+    g.manual_seed(12)
+    for dt in F8_DTYPES:
+        es = torch.tensor([], dtype=dt).element_size()
+        f = max(1, 4 // es)
+        name = str(dt).replace("torch.", "")
+
+        def make(shape):
+            if dt == torch.bool:
+                return torch.randint(0, 2, shape, generator=g, device=dev, dtype=torch.int32).to(dt)
+            return torch.randint(0, 100, shape, generator=g, device=dev, dtype=torch.int32).to(dt)
+
+        a0 = max(64 * f // scale, 1)
+        a, b = make((a0, 1, 4096)), make((1, 512, 4096))
+        ob = torch.empty(a0, 512, 4096, dtype=dt, device=dev)
+        meta = backend.binary_meta(list(a.shape), list(a.stride()), list(b.shape), list(b.stride()))
+        ms = _time(lambda: backend.binary("add", a, b, out=ob, meta=meta), stream)
+        out.append(_line(f"F8-{name}-add", f"broadcast Add {name} a[{a0},1,4096] + b[1,512,4096]",
+                         (ob.numel() + a.numel() + b.numel()) * es, ms, peak))
+        del a, b, ob
+        r0 = max(4096 * f // scale, 1)
+        x = make((r0, 32768))
+        for op in ("sum", "max", "argmax"):
+            m = backend.reduce_meta(list(x.shape), list(x.stride()), 1)
+            o = backend.reduce(op, x, 1, meta=m)
+            ms = _time(lambda: backend.reduce(op, x, 1, out=o, meta=m), stream)
+            out.append(_line(f"F8-{name}-{op}-rows", f"{op}(axis=-1) {name} [{r0},32768]",
+                             x.numel() * es + o.numel() * o.element_size(), ms, peak))
+        del x
+        c0 = max(16 * f // scale, 1)
+        x = make((c0, 8192, 1024))
+        for op in ("max", "argmax", "sum"):
+            m = backend.reduce_meta(list(x.shape), list(x.stride()), 1)
+            o = backend.reduce(op, x, 1, meta=m)
+            ms = _time(lambda: backend.reduce(op, x, 1, out=o, meta=m), stream)
+            out.append(_line(f"F8-{name}-{op}-cols", f"{op}(axis=1) {name} [{c0},8192,1024]",
+                             x.numel() * es + o.numel() * o.element_size(), ms, peak))
+        del x
