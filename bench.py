@@ -778,6 +778,9 @@ def run_c5b(args):
             hook = None if args.no_cpu else suite_cpu_hook()
             for extra in suite.run_all(dev, main_s, cfgs, args.suite_scale, cpu_hook=hook):
                 print(json.dumps(extra), flush=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # every rank's exchanges are done before any rank releases its buffers
     comm.close()
     if world > 1:
         dist.barrier()
@@ -1063,6 +1066,8 @@ def run_sharded(args):
                                 "note": "8 exchange steps recorded once into a CUDA graph (the NCCL all-gather "
                                         "included) and replayed, no pre-roll: one graph launch per 8 steps"}
         print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()  # every rank's exchanges are done before any rank releases its buffers
     if comm is not None:
         comm.close()
     dist.barrier()

@@ -394,10 +394,14 @@ int mtxc_softmax_lastdim(int dtype, void* dst, const void* src, uint64_t rows, u
  * NCCL (libnccl.so.2) is loaded at run time, reusing the copy already in the process if there is one;
  * a one-rank communicator does not need it.
  *
- * The exchange is an all-gather of the per-rank partials plus a merge in rank order on every rank
- * (mtxc_merge_partials): every rank ends with the same result, float sums are deterministic, and Max /
- * ArgMax keep the first-index rule across GPUs.  Everything is enqueued on the calling thread's stream;
- * like every collective, all ranks must make the same calls in the same order.
+ * The exchange is an all-gather of the per-rank partials plus a merge in rank order on every rank: every
+ * rank ends with the same result, float sums are deterministic, and Max / ArgMax keep the first-index rule
+ * across GPUs.  When every rank drives its own GPU of one node it runs as one kernel over NVLink peer
+ * memory (each rank stores its partials into every rank's buffer, raises a flag there and merges once
+ * every rank's flag has arrived); otherwise as an NCCL all-gather and a merge kernel.  Everything is
+ * enqueued on the calling thread's stream; like every collective, all ranks must make the same calls in
+ * the same order, and one communicator's calls must not overlap on the GPU (issue them on one stream, or
+ * order them with events).
  * ---------------------------------------------------------------------------------------- */
 #define MTXC_COMM_ID_BYTES 128
 
@@ -406,13 +410,21 @@ int mtxc_softmax_lastdim(int dtype, void* dst, const void* src, uint64_t rows, u
 int mtxc_comm_unique_id(void* id, size_t bytes);
 
 /* Joins the calling thread (bound to its device by mtxc_init) to a communicator of nranks ranks as
- * rank `rank`.  Blocks until all nranks ranks have joined (ncclCommInitRank).  Allocates the gather
- * buffer the exchanges use, buffer_bytes (0: 16 MiB), once, here: the exchanges never allocate.  One
- * communicator per thread; mtxc_comm_destroy (or mtxc_shutdown) releases it.  nranks == 1 needs no id and
- * no NCCL. */
+ * rank `rank`.  Blocks until all nranks ranks have joined (ncclCommInitRank), then sets up the peer
+ * exchange (collectively; see mtxc_comm_status).  Allocates the buffers the exchanges use, each about
+ * buffer_bytes (0: 16 MiB; at least 64 KiB with several ranks; the same value on every rank), once, here:
+ * the exchanges never allocate.  One communicator per thread; mtxc_comm_destroy (or mtxc_shutdown) releases
+ * it.  nranks == 1 needs no id and no NCCL. */
 int mtxc_comm_init(int nranks, int rank, const void* id, size_t buffer_bytes);
 int mtxc_comm_destroy(void);
 int mtxc_comm_size(int* nranks, int* rank);
+/* *peer_exchange (if non-NULL): 1 when the exchanges run as one kernel over peer memory (every rank on its
+ * own GPU of one node, the ranks' exchange buffers mapped into each other with CUDA IPC at mtxc_comm_init;
+ * MTXC_COMM_PEER=0 in the environment keeps the NCCL all-gather + merge instead), else 0.  *timed_out (if
+ * non-NULL): waits for the thread's stream, then reports whether an exchange since the last query gave up
+ * waiting for a rank (a rank that never made the call: the peer exchange's waits are bounded, so it returns
+ * instead of hanging and its outputs are not valid) and clears the flag. */
+int mtxc_comm_status(int* peer_exchange, int* timed_out);
 
 /* A reduction over an axis that is sharded across the ranks: this rank holds a contiguous slice of the
  * reduced axis, described exactly as for mtxc_reduce (reduce_len = the slice's length, which may be 0).

@@ -95,6 +95,7 @@ def lib() -> C.CDLL:
             "mtxc_comm_init": (i32, [i32, i32, vp, sz]),
             "mtxc_comm_destroy": (i32, []),
             "mtxc_comm_size": (i32, [C.POINTER(i32), C.POINTER(i32)]),
+            "mtxc_comm_status": (i32, [C.POINTER(i32), C.POINTER(i32)]),
             "mtxc_reduce_sharded": (i32, [i32, i32, vp, vp, u32, u32, u32, U32P, U32P, U32P, C.POINTER(C.c_int64)]),
             "mtxc_allreduce": (i32, [i32, i32, vp, u64]),
             "mtxc_arange": (i32, [i32, vp, vp, vp, u64]),

@@ -3,15 +3,10 @@
 //
 // Each of `parts` shards reduced its contiguous slice of the axis; their partial results arrive
 // part-major (part p's `outputs` results at p * outputs, in shard order, e.g. from an NCCL
-// all-gather).  Merging in part order keeps the reference's semantics across shards exactly as the
-// kernels keep them across CTAs: Sum adds the partials in part order (integer sums wrap); Max / Min
-// take a later part's value only when strictly better, so the first shard wins ties; ArgMax / ArgMin
-// do the same on the (value, local index) pairs and add the winning shard's index offset, so the
-// result is the first global index of the extreme -- and 0 when no element beat the initial value,
-// since shard 0 (offset 0) then wins with its index 0.
+// all-gather) and are merged in part order (merge_one, merge.cuh).
 #include <algorithm>
 
-#include "mtxc_internal.cuh"
+#include "merge.cuh"
 
 namespace mtxc {
 namespace {
@@ -33,38 +28,9 @@ template <int OP, typename T>
 __global__ void __launch_bounds__(kBlock) merge_partials_kernel(const MergeArgs a) {
     const T* v = static_cast<const T*>(a.vals);
     for (uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < a.outputs;
-         gid += (uint64_t)gridDim.x * blockDim.x) {
-        if constexpr (OP == MTXC_REDUCE_SUM) {
-            if constexpr (Traits<T>::kFloat) {
-                float s = to_float(v[gid]);
-                for (uint32_t p = 1; p < a.parts; ++p) s = __fadd_rn(s, to_float(v[(uint64_t)p * a.outputs + gid]));
-                static_cast<T*>(a.dst)[gid] = from_float<T>(s);
-            } else if constexpr (Traits<T>::kBool) {
-                bool s = false;
-                for (uint32_t p = 0; p < a.parts; ++p) s = s || (uint8_t)v[(uint64_t)p * a.outputs + gid];
-                static_cast<T*>(a.dst)[gid] = mbool(s);
-            } else {
-                using W = typename Traits<T>::Acc;
-                W s = (W)v[gid];
-                for (uint32_t p = 1; p < a.parts; ++p) s = (W)(s + (W)v[(uint64_t)p * a.outputs + gid]);
-                static_cast<T*>(a.dst)[gid] = (T)s;
-            }
-        } else {
-            constexpr bool kMax = (OP == MTXC_REDUCE_MAX || OP == MTXC_REDUCE_ARGMAX);
-            T best = v[gid];
-            uint32_t from = 0;
-            for (uint32_t p = 1; p < a.parts; ++p) {
-                const T x = v[(uint64_t)p * a.outputs + gid];
-                if (kMax ? less(best, x) : less(x, best)) {
-                    best = x;
-                    from = p;
-                }
-            }
-            if (a.dst) static_cast<T*>(a.dst)[gid] = best;
-            if constexpr (OP == MTXC_REDUCE_ARGMAX || OP == MTXC_REDUCE_ARGMIN)
-                a.dst_idx[gid] = (int32_t)(a.idx[(uint64_t)from * a.outputs + gid] + a.offsets[from]);
-        }
-    }
+         gid += (uint64_t)gridDim.x * blockDim.x)
+        merge_one<OP, T>(a.dst, a.dst_idx, v + gid, a.outputs, a.idx ? a.idx + gid : nullptr, a.outputs, a.parts,
+                         a.offsets, gid);
 }
 
 template <typename T>

@@ -79,6 +79,18 @@ class NativeComm:
         _abi.check(_abi.lib().mtxc_comm_init(self.world, self.rank, uid, int(buffer_bytes)))
         self.open = True
 
+    def status(self, wait: bool = True) -> tuple[bool, bool]:
+        """(peer_exchange, timed_out): whether the exchanges run as one kernel over peer memory, and -- when
+        `wait` (the thread's stream is synchronised first) -- whether an exchange since the last query gave up
+        waiting for a rank."""
+        import ctypes
+
+        from . import _abi
+
+        peer, late = ctypes.c_int(0), ctypes.c_int(0)
+        _abi.check(_abi.lib().mtxc_comm_status(ctypes.byref(peer), ctypes.byref(late) if wait else None))
+        return bool(peer.value), bool(late.value)
+
     def close(self) -> None:
         from . import _abi
 

@@ -7,8 +7,14 @@ torch.distributed's all-gather with the same merge kernel.  Every result is chec
 oracle's reduction of the whole tensor.  The tensors include ArgMax / ArgMin ties that straddle the
 shard boundary (the first global index must win: Matrix.mm:16291-16299), a column whose only extreme
 sits at the first row of the second shard, constant columns (index 0), NaNs, and int32 sums that wrap.
-mtxc_allreduce (sum / max / min) is checked against numpy on the gathered buffers.  Prints "rank ok" on
-success; any mismatch raises.
+mtxc_allreduce (sum / max / min) is checked against numpy on the gathered buffers.  Each rank prints which
+exchange the communicator uses ("peer=1": one kernel over NVLink peer memory; "peer=0": NCCL all-gather +
+merge, e.g. with MTXC_COMM_PEER=0) and "rank ok" on success; any mismatch raises.
+
+With MTXC_SHARD_CHECK_TIMEOUT=1 the program instead checks the peer exchange's bounded wait: rank 1 skips
+one exchange that rank 0 makes, so rank 0's wait for rank 1 runs out (MTXC_COMM_SPIN_LIMIT keeps that short),
+the kernel returns, and mtxc_comm_status reports it; rank 0 prints "timeout reported".  No GPU hangs or
+faults: the wait is bounded and nothing is read or written out of bounds.
 """
 import datetime
 import os
@@ -57,6 +63,21 @@ def main():
     comm = NativeComm()
     try:
         assert (comm.world, comm.rank) == (world, rank)
+        peer, _ = comm.status(wait=False)
+        print(f"rank {rank} peer={int(peer)}", flush=True)
+        if os.environ.get("MTXC_SHARD_CHECK_TIMEOUT") == "1":
+            assert peer, "the timeout check needs the peer exchange"
+            x = torch.arange(4096, dtype=torch.float32, device=dev).reshape(1, 4096)
+            got = reduce_sharded("sum", x, 0, world)           # both ranks: completes
+            torch.cuda.synchronize()
+            assert comm.status() == (True, False)
+            if rank == 0:
+                reduce_sharded("sum", x, 0, world)             # rank 1 never makes this call
+                assert comm.status() == (True, True), "a wait that ran out must be reported"
+                print("timeout reported", flush=True)
+            assert got.shape == (4096,)
+            print("rank ok", flush=True)
+            return
         shape, xs = tensors(world)
         for x in xs:
             lo, hi = shard_range(shape[0], world, rank)
@@ -89,6 +110,8 @@ def main():
             assert_bits_equal(buf.cpu().numpy(), want, f"rank {rank} allreduce {op}")
         print("rank ok", flush=True)
     finally:
+        torch.cuda.synchronize()
+        dist.barrier()      # every rank's kernels are done before any rank unmaps or frees its buffers
         comm.close()
         dist.barrier()
         dist.destroy_process_group()

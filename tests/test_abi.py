@@ -60,6 +60,7 @@ def test_calls_before_init_fail_cleanly():
     assert lib.mtxc_allreduce(0, 0, None, 4) == _abi.ERR_NOT_INITIALIZED
     n, r = C.c_int(-1), C.c_int(-1)
     assert lib.mtxc_comm_size(C.byref(n), C.byref(r)) == _abi.ERR_NOT_INITIALIZED
+    assert lib.mtxc_comm_status(C.byref(n), C.byref(r)) == _abi.ERR_NOT_INITIALIZED
     assert lib.mtxc_comm_destroy() == 0
     size = C.c_size_t(123)
     assert lib.mtxc_workspace_size(C.byref(size)) == 0 and size.value == 0

@@ -125,17 +125,37 @@ def _free_port():
     return p
 
 
-def test_reduce_sharded_on_two_gpus():
-    """torchrun, 2 ranks, NCCL: every op over the sharded and a local axis (skipped on 1 GPU)."""
+def _two_rank_run(extra_env):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=repo)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=repo, **extra_env)
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(repo, "tests", "multirank_shard_check.py")]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert res.stdout.count("rank ok") == 2, res.stdout[-2000:]
+    return res.stdout
+
+
+def test_reduce_sharded_on_two_gpus():
+    """torchrun, 2 ranks on 2 GPUs: every op over the sharded and a local axis against the oracle, through
+    the peer-memory exchange (one kernel over NVLink) -- skipped on 1 GPU."""
+    out = _two_rank_run({})
+    assert out.count("peer=1") == 2, out[-2000:]
+
+
+def test_reduce_sharded_on_two_gpus_nccl_path():
+    """The same with MTXC_COMM_PEER=0: the NCCL all-gather + merge kernel path."""
+    out = _two_rank_run({"MTXC_COMM_PEER": "0"})
+    assert out.count("peer=0") == 2, out[-2000:]
+
+
+def test_peer_exchange_wait_is_bounded():
+    """Rank 1 skips an exchange rank 0 makes: rank 0's wait runs out after MTXC_COMM_SPIN_LIMIT sleeps, the
+    kernel returns and mtxc_comm_status reports it (no hang, no fault)."""
+    out = _two_rank_run({"MTXC_SHARD_CHECK_TIMEOUT": "1", "MTXC_COMM_SPIN_LIMIT": "300000"})
+    assert "timeout reported" in out, out[-2000:]
