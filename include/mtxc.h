@@ -422,8 +422,9 @@ int mtxc_comm_size(int* nranks, int* rank);
  * own GPU of one node, the ranks' exchange buffers mapped into each other with CUDA IPC at mtxc_comm_init;
  * MTXC_COMM_PEER=0 in the environment keeps the NCCL all-gather + merge instead), else 0.  *timed_out (if
  * non-NULL): waits for the thread's stream, then reports whether an exchange since the last query gave up
- * waiting for a rank (a rank that never made the call: the peer exchange's waits are bounded, so it returns
- * instead of hanging and its outputs are not valid) and clears the flag. */
+ * waiting for a rank (a rank that never made the call: the peer exchange's waits are bounded -- 2^22 polls
+ * of the rank's flag, each followed by a short sleep, or MTXC_COMM_SPIN_LIMIT polls -- so it returns instead
+ * of hanging, and its outputs are not valid) and clears the flag. */
 int mtxc_comm_status(int* peer_exchange, int* timed_out);
 
 /* A reduction over an axis that is sharded across the ranks: this rank holds a contiguous slice of the

@@ -115,7 +115,7 @@ constexpr int kMaxRanks = 256;  // mtxc_merge_partials' limit on parts
 constexpr int kMaxPeerRanks = 16;    // one node
 constexpr int kExchBlocks = 32;      // fixed grid: every call runs the same blocks (per-block generations)
 constexpr int kExchThreads = 256;
-constexpr uint64_t kDefaultSpinLimit = uint64_t(1) << 25;  // x ~64 ns sleeps: a few seconds
+constexpr uint64_t kDefaultSpinLimit = uint64_t(1) << 22;  // polls of a flag, each followed by a short sleep
 constexpr size_t kMinMultiRankBytes = size_t(64) << 10;    // the setup's all-gathers of per-rank cards
 
 // Byte offsets within every rank's exchange buffer (the same layout on all ranks).

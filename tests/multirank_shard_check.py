@@ -72,8 +72,13 @@ def main():
             torch.cuda.synchronize()
             assert comm.status() == (True, False)
             if rank == 0:
+                import time
+
+                t0 = time.perf_counter()
                 reduce_sharded("sum", x, 0, world)             # rank 1 never makes this call
-                assert comm.status() == (True, True), "a wait that ran out must be reported"
+                status = comm.status()
+                print(f"rank 0 waited {time.perf_counter() - t0:.3f} s, status {status}", flush=True)
+                assert status == (True, True), "a wait that ran out must be reported"
                 print("timeout reported", flush=True)
             assert got.shape == (4096,)
             print("rank ok", flush=True)
