@@ -416,6 +416,9 @@ int mtxc_comm_unique_id(void* id, size_t bytes);
  * the exchanges never allocate.  One communicator per thread; mtxc_comm_destroy (or mtxc_shutdown) releases
  * it.  nranks == 1 needs no id and no NCCL. */
 int mtxc_comm_init(int nranks, int rank, const void* id, size_t buffer_bytes);
+/* Waits for the thread's stream and releases its communicator.  With the peer exchange, every rank's last
+ * exchange must have finished before any rank destroys (synchronise every rank, then a barrier): a rank still
+ * running one writes into the others' buffers. */
 int mtxc_comm_destroy(void);
 int mtxc_comm_size(int* nranks, int* rank);
 /* *peer_exchange (if non-NULL): 1 when the exchanges run as one kernel over peer memory (every rank on its

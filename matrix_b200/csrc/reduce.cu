@@ -148,6 +148,45 @@ struct Reducer<MTXC_REDUCE_SUM, T> {
         if constexpr (Traits<T>::kBool) s |= (p.w[0] | p.w[1] | p.w[2] | p.w[3]) != 0u;
         else s = (State)(s + (State)(p.w[0] + p.w[1] + p.w[2] + p.w[3]));
     }
+    // Column kernel, 1-byte types: a lane's 16 columns accumulate in the 16-bit halves of eight words
+    // (even bytes, odd bytes), masked back to their low byte every 256 rows before a half can carry into
+    // its neighbour.  The low byte is the sum modulo 2^8, all that the 1-byte result keeps of the
+    // wrap-around sum.  Bool ors the words.
+    static constexpr bool kColSimd = sizeof(T) == 1;
+    struct ColState {
+        uint32_t e[4], o[4];
+        uint32_t n;
+    };
+    __device__ static ColState col_init(uint32_t, uint32_t, uint32_t = 0) { return ColState{}; }
+    __device__ static void col_fold(ColState& c, const uint32_t (&w)[4], uint32_t) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (Traits<T>::kBool) {
+                c.e[i] |= w[i];
+            } else {
+                c.e[i] += w[i] & 0x00ff00ffu;
+                c.o[i] += __byte_perm(w[i], 0u, 0x4341u);  // bytes 1 and 3 into the halves' low bytes
+            }
+        }
+        if constexpr (!Traits<T>::kBool) {
+            if (++c.n == 256u) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    c.e[i] &= 0x00ff00ffu;
+                    c.o[i] &= 0x00ff00ffu;
+                }
+                c.n = 0;
+            }
+        }
+    }
+    __device__ static void col_finish(ColState& c, State (&st)[16]) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = j / 4, b = j % 4;
+            if constexpr (Traits<T>::kBool) st[j] = (State)((c.e[i] >> (8 * b)) & 0xffu);
+            else st[j] = (State)(((b % 2 ? c.o[i] : c.e[i]) >> (16 * (b / 2))) & 0xffu);
+        }
+    }
     __device__ static void store(const Out& o, uint64_t gid, const State& s) {
         if constexpr (Traits<T>::kFloat) static_cast<T*>(o.v)[gid] = from_float<T>(s);
         else if constexpr (Traits<T>::kBool) static_cast<T*>(o.v)[gid] = mbool(s != 0);
@@ -184,18 +223,132 @@ struct PairExtremum {
     }
     __device__ static State shfl(const State& s, int m) { return State{shfl_xor(s.v, m), shfl_xor(s.i, m)}; }
 
-    // Column kernel, 1- and 2-byte types (integers, Bool whose bytes compare unsigned, and the half
-    // types, compared as the floats they widen to): the lane's 16 bytes of columns keep their best
-    // values packed in four words; per reduced row, one SIMD compare per word gives the lanes the row
-    // beats (strictly, so the first row of a tie is kept; NaN never beats), the row's bits replace the
-    // best in exactly those lanes, and the row's number within the current chunk of rows (1-based, 16
-    // bits) is merged into the packed 16-bit "row of the best" lanes there (a row that beats no lane
-    // skips both).  A chunk ends after 65,535 rows or at the end of the lane's rows: lanes that won in
-    // it turn their chunk number back into a row index.  No branch per element; every index stays
-    // exact whatever the length.
+    // Column kernel (and the row kernel's lanes), 1- and 2-byte types.  A lane's 16 bytes of columns
+    // are folded without per-element branches in one of two ways.
+    //
+    // Integers and Bool (keyed): each element and its row form one 32-bit key, the element's bits on
+    // top (24 or 16 bits up) and a row part below that decreases with the row for Max (increases for
+    // Min), so one integer max (min) of keys -- signed for the signed types, unsigned for the others
+    // and Bool -- picks the larger value and, among equal values, the earlier row: exactly the strict
+    // "first index wins" rule.  Building a key is one byte permute; two rows fold with one 3-input
+    // max (min).  The row part counts the lane's rows within a chunk (at most 2^24 - 2 or 2^16 - 2
+    // rows); at a chunk's end the lanes whose best came from it turn the count back into a row index,
+    // and their key's row part becomes the carried mark, which beats (loses to) every later row of
+    // the same value.  The initial key (dtype_lowest / dtype_max with the row part that loses every
+    // tie) marks a lane that saw no row.
+    //
+    // The half types (packed): the lane's best values stay packed in four words; per reduced row, one
+    // SIMD compare per word (as the floats they widen to) gives the lanes the row beats (strictly, so
+    // the first row of a tie is kept; NaN never beats), the row's bits replace the best in exactly
+    // those lanes, and the row's number within the current chunk of rows (1-based, 16 bits) is merged
+    // into the packed 16-bit "row of the best" lanes there (a row that beats no lane skips both).  A
+    // chunk ends after 65,535 rows or at the end of the lane's rows: lanes that won in it turn their
+    // chunk number back into a row index.
+    //
+    // Either way every index stays exact whatever the length.
     static constexpr bool kColSimd = sizeof(T) <= 2;
     static constexpr int kLanes = 16 / (int)sizeof(T);
-    struct ColState {
+    static constexpr bool kKeyed = kColSimd && !Traits<T>::kFloat;
+    static constexpr bool kColFold2 = kKeyed;
+    static constexpr int kKeyShift = 32 - 8 * (int)sizeof(T);
+    static constexpr uint32_t kLow = (1u << kKeyShift) - 1u;          // the row part of a key
+    static constexpr uint32_t kCarried = kMax ? kLow : 0u;             // best from an earlier chunk
+    static constexpr uint32_t kUnset = kMax ? 0u : kLow;               // no row yet
+    struct KeyState {
+        uint32_t key[kLanes];
+        int32_t idx[kLanes];       // row index of a carried best
+        uint32_t n;                // rows of the current chunk so far
+        uint32_t row;              // last row folded
+        uint32_t step;             // distance between the lane's consecutive rows
+        uint32_t limit;            // rows per chunk (at most kLow - 1, so row parts stay clear of both marks)
+        uint32_t lane_stride;      // index distance between neighbouring lanes (rows: 1, columns: 0)
+    };
+    __device__ static uint32_t key_bits(T v) {
+        uint32_t b = 0;
+        memcpy(&b, &v, sizeof(T));
+        return b << kKeyShift;
+    }
+    __device__ static uint32_t key_ext(uint32_t a, uint32_t b) {
+        if constexpr (std::is_signed_v<T>) return (uint32_t)(kMax ? max((int)a, (int)b) : min((int)a, (int)b));
+        else return kMax ? umax(a, b) : umin(a, b);
+    }
+    __device__ static uint32_t key_ext3(uint32_t a, uint32_t b, uint32_t c) {
+        if constexpr (std::is_signed_v<T>)
+            return (uint32_t)(kMax ? __vimax3_s32((int)a, (int)b, (int)c) : __vimin3_s32((int)a, (int)b, (int)c));
+        else return kMax ? __vimax3_u32(a, b, c) : __vimin3_u32(a, b, c);
+    }
+    // the key of lane j of the packed row w: its element on top, the row part rk below
+    __device__ static uint32_t key_of(const uint32_t (&w)[4], int j, uint32_t rk) {
+        if constexpr (sizeof(T) == 1) return __byte_perm(w[j / 4], rk, 0x0654u | ((uint32_t)(j % 4) << 12));
+        else return __byte_perm(w[j / 2], rk, 0x0054u | ((uint32_t)(j % 2) << 9) | ((uint32_t)(j % 2 * 2 + 1) << 12));
+    }
+    __device__ static uint32_t row_part(uint32_t n) { return kMax ? (kLow - 1u) - n : n + 1u; }
+    __device__ static KeyState col_init_keyed(uint32_t step, uint32_t limit, uint32_t lane_stride) {
+        KeyState c;
+        const uint32_t k0 = key_bits(kMax ? lowest_value<T>() : highest_value<T>()) | kUnset;
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) {
+            c.key[j] = k0;
+            c.idx[j] = 0;
+        }
+        c.n = 0;
+        c.row = 0;
+        c.step = step;
+        c.limit = min(limit, kLow - 1u);
+        c.lane_stride = lane_stride;
+        return c;
+    }
+    __device__ static void col_flush(KeyState& c) {
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) {
+            const uint32_t low = c.key[j] & kLow;
+            if (low != kCarried && low != kUnset) {
+                const uint32_t cnt = kMax ? (kLow - 1u) - low : low - 1u;  // the row's count in this chunk
+                c.idx[j] = (int32_t)(c.row - (c.n - 1u - cnt) * c.step + (uint32_t)j * c.lane_stride);
+                c.key[j] = (c.key[j] & ~kLow) | kCarried;
+            }
+        }
+        c.n = 0;
+    }
+    __device__ static void col_fold(KeyState& c, const uint32_t (&w)[4], uint32_t row) {
+        const uint32_t rk = row_part(c.n);
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) c.key[j] = key_ext(c.key[j], key_of(w, j, rk));
+        c.n += 1;
+        c.row = row;
+        if (c.n == c.limit) col_flush(c);
+    }
+    // two consecutive rows of the lane (row_b = row_a + step)
+    __device__ static void col_fold2(KeyState& c, const uint32_t (&wa)[4], const uint32_t (&wb)[4], uint32_t row_a,
+                                     uint32_t row_b) {
+        if (c.n + 2u > c.limit) {
+            col_fold(c, wa, row_a);
+            col_fold(c, wb, row_b);
+            return;
+        }
+        const uint32_t ra = row_part(c.n), rb = row_part(c.n + 1u);
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) c.key[j] = key_ext3(c.key[j], key_of(wa, j, ra), key_of(wb, j, rb));
+        c.n += 2;
+        c.row = row_b;
+        if (c.n == c.limit) col_flush(c);
+    }
+    __device__ static void col_finish(KeyState& c, State (&st)[kLanes]) {
+        if (c.n) col_flush(c);
+#pragma unroll
+        for (int j = 0; j < kLanes; ++j) {
+            if ((c.key[j] & kLow) == kUnset) {
+                st[j] = init();
+            } else {
+                T v;
+                const uint32_t b = c.key[j] >> kKeyShift;
+                memcpy(&v, &b, sizeof(T));  // little-endian: the element's bits are the low bytes of b
+                st[j] = State{widen(v), c.idx[j]};
+            }
+        }
+    }
+
+    struct PackedState {
         Lanes best;
         uint32_t won[kLanes / 2];  // 16-bit lanes: chunk row number of the lane's best, 0 = none yet
         int32_t idx[kLanes];       // row index of the best as of the last finished chunk
@@ -226,8 +379,13 @@ struct PairExtremum {
             return kMax ? __vcmpgtu2(x, b) : __vcmpltu2(x, b);
         }
     }
+    using ColState = std::conditional_t<kKeyed, KeyState, PackedState>;
     __device__ static ColState col_init(uint32_t step, uint32_t limit, uint32_t lane_stride = 0) {
-        ColState c;
+        if constexpr (kKeyed) return col_init_keyed(step, limit, lane_stride);
+        else return col_init_packed(step, limit, lane_stride);
+    }
+    __device__ static PackedState col_init_packed(uint32_t step, uint32_t limit, uint32_t lane_stride) {
+        PackedState c;
         Vec16<T> v;
 #pragma unroll
         for (int j = 0; j < kLanes; ++j) {
@@ -245,7 +403,7 @@ struct PairExtremum {
         return c;
     }
     // lanes that won in the current chunk take the row index of their last win; the chunk restarts
-    __device__ static void col_flush(ColState& c) {
+    __device__ static void col_flush(PackedState& c) {
 #pragma unroll
         for (int j = 0; j < kLanes; ++j) {
             const uint32_t t = (c.won[j / 2] >> (16 * (j % 2))) & 0xffffu;
@@ -255,7 +413,7 @@ struct PairExtremum {
         for (int i = 0; i < kLanes / 2; ++i) c.won[i] = 0;
         c.n = 0;
     }
-    __device__ static void col_fold(ColState& c, const uint32_t (&w)[4], uint32_t row) {
+    __device__ static void col_fold(PackedState& c, const uint32_t (&w)[4], uint32_t row) {
         c.n += 1;
         c.row = row;
         const uint32_t t2 = c.n * 0x00010001u;  // the chunk row number in both 16-bit halves
@@ -280,7 +438,7 @@ struct PairExtremum {
         }
         if (c.n == c.limit) col_flush(c);
     }
-    __device__ static void col_finish(ColState& c, State (&st)[kLanes]) {
+    __device__ static void col_finish(PackedState& c, State (&st)[kLanes]) {
         col_flush(c);
         Vec16<T> v;
         memcpy(&v, &c.best, 16);
@@ -436,6 +594,7 @@ struct StatReducer : Reducer<MTXC_REDUCE_SUM, T> {
     using Sum = Reducer<MTXC_REDUCE_SUM, T>;
     using State = typename Sum::State;
     static constexpr bool kVecFold = OP == kStatMean && Sum::kVecFold;  // rms / norm square each element
+    static constexpr bool kColSimd = OP == kStatMean && Sum::kColSimd;
     __device__ static void fold(State& s, T v, uint32_t i) { Sum::fold(s, OP == kStatMean ? v : square_in_type(v), i); }
     // sum / (float)n in the division's dtype; *as_half tells whether that dtype is Float16
     __device__ static float mean_of(T sum, uint32_t n, bool* as_half) {
@@ -507,6 +666,36 @@ template <class R, class = void>
 struct ColSimd : std::false_type {};
 template <class R>
 struct ColSimd<R, std::void_t<decltype(R::kColSimd)>> : std::bool_constant<R::kColSimd> {};
+// Column folds that take two rows per call (col_fold2).
+template <class R, class = void>
+struct ColFold2 : std::false_type {};
+template <class R>
+struct ColFold2<R, std::void_t<decltype(R::kColFold2)>> : std::bool_constant<R::kColFold2> {};
+
+static_assert(kUnroll % 2 == 0, "col_fold_rows folds rows in pairs");
+
+// Folds kUnroll packed rows x[k] (row numbers row0 + k * step) into a column state, two at a time where
+// the reducer can.
+template <class R, class X>
+__device__ __forceinline__ void col_fold_rows(typename R::ColState& cs, const X (&x)[kUnroll], uint32_t row0,
+                                              uint32_t step) {
+    if constexpr (ColFold2<R>::value) {
+#pragma unroll
+        for (int k = 0; k < kUnroll; k += 2) {
+            uint32_t wa[4], wb[4];
+            memcpy(wa, &x[k], 16);
+            memcpy(wb, &x[k + 1], 16);
+            R::col_fold2(cs, wa, wb, row0 + k * step, row0 + (k + 1) * step);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+            uint32_t w[4];
+            memcpy(w, &x[k], 16);
+            R::col_fold(cs, w, row0 + k * step);
+        }
+    }
+}
 
 template <typename R>
 __device__ __forceinline__ void warp_reduce(typename R::State& s) {
@@ -592,12 +781,7 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
                 Vec16<T> x[kUnroll];
 #pragma unroll
                 for (int k = 0; k < kUnroll; ++k) x[k] = load_stream(pv + (size_t)(c + k * G) * V);
-#pragma unroll
-                for (int k = 0; k < kUnroll; ++k) {
-                    uint32_t w[4];
-                    memcpy(w, &x[k], 16);
-                    R::col_fold(cs, w, vbeg + (c + k * G) * V);
-                }
+                col_fold_rows<R>(cs, x, vbeg + c * V, G * V);
             }
             for (; c < nvec; c += G) {
                 Vec16<T> x = load_stream(pv + (size_t)c * V);
@@ -723,12 +907,7 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
                 ew::Slot<T, V> x[kUnroll];
 #pragma unroll
                 for (int k = 0; k < kUnroll; ++k) ew::load_slot(x[k], p + (size_t)(r + k * step) * a.rstride);
-#pragma unroll
-                for (int k = 0; k < kUnroll; ++k) {
-                    uint32_t w[4];
-                    memcpy(w, &x[k], 16);
-                    R::col_fold(cs, w, r + k * step);
-                }
+                col_fold_rows<R>(cs, x, r, step);
             }
             for (; r < end; r += step) {
                 ew::Slot<T, V> x;

@@ -68,14 +68,14 @@ def main():
         if os.environ.get("MTXC_SHARD_CHECK_TIMEOUT") == "1":
             assert peer, "the timeout check needs the peer exchange"
             x = torch.arange(4096, dtype=torch.float32, device=dev).reshape(1, 4096)
-            got = reduce_sharded("sum", x, 0, world)           # both ranks: completes
+            got = reduce_sharded("sum", x, 0, world, comm=comm)  # both ranks: completes
             torch.cuda.synchronize()
             assert comm.status() == (True, False)
             if rank == 0:
                 import time
 
                 t0 = time.perf_counter()
-                reduce_sharded("sum", x, 0, world)             # rank 1 never makes this call
+                reduce_sharded("sum", x, 0, world, comm=comm)  # rank 1 never makes this call
                 status = comm.status()
                 print(f"rank 0 waited {time.perf_counter() - t0:.3f} s, status {status}", flush=True)
                 assert status == (True, True), "a wait that ran out must be reported"

@@ -250,6 +250,47 @@ def test_reduce_split_workspace_too_small(gpu, port):
     test_reduce_split_workspace_too_small.workspace = keep
 
 
+@pytest.mark.parametrize("dtype", [np.int8, np.uint8, np.bool_], ids=lambda d: np.dtype(d).name)
+def test_reduce_narrow_column_sums(gpu, port, dtype):
+    """Sum (and the fused uint8 / int8 mean) of the 1-byte types over a strided axis, through the column
+    kernel's 16-bit-lane fold: long columns with the default workspace and with none (one split, so each
+    thread folds ~375 rows and the lanes are masked back to their low byte mid-run), 16-byte aligned
+    operands and one 4 bytes off the boundary (the 4-byte lanes).  Full-range values: the sums wrap.
+    Bit-exact."""
+    import ctypes
+
+    import torch
+
+    from matrix_b200 import _abi
+
+    rng = np.random.default_rng(zlib.crc32(f"colsum{np.dtype(dtype).name}".encode()))
+    L = _abi.lib()
+    size = ctypes.c_size_t()
+    _abi.check(L.mtxc_workspace_size(ctypes.byref(size)))
+    keep = torch.empty(size.value, dtype=torch.uint8, device="cuda")
+    cases = [([3000, 512], 0, 0), ([2, 2100, 64], 1, 0), ([1100, 96], 0, 4), ([5000, 16], 0, 16)]
+    try:
+        for ws in ("default", "none"):
+            if ws == "none":
+                _abi.check(L.mtxc_set_workspace(None, 0))
+            for shape, axis, off in cases:
+                n = int(np.prod(shape))
+                v = rng.integers(0, 2, n).astype(np.bool_) if dtype == np.bool_ else make_values(rng, n, dtype, "full")
+                base = np.concatenate([np.zeros(off, dtype=v.dtype), v])
+                strides = [int(np.prod(shape[i + 1:])) for i in range(len(shape))]
+                check_reduce(gpu, port, "sum", base, shape, strides, off, axis, False, f"workspace {ws}")
+                if dtype != np.bool_:
+                    x = strided_view(base, shape, strides, off)
+                    want, _ = port.stat("mean", x, axis, False)
+                    got = gpu.stat("mean", device_view(to_device(base), shape, strides, off), axis, False)
+                    gpu.sync()
+                    assert_bits_equal(got.cpu().numpy(), np.asarray(want),
+                                      f"mean {np.dtype(dtype).name} {shape} axis {axis} +{off} workspace {ws}")
+    finally:
+        _abi.check(L.mtxc_set_workspace(keep.data_ptr(), size.value))
+    test_reduce_narrow_column_sums.workspace = keep
+
+
 def test_unsupported_dtype_is_an_error(gpu):
     import torch
 

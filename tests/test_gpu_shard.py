@@ -9,6 +9,7 @@
   the oracle on every rank.
 """
 import os
+import re
 import socket
 import subprocess
 import sys
@@ -160,3 +161,7 @@ def test_peer_exchange_wait_is_bounded():
     kernel returns and mtxc_comm_status reports it (no hang, no fault)."""
     out = _two_rank_run({"MTXC_SHARD_CHECK_TIMEOUT": "1", "MTXC_COMM_SPIN_LIMIT": "20000"})
     assert "timeout reported" in out, out[-2000:]
+    # 20,000 polls of ~64 ns sleeps: milliseconds, far below the process group's 60 s timeout, so the kernel's
+    # own bound ended the wait
+    waited = float(re.search(r"rank 0 waited ([0-9.]+) s", out).group(1))
+    assert waited < 10.0, out[-2000:]
