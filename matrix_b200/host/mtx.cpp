@@ -72,8 +72,6 @@ uint64_t span(const std::vector<size_m>& shape, const std::vector<size_m>& strid
     return last + 1;
 }
 
-// Allocate-or-adopt the output and fill the tape's cache (primitives.cpp:2866-2882), before the
-// single COMPILE_TRACE return.
 // Bytes of device memory a node's output needs.
 size_t output_bytes(const matrix& out) {
     return std::max<uint64_t>(span(out.shape(), out.strides()), 1) * dtype_size(out.type());
@@ -152,6 +150,51 @@ private:
     matrix input_;
     int axis_;
     bool keepdims_;
+    uint32_t cdims_ = 0, rstride_ = 0, rlen_ = 0;
+    uint32_t shape_[MTXC_MAX_DIMS] = {}, s_out_[MTXC_MAX_DIMS] = {}, s_in_[MTXC_MAX_DIMS] = {};
+};
+
+// A reduction over axis 0 of a matrix sharded along that axis across the calling thread's communicator's
+// ranks: the local reduction and the exchange of the partials, one mtxc_reduce_sharded call (no
+// counterpart in the reference, which runs on one device).
+class ShardedReducePrimitive : public Primitive {
+public:
+    ShardedReducePrimitive(int op, const matrix& in, bool keepdims, const std::vector<size_m>& out_shape,
+                           std::vector<int64_t> first_rows)
+        : op_(op), input_(in), first_rows_(std::move(first_rows)) {
+        const uint32_t dims = in.dims();
+        std::vector<size_m> out_strides = row_major(out_shape);
+        out_strides.resize(dims, 0);
+        cdims_ = mtxc_collapse_dims_reduce2(in.shape().data(), out_strides.data(), in.strides().data(), dims, 0, 0,
+                                            keepdims ? 0 : 1, 0xFFFFFFFFu, shape_, s_out_, s_in_);
+        rstride_ = in.strides()[0];
+        rlen_ = in.shape()[0];
+    }
+    void eval(matrix& out, EvalType t) override {
+        eval_input(input_, t);
+        allocate_output(*this, out);
+        if (t == EvalType::COMPILE_TRACE) return;
+        if (evaluated) return;
+        evaluated = true;
+        const bool arg = op_ == MTXC_REDUCE_ARGMAX || op_ == MTXC_REDUCE_ARGMIN;
+        check(mtxc_reduce_sharded(op_, (int)input_.type(), out.data(), input_.data(), rstride_, rlen_, cdims_, shape_,
+                                  s_out_, s_in_, arg ? first_rows_.data() : nullptr),
+              "mtxc_reduce_sharded");
+    }
+    void clear_trace_checks() override {
+        evaluated = false;
+        if (input_.has_tape()) input_.tape_ptr()->clear_trace_checks();
+    }
+    std::vector<matrix*> inputs() override { return {&input_}; }
+    const char* name() const override {
+        static const char* n[] = {"ShardedSum", "ShardedMax", "ShardedMin", "ShardedArgMax", "ShardedArgMin"};
+        return n[op_];
+    }
+
+private:
+    int op_;
+    matrix input_;
+    std::vector<int64_t> first_rows_;
     uint32_t cdims_ = 0, rstride_ = 0, rlen_ = 0;
     uint32_t shape_[MTXC_MAX_DIMS] = {}, s_out_[MTXC_MAX_DIMS] = {}, s_in_[MTXC_MAX_DIMS] = {};
 };
@@ -1259,6 +1302,70 @@ std::vector<uint8_t> matrix::to_host_bytes() const {
         }
         std::memcpy(&out[g * es], &raw[off * es], es);
     }
+    return out;
+}
+
+// ------------------------------------------------------------------------------------------
+// Several GPUs (mtxc_comm_*)
+// ------------------------------------------------------------------------------------------
+std::string Communicator::unique_id() {
+    std::string id(MTXC_COMM_ID_BYTES, '\0');
+    check(mtxc_comm_unique_id(id.data(), id.size()), "mtxc_comm_unique_id");
+    return id;
+}
+
+Communicator::Communicator(int nranks, int rank, const std::string& id, size_t buffer_bytes)
+    : nranks_(nranks), rank_(rank) {
+    if (nranks > 1 && id.size() != MTXC_COMM_ID_BYTES)
+        throw std::invalid_argument("Communicator: the id must be MTXC_COMM_ID_BYTES bytes (Communicator::unique_id)");
+    check(mtxc_comm_init(nranks, rank, nranks > 1 ? id.data() : nullptr, buffer_bytes), "mtxc_comm_init");
+    if (int rc = mtxc_alloc(sizeof(int32_t), &token_)) {
+        mtxc_comm_destroy();
+        raise(rc, "mtxc_alloc");
+    }
+}
+
+Communicator::~Communicator() {
+    mtxc_sync();
+    mtxc_comm_destroy();
+    if (token_) mtxc_free(token_);
+}
+
+bool Communicator::peer_exchange() const {
+    int peer = 0;
+    check(mtxc_comm_status(&peer, nullptr), "mtxc_comm_status");
+    return peer != 0;
+}
+
+bool Communicator::timed_out() {
+    int late = 0;
+    check(mtxc_comm_status(nullptr, &late), "mtxc_comm_status");
+    return late != 0;
+}
+
+void Communicator::barrier() {
+    // a rank's exchange starts after its earlier ones have finished (one stream) and completes only when
+    // every rank's part of it has arrived, so when it completes here every rank is done writing into this
+    // rank's buffers for the earlier ones
+    check(mtxc_allreduce(MTXC_REDUCE_SUM, MTXC_INT32, token_, 1), "mtxc_allreduce");
+    check(mtxc_sync(), "mtxc_sync");
+}
+
+matrix reduce_sharded(ReduceOp op, const matrix& local, const std::vector<int64_t>& first_rows, bool keepdims) {
+    if (local.dims() == 0) throw std::invalid_argument("reduce_sharded: a 0-d matrix has no axis 0");
+    const int code = (int)op;
+    if (code < MTXC_REDUCE_SUM || code > MTXC_REDUCE_ARGMIN) throw std::invalid_argument("reduce_sharded: unknown op");
+    const bool arg = op == ReduceOp::ArgMax || op == ReduceOp::ArgMin;
+    int nranks = 0, rank = 0;
+    check(mtxc_comm_size(&nranks, &rank), "reduce_sharded (needs a Communicator on this thread)");
+    if (arg && first_rows.size() != (size_t)nranks)
+        throw std::invalid_argument("reduce_sharded: ArgMax / ArgMin need first_rows for every rank");
+    std::vector<size_m> out_shape = local.shape();
+    if (keepdims) out_shape[0] = 1;
+    else out_shape.erase(out_shape.begin());
+    matrix out;
+    out.set_layout(out_shape, row_major(out_shape), arg ? dtype::Int32 : local.type());
+    out.set_tape(std::make_shared<ShardedReducePrimitive>(code, local, keepdims, out_shape, first_rows));
     return out;
 }
 

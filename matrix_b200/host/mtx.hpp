@@ -21,6 +21,8 @@
 //               only -- recorded into a CUDA graph per binding of device pointers, replayed while the
 //               binding holds (Matrix.mm:8415-8475); jit_graph_gpu / multi_jit_graph_gpu hand each call's
 //               buffers to a compiled graph (Matrix.mm:1076-1149)
+//   several GPUs Communicator (mtxc_comm_*) and reduce_sharded: a reduction over an axis sharded across
+//               the GPUs of a node, one lazy node per rank (no counterpart in the reference)
 // mean / rms / norm build one fused node (mtxc_reduce_stat: one read of x) whose result and dtype are
 // those of the reference's composition (sum, scalar division, sqrt); the other frontends build the
 // reference's own nodes.
@@ -213,5 +215,48 @@ private:
     std::shared_ptr<Primitive> tape_;
     std::shared_ptr<GraphCache> graphs_;  // the recorded execute passes of the graph rooted here
 };
+
+// ------------------------------------------------------------------------------------------------
+// Several GPUs.  The reference drives one Metal device (Mods/GPUManager.h:53-54) and has no multi-GPU
+// API; this mirrors the C ABI's communicator (mtxc_comm_*, mtxc_reduce_sharded) for C++ callers.  One
+// process (or host thread) per GPU, each bound with init(device); like any collective, every rank builds
+// and evaluates the same sharded reductions in the same order.
+// ------------------------------------------------------------------------------------------------
+class Communicator {
+public:
+    // A new communicator id (rank 0 makes it; the caller carries it to the other ranks: MPI, a file, ...).
+    static std::string unique_id();
+    // Joins the calling thread as `rank` of `nranks` (mtxc_comm_init); blocks until every rank has joined.
+    Communicator(int nranks, int rank, const std::string& id, size_t buffer_bytes = 0);
+    // Waits for the thread's stream and releases the communicator.  Call barrier() on every rank first:
+    // a rank still exchanging writes into the other ranks' buffers.
+    ~Communicator();
+    Communicator(const Communicator&) = delete;
+    Communicator& operator=(const Communicator&) = delete;
+    int size() const { return nranks_; }
+    int rank() const { return rank_; }
+    // whether the exchanges run as one kernel over NVLink peer memory (else NCCL all-gather + merge)
+    bool peer_exchange() const;
+    // waits for the thread's stream; whether an exchange since the last query gave up waiting for a rank
+    bool timed_out();
+    // a one-value exchange on every rank, then a wait: once it returns, no rank writes into this rank's
+    // buffers for any earlier exchange
+    void barrier();
+
+private:
+    int nranks_ = 1, rank_ = 0;
+    void* token_ = nullptr;  // one int32 of device memory for barrier()
+};
+
+enum class ReduceOp { Sum = 0, Max = 1, Min = 2, ArgMax = 3, ArgMin = 4 };
+
+// local.op(0, keepdims) of a matrix sharded along axis 0 across the ranks of the calling thread's
+// Communicator: this rank holds `local`, a contiguous slice of the global axis (possibly empty), and
+// first_rows[r] is the global index of rank r's first row (ArgMax / ArgMin turn local indices into global
+// ones with it; the other ops may pass none).  Lazy like the other reductions; the result is the whole
+// reduction, identical on every rank, with the reference's order and tie rules across the shards (float
+// sums in rank order, the first global index of an extreme).
+matrix reduce_sharded(ReduceOp op, const matrix& local, const std::vector<int64_t>& first_rows = {},
+                      bool keepdims = false);
 
 }  // namespace mtx
