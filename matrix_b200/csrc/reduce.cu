@@ -250,6 +250,7 @@ struct PairExtremum {
     static constexpr int kLanes = 16 / (int)sizeof(T);
     static constexpr bool kKeyed = kColSimd && !Traits<T>::kFloat;
     static constexpr bool kColFold2 = kKeyed;
+    static constexpr bool kColStream = !(kKeyed && sizeof(T) == 1);
     static constexpr int kKeyShift = 32 - 8 * (int)sizeof(T);
     static constexpr uint32_t kLow = (1u << kKeyShift) - 1u;          // the row part of a key
     static constexpr uint32_t kCarried = kMax ? kLow : 0u;             // best from an earlier chunk
@@ -666,6 +667,15 @@ template <class R, class = void>
 struct ColSimd : std::false_type {};
 template <class R>
 struct ColSimd<R, std::void_t<decltype(R::kColSimd)>> : std::bool_constant<R::kColSimd> {};
+// Column folds whose lanes stream (stream_col_fold: the next rows' loads in flight while the current ones
+// fold).  The 1-byte keyed fold holds 16 keys and 16 indices per thread: a second batch of loads in registers
+// costs it a CTA per SM, which measured slower (B200, int8 ArgMax over a strided axis 0.81 -> 0.71 of the
+// copy figure), so it folds batch by batch (kColStream false); for the other packed folds streaming measured
+// faster (uint16 ArgMax 0.83 -> 0.90).
+template <class R, class = void>
+struct ColStream : std::true_type {};
+template <class R>
+struct ColStream<R, std::void_t<decltype(R::kColStream)>> : std::bool_constant<R::kColStream> {};
 // Column folds that take two rows per call (col_fold2).
 template <class R, class = void>
 struct ColFold2 : std::false_type {};
@@ -693,6 +703,51 @@ __device__ __forceinline__ void col_fold_rows(typename R::ColState& cs, const X 
             uint32_t w[4];
             memcpy(w, &x[k], 16);
             R::col_fold(cs, w, row0 + k * step);
+        }
+    }
+}
+
+// Streams a thread's n slots (slot i at position p0 + i * step) through a packed column state in batches of
+// kUnroll: the next batch's loads are issued before the current batch folds, so a warp keeps loads in flight
+// while it computes, and the last partial batch is loaded at once under per-slot predicates instead of one
+// slot per memory round trip.  load(x, pos) fills x from position pos.
+template <class R, class X, class Load>
+__device__ __forceinline__ void stream_col_fold(typename R::ColState& cs, uint32_t p0, uint32_t step, uint32_t n,
+                                                Load load) {
+    uint32_t i = 0;
+    if (n >= (uint32_t)kUnroll) {
+        X a[kUnroll], b[kUnroll];
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) load(a[k], p0 + k * step);
+        while (true) {
+            bool more = i + 2 * kUnroll <= n;
+            if (more) {
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) load(b[k], p0 + (i + kUnroll + k) * step);
+            }
+            col_fold_rows<R>(cs, a, p0 + i * step, step);
+            i += kUnroll;
+            if (!more) break;
+            more = i + 2 * kUnroll <= n;
+            if (more) {
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k) load(a[k], p0 + (i + kUnroll + k) * step);
+            }
+            col_fold_rows<R>(cs, b, p0 + i * step, step);
+            i += kUnroll;
+            if (!more) break;
+        }
+    }
+    X t[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k)
+        if (i + k < n) load(t[k], p0 + (i + k) * step);
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+        if (i + k < n) {
+            uint32_t w[4];
+            memcpy(w, &t[k], 16);
+            R::col_fold(cs, w, p0 + (i + k) * step);
         }
     }
 }
@@ -903,18 +958,26 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
         const uint32_t step = ty_count;
         if constexpr (ColSimd<R>::value && V * sizeof(T) == 16) {
             typename R::ColState cs = R::col_init(step, a.chunk);
-            for (; r + (kUnroll - 1) * step < end; r += kUnroll * step) {
-                ew::Slot<T, V> x[kUnroll];
+            if constexpr (ColStream<R>::value) {
+                const uint32_t n = r < end ? (end - 1 - r) / step + 1 : 0;
+                const uint32_t rs = a.rstride;
+                stream_col_fold<R, ew::Slot<T, V>>(cs, r, step, n, [&](ew::Slot<T, V>& x, uint32_t row) {
+                    ew::load_slot(x, p + (size_t)row * rs);
+                });
+            } else {
+                for (; r + (kUnroll - 1) * step < end; r += kUnroll * step) {
+                    ew::Slot<T, V> x[kUnroll];
 #pragma unroll
-                for (int k = 0; k < kUnroll; ++k) ew::load_slot(x[k], p + (size_t)(r + k * step) * a.rstride);
-                col_fold_rows<R>(cs, x, r, step);
-            }
-            for (; r < end; r += step) {
-                ew::Slot<T, V> x;
-                ew::load_slot(x, p + (size_t)r * a.rstride);
-                uint32_t w[4];
-                memcpy(w, &x, 16);
-                R::col_fold(cs, w, r);
+                    for (int k = 0; k < kUnroll; ++k) ew::load_slot(x[k], p + (size_t)(r + k * step) * a.rstride);
+                    col_fold_rows<R>(cs, x, r, step);
+                }
+                for (; r < end; r += step) {
+                    ew::Slot<T, V> x;
+                    ew::load_slot(x, p + (size_t)r * a.rstride);
+                    uint32_t w[4];
+                    memcpy(w, &x, 16);
+                    R::col_fold(cs, w, r);
+                }
             }
             R::col_finish(cs, st);
         } else if constexpr (V > 1) {
