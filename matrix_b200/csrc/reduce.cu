@@ -249,25 +249,32 @@ struct PairExtremum {
     static constexpr bool kColSimd = sizeof(T) <= 2;
     static constexpr int kLanes = 16 / (int)sizeof(T);
     static constexpr bool kKeyed = kColSimd && !Traits<T>::kFloat;
-    static constexpr bool kColFold2 = kKeyed;
-    static constexpr bool kColStream = !(kKeyed && sizeof(T) == 1);
-    static constexpr int kKeyShift = 32 - 8 * (int)sizeof(T);
-    static constexpr uint32_t kLow = (1u << kKeyShift) - 1u;          // the row part of a key
-    static constexpr uint32_t kCarried = kMax ? kLow : 0u;             // best from an earlier chunk
-    static constexpr uint32_t kUnset = kMax ? 0u : kLow;               // no row yet
+    // the key layout (a nested class: instantiated only with the keyed folds that use it)
+    struct Key {
+        static constexpr int kShift = 32 - 8 * (int)sizeof(T);
+        static constexpr uint32_t kLow = (1u << kShift) - 1u;         // the row part of a key
+        static constexpr uint32_t kCarried = kMax ? kLow : 0u;          // best from an earlier chunk
+        static constexpr uint32_t kUnset = kMax ? 0u : kLow;            // no row yet
+        // int32 words from one carried index to the next: the index fields of consecutive (value, index) states
+        static constexpr int kIdxStride = (int)(sizeof(Pair<V>) / sizeof(int32_t));
+    };
     struct KeyState {
         uint32_t key[kLanes];
-        int32_t idx[kLanes];       // row index of a carried best
+        // row indices of carried bests (lane j at idx[j * Key::kIdxStride]): memory of the caller's choosing,
+        // written only at a chunk's end and read at the finish -- the column kernel points it at the index
+        // fields of the thread's own shared-memory staging slots, which are free until its epilogue, so the
+        // indices hold no registers through the loop
+        int32_t* idx;
         uint32_t n;                // rows of the current chunk so far
         uint32_t row;              // last row folded
         uint32_t step;             // distance between the lane's consecutive rows
-        uint32_t limit;            // rows per chunk (at most kLow - 1, so row parts stay clear of both marks)
+        uint32_t limit;            // rows per chunk (at most Key::kLow - 1, so row parts stay clear of both marks)
         uint32_t lane_stride;      // index distance between neighbouring lanes (rows: 1, columns: 0)
     };
     __device__ static uint32_t key_bits(T v) {
         uint32_t b = 0;
         memcpy(&b, &v, sizeof(T));
-        return b << kKeyShift;
+        return b << Key::kShift;
     }
     __device__ static uint32_t key_ext(uint32_t a, uint32_t b) {
         if constexpr (std::is_signed_v<T>) return (uint32_t)(kMax ? max((int)a, (int)b) : min((int)a, (int)b));
@@ -283,30 +290,30 @@ struct PairExtremum {
         if constexpr (sizeof(T) == 1) return __byte_perm(w[j / 4], rk, 0x0654u | ((uint32_t)(j % 4) << 12));
         else return __byte_perm(w[j / 2], rk, 0x0054u | ((uint32_t)(j % 2) << 9) | ((uint32_t)(j % 2 * 2 + 1) << 12));
     }
-    __device__ static uint32_t row_part(uint32_t n) { return kMax ? (kLow - 1u) - n : n + 1u; }
-    __device__ static KeyState col_init_keyed(uint32_t step, uint32_t limit, uint32_t lane_stride) {
+    __device__ static uint32_t row_part(uint32_t n) { return kMax ? (Key::kLow - 1u) - n : n + 1u; }
+    __device__ static KeyState col_init_keyed(uint32_t step, uint32_t limit, uint32_t lane_stride, int32_t* idx) {
         KeyState c;
-        const uint32_t k0 = key_bits(kMax ? lowest_value<T>() : highest_value<T>()) | kUnset;
+        const uint32_t k0 = key_bits(kMax ? lowest_value<T>() : highest_value<T>()) | Key::kUnset;
 #pragma unroll
         for (int j = 0; j < kLanes; ++j) {
-            c.key[j] = k0;
-            c.idx[j] = 0;
+            c.key[j] = k0;  // idx needs no initial value: it is read only for lanes that a flush carried
         }
+        c.idx = idx;
         c.n = 0;
         c.row = 0;
         c.step = step;
-        c.limit = min(limit, kLow - 1u);
+        c.limit = min(limit, Key::kLow - 1u);
         c.lane_stride = lane_stride;
         return c;
     }
     __device__ static void col_flush(KeyState& c) {
 #pragma unroll
         for (int j = 0; j < kLanes; ++j) {
-            const uint32_t low = c.key[j] & kLow;
-            if (low != kCarried && low != kUnset) {
-                const uint32_t cnt = kMax ? (kLow - 1u) - low : low - 1u;  // the row's count in this chunk
-                c.idx[j] = (int32_t)(c.row - (c.n - 1u - cnt) * c.step + (uint32_t)j * c.lane_stride);
-                c.key[j] = (c.key[j] & ~kLow) | kCarried;
+            const uint32_t low = c.key[j] & Key::kLow;
+            if (low != Key::kCarried && low != Key::kUnset) {
+                const uint32_t cnt = kMax ? (Key::kLow - 1u) - low : low - 1u;  // the row's count in this chunk
+                c.idx[j * Key::kIdxStride] = (int32_t)(c.row - (c.n - 1u - cnt) * c.step + (uint32_t)j * c.lane_stride);
+                c.key[j] = (c.key[j] & ~Key::kLow) | Key::kCarried;
             }
         }
         c.n = 0;
@@ -338,13 +345,13 @@ struct PairExtremum {
         if (c.n) col_flush(c);
 #pragma unroll
         for (int j = 0; j < kLanes; ++j) {
-            if ((c.key[j] & kLow) == kUnset) {
+            if ((c.key[j] & Key::kLow) == Key::kUnset) {
                 st[j] = init();
             } else {
                 T v;
-                const uint32_t b = c.key[j] >> kKeyShift;
+                const uint32_t b = c.key[j] >> Key::kShift;
                 memcpy(&v, &b, sizeof(T));  // little-endian: the element's bits are the low bytes of b
-                st[j] = State{widen(v), c.idx[j]};
+                st[j] = State{widen(v), c.idx[j * Key::kIdxStride]};
             }
         }
     }
@@ -381,9 +388,10 @@ struct PairExtremum {
         }
     }
     using ColState = std::conditional_t<kKeyed, KeyState, PackedState>;
-    __device__ static ColState col_init(uint32_t step, uint32_t limit, uint32_t lane_stride = 0) {
-        if constexpr (kKeyed) return col_init_keyed(step, limit, lane_stride);
-        else return col_init_packed(step, limit, lane_stride);
+    // the half types' state (the keyed types start with col_init_keyed, which also takes the carried
+    // indices' storage)
+    __device__ static PackedState col_init(uint32_t step, uint32_t limit, uint32_t lane_stride = 0) {
+        return col_init_packed(step, limit, lane_stride);
     }
     __device__ static PackedState col_init_packed(uint32_t step, uint32_t limit, uint32_t lane_stride) {
         PackedState c;
@@ -667,21 +675,11 @@ template <class R, class = void>
 struct ColSimd : std::false_type {};
 template <class R>
 struct ColSimd<R, std::void_t<decltype(R::kColSimd)>> : std::bool_constant<R::kColSimd> {};
-// Column folds whose lanes stream (stream_col_fold: the next rows' loads in flight while the current ones
-// fold).  The 1-byte keyed fold holds 16 keys and 16 indices per thread: a second batch of loads in registers
-// costs it a CTA per SM, which measured slower (B200, int8 ArgMax over a strided axis 0.81 -> 0.71 of the
-// copy figure), so it folds batch by batch (kColStream false); for the other packed folds streaming measured
-// faster (uint16 ArgMax 0.83 -> 0.90).
+// Keyed column folds (col_init_keyed: the caller supplies the carried indices' storage).
 template <class R, class = void>
-struct ColStream : std::true_type {};
+struct ColKeyed : std::false_type {};
 template <class R>
-struct ColStream<R, std::void_t<decltype(R::kColStream)>> : std::bool_constant<R::kColStream> {};
-// Column folds that take two rows per call (col_fold2).
-template <class R, class = void>
-struct ColFold2 : std::false_type {};
-template <class R>
-struct ColFold2<R, std::void_t<decltype(R::kColFold2)>> : std::bool_constant<R::kColFold2> {};
-
+struct ColKeyed<R, std::void_t<decltype(R::kKeyed)>> : std::bool_constant<R::kKeyed> {};
 static_assert(kUnroll % 2 == 0, "col_fold_rows folds rows in pairs");
 
 // Folds kUnroll packed rows x[k] (row numbers row0 + k * step) into a column state, two at a time where
@@ -689,7 +687,7 @@ static_assert(kUnroll % 2 == 0, "col_fold_rows folds rows in pairs");
 template <class R, class X>
 __device__ __forceinline__ void col_fold_rows(typename R::ColState& cs, const X (&x)[kUnroll], uint32_t row0,
                                               uint32_t step) {
-    if constexpr (ColFold2<R>::value) {
+    if constexpr (ColKeyed<R>::value) {  // keyed folds take two rows per call (col_fold2)
 #pragma unroll
         for (int k = 0; k < kUnroll; k += 2) {
             uint32_t wa[4], wb[4];
@@ -796,6 +794,10 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
     constexpr int V = Vec16<T>::N;
     constexpr int kUnitsPerBlock = kBlock / G;
     __shared__ S warp_partial[kBlock / 32];
+    // a keyed fold's carried indices: an odd run of words per thread (lane j at word 2j, the stride of the
+    // column kernel's staging slots), so a warp's accesses to one lane fall on 32 different banks
+    constexpr int kCarriedRun = 2 * V + 1;
+    __shared__ int32_t s_carried[ColKeyed<R>::value ? kBlock * kCarriedRun : 1];
 
     const int slot = threadIdx.x / G;
     const int lane = threadIdx.x % G;
@@ -831,7 +833,10 @@ __global__ void __launch_bounds__(kBlock) reduce_rows_kernel(const RowArgs a) {
         // 0.86, int8 0.37 / 0.74 of the measured copy bandwidth)
         constexpr bool kPackedPair = !VecFold<R>::value && ColSimd<R>::value && !std::is_same_v<T, __half>;
         if constexpr (kPackedPair) {
-            typename R::ColState cs = R::col_init(G * V, a.chunk, 1);
+            typename R::ColState cs = [&] {
+                if constexpr (ColKeyed<R>::value) return R::col_init_keyed(G * V, a.chunk, 1, &s_carried[threadIdx.x * kCarriedRun]);
+                else return R::col_init(G * V, a.chunk, 1);
+            }();
             for (; c + (kUnroll - 1) * G < nvec; c += kUnroll * G) {
                 Vec16<T> x[kUnroll];
 #pragma unroll
@@ -957,8 +962,16 @@ __global__ void __launch_bounds__(kBlock) reduce_cols_kernel(const ColArgs a) {
         uint32_t r = begin + ty;
         const uint32_t step = ty_count;
         if constexpr (ColSimd<R>::value && V * sizeof(T) == 16) {
-            typename R::ColState cs = R::col_init(step, a.chunk);
-            if constexpr (ColStream<R>::value) {
+            // a keyed fold keeps its carried indices in this thread's staging slots (free until the epilogue)
+            typename R::ColState cs = [&] {
+                if constexpr (ColKeyed<R>::value)
+                    return R::col_init_keyed(step, a.chunk, 0, &partial[threadIdx.x * VP].i);
+                else return R::col_init(step, a.chunk);
+            }();
+            // the packed folds stream (next rows' loads in flight while the current ones fold: uint16 ArgMax
+            // 0.83 -> 0.90 of the copy figure on B200), except the 1-byte keyed fold, whose 16 keys plus a second
+            // batch of loads cost a CTA per SM before its indices moved to shared memory and gain nothing since
+            if constexpr (!(ColKeyed<R>::value && sizeof(T) == 1)) {
                 const uint32_t n = r < end ? (end - 1 - r) / step + 1 : 0;
                 const uint32_t rs = a.rstride;
                 stream_col_fold<R, ew::Slot<T, V>>(cs, r, step, n, [&](ew::Slot<T, V>& x, uint32_t row) {
